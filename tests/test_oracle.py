@@ -1,0 +1,127 @@
+"""The CPU oracle against the reference's golden vectors (CPU only, no GPU)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import inputs
+import seqbuild
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _vector_lines():
+    out = []
+    for ln in open(os.path.join(GOLDEN, "expected_vectors.txt")):
+        m = re.match(r"seal D=(\d+) bk=(\d) bv=(\d) body=(\d) bytes=(\d+) rec=([0-9a-f]+) dec=([0-9a-f]+)", ln)
+        if m:
+            out.append(tuple(map(int, m.groups()[:5])) + (int(m.group(6), 16), int(m.group(7), 16)))
+    return out
+
+
+_INPUTS = {}
+
+
+def group_inputs(D):
+    if D not in _INPUTS:
+        _INPUTS[D] = inputs.fill_group(D, 128, 1)
+    return _INPUTS[D]
+
+
+@pytest.mark.parametrize("D,bk,bv,body,nbytes,erec,edec", _vector_lines())
+def test_seal_golden(oracle_lib, D, bk, bv, body, nbytes, erec, edec):
+    o = oracle_lib
+    K, V = group_inputs(D)
+    lay = o.layout(D, bk, bv, body)
+    assert lay.bytes == nbytes
+    rec = o.seal(lay, K, V)
+    assert o.fnv(rec) == erec
+    k, v = o.decode(lay, rec)
+    h = o.fnv(np.stack([k, v], axis=1))   # row order: K row t, then V row t
+    assert h == edec
+
+
+def test_tq6_golden(oracle_lib):
+    o = oracle_lib
+    for ln in open(os.path.join(GOLDEN, "expected_vectors.txt")):
+        m = re.match(r"tq6 rows=(\d+) n=(\d+) enc=([0-9a-f]+) dec=([0-9a-f]+)", ln)
+        if not m:
+            continue
+        rows, n = int(m.group(1)), int(m.group(2))
+        x = inputs.fill_rows(rows, n)
+        enc = o.tq6_encode(x)
+        dec = o.tq6_decode(enc, rows * n)
+        assert o.fnv(enc) == int(m.group(3), 16)
+        assert o.fnv(dec) == int(m.group(4), 16)
+
+
+def test_state_golden(oracle_lib):
+    o = oracle_lib
+    exp = {}
+    for ln in open(os.path.join(GOLDEN, "expected_state.txt")):
+        m = re.match(r"state (\S+) v1 hash=([0-9a-f]+)", ln)
+        if m:
+            exp[m.group(1)] = int(m.group(2), 16)
+    assert len(exp) == 5
+    for name, bk, bv, tr, st, sf, fc in seqbuild.GOLDEN_CFGS:
+        s = seqbuild.OracleSeq(bk, bv, tr, st, sf, fc)
+        seqbuild.grow(s, 23, 0, 1500, 4)
+        assert o.fnv(s.state()) == exp[name], name
+        s.close()
+
+
+def test_fp16_roundtrip_exhaustive(oracle_lib):
+    """Every non-NaN half decodes and re-encodes to itself (reference tests/test_fp16.c:26-33)."""
+    o = oracle_lib
+    h = np.arange(65536, dtype=np.uint32)
+    nan = ((h & 0x7C00) == 0x7C00) & ((h & 0x3FF) != 0)
+    bad = 0
+    for x in h[~nan][::7]:
+        f = o.lib().ora_h2f(int(x))
+        bad += o.lib().ora_f2h(f) != int(x)
+    assert bad == 0
+
+
+def test_fp16_rne_sweep(oracle_lib):
+    """f32 -> f16 rounds to nearest even over the half range, ties and subnormals included,
+    compared with numpy's IEEE conversion (the reference checks the same rule in
+    tests/test_fp16.c:34-40)."""
+    o = oracle_lib
+    i = np.arange(20000, dtype=np.uint64)
+    w = (0x33000000 + i * ((0x47800000 - 0x33000000) // 20000) + (i & 0x1FFF)).astype(np.uint32)
+    f = w.view(np.float32)
+    want = f.astype(np.float16).view(np.uint16)
+    got = np.array([o.lib().ora_f2h(float(x)) for x in f], dtype=np.uint16)
+    assert np.array_equal(got, want)
+    got_neg = np.array([o.lib().ora_f2h(float(-x)) for x in f[::13]], dtype=np.uint16)
+    assert np.array_equal(got_neg, (-f[::13]).astype(np.float16).view(np.uint16))
+    # NaN, infinities and the overflow threshold
+    assert o.lib().ora_f2h(float("nan")) & 0x7FFF == 0x7E00
+    assert o.lib().ora_f2h(float("inf")) == 0x7C00
+    assert o.lib().ora_f2h(65519.99) == 0x7BFF
+    assert o.lib().ora_f2h(65520.0) == 0x7C00
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref", "libsjref.so")),
+                    reason="reference not compiled here")
+def test_oracle_matches_compiled_reference_fp16(oracle_lib):
+    """Oracle conversion == the compiled reference's sj_kvarn_f32_to_f16 on a dense sweep."""
+    import ctypes as C
+    import oracle
+    r = oracle.ref()
+    r.sj_kvarn_f32_to_f16.argtypes = [C.c_float]
+    r.sj_kvarn_f32_to_f16.restype = C.c_uint16
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 2 ** 32, size=20000, dtype=np.uint64).astype(np.uint32)
+    for x in w.view(np.float32):
+        assert r.sj_kvarn_f32_to_f16(float(x)) == oracle_lib.lib().ora_f2h(float(x))
+
+
+def test_window_and_layout_offsets(oracle_lib):
+    """Record offsets of the three headline bodies at D=256 (reference README, Formats)."""
+    o = oracle_lib
+    assert o.layout(256, 4, 4, 0).bytes == 35072
+    assert o.layout(256, 3, 3, 1).bytes == 26880
+    assert o.layout(256, 3, 2, 1).bytes == 22784
+    assert o.layout(256, 2, 2, 1).bytes == 18688
