@@ -1,0 +1,351 @@
+/*
+ * sjk.h - B200 (sm_100a) implementation of the SJ-KVaRN hot path behind the sj_kvarn.h C API.
+ *
+ * Link libsjk_b200.so and include this header instead of the reference's single-header
+ * library (JakeATX/sj-kvarn-codec, sj_kvarn.h). Names, argument meaning, status codes and
+ * stored bytes are those of sj_kvarn.h; the difference is where the data lives:
+ *
+ *   - every cache buffer (sink, staging ring, sealed body, pool slab) is DEVICE memory;
+ *   - row arguments of the codec and cache calls (k_rot, v_rot, q_rot, out_rot, records,
+ *     staging rows, seal inputs) are DEVICE pointers;
+ *   - state save/restore streams (sj_kvarn_seq_state_write/_read/_peek) are HOST buffers;
+ *   - the policy, layout, pool bookkeeping and status calls are host code, unchanged.
+ *
+ * Cache calls run on the object's stream (sj_kvarn_layer.stream / sj_kvarn_seq.stream,
+ * 0 = the legacy default stream) and are asynchronous like any CUDA launch; calls that
+ * return data to the host (state write, sj_kvarn_layer_record_copy) synchronise it.
+ * Functions that return void in sj_kvarn.h record a sticky error instead (sjk_last_error).
+ *
+ * A second, thinner layer (sjk_*) exposes the device kernels with explicit streams and
+ * batched shapes; it mirrors the reference's CUDA entry points (sj_kvarn_cuda.cuh) and is
+ * what an engine's own graph calls.
+ */
+#ifndef SJK_H
+#define SJK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st * sjk_stream;   /* same type as cudaStream_t */
+
+/* ---- versions and format constants (sj_kvarn.h:85-128) ---- */
+#define SJKVARN_VERSION_MAJOR 2
+#define SJKVARN_VERSION_MINOR 0
+#define SJKVARN_FORMAT_VERSION 1
+#define SJKVARN_STATE_VERSION  1
+
+#define SJKVARN_GROUP_DEFAULT     128
+#define SJKVARN_SINK_DEFAULT      128
+#define SJKVARN_TAIL_DEFAULT      4096
+#define SJKVARN_TAIL_MAX_DEFAULT  8192
+#define SJKVARN_ITERS_DEFAULT     16
+#define SJKVARN_RED_LANES         8
+#define SJKVARN_TQ6_QK            128
+#define SJKVARN_TQ6_BLOCK_BYTES   98
+#define SJKVARN_TRELLIS_SEQ       128
+#define SJKVARN_TRELLIS_HIST_BITS 6
+#define SJKVARN_TRELLIS_NSTATE    64
+
+typedef enum sj_kvarn_body {
+    SJKVARN_BODY_SCALAR  = 0,
+    SJKVARN_BODY_TRELLIS = 1,
+    SJKVARN_BODY_AUTO    = 2
+} sj_kvarn_body;
+
+typedef enum sj_kvarn_staging {
+    SJKVARN_STAGING_TQ6_0 = 0,
+    SJKVARN_STAGING_F16   = 1
+} sj_kvarn_staging;
+
+typedef enum sj_kvarn_sink_type {
+    SJKVARN_SINK_F16     = 0,
+    SJKVARN_SINK_INHERIT = 1
+} sj_kvarn_sink_type;
+
+/* staging block, 98 bytes (sj_kvarn.h:146-154) */
+typedef struct sj_kvarn_tq6_block {
+    uint16_t norm;
+    uint8_t  qs[64];
+    uint8_t  qh[32];
+} sj_kvarn_tq6_block;
+
+/* record layout (sj_kvarn.h:156-175) */
+typedef struct sj_kvarn_layout {
+    int D, G, bits_k, bits_v, body;
+    uint32_t k_payload, v_payload;
+    uint32_t k_scale, k_zero, k_tok, v_ch, v_scale, v_zero;
+    uint32_t bytes;
+} sj_kvarn_layout;
+
+/* ---- fp16 (host; sj_kvarn.h:178-179) ---- */
+uint16_t sj_kvarn_f32_to_f16(float f);
+float    sj_kvarn_f16_to_f32(uint16_t h);
+
+/* ---- rotation (sj_kvarn.h:182-185). x: DEVICE [n] / [n_heads][head_dim] floats, in place. ---- */
+void sj_kvarn_hadamard(float * x, int n);
+void sj_kvarn_rotate_heads(float * x, int n_heads, int head_dim);
+
+/* ---- record layout (host; sj_kvarn.h:187-195) ---- */
+int      sj_kvarn_body_resolve(int body, int bits_k, int bits_v);
+int      sj_kvarn_layout_init(sj_kvarn_layout * l, int D, int G, int bits_k, int bits_v, int body);
+size_t   sj_kvarn_record_bytes(int D, int G, int bits_k, int bits_v);
+double   sj_kvarn_body_bits_per_element(const sj_kvarn_layout * l);
+uint32_t sj_kvarn_code_bit(const sj_kvarn_layout * l, int t, int d, int is_v);
+int      sj_kvarn_k_ch_idx(const sj_kvarn_layout * l, int d);
+int      sj_kvarn_v_ch_idx(const sj_kvarn_layout * l, int d);
+
+/* ---- seal / decode / staging of single objects (sj_kvarn.h:197-216); DEVICE pointers ---- */
+/* The B200 sealer keeps its scratch on chip; `work` is accepted and ignored (may be NULL). */
+size_t sj_kvarn_seal_workspace_bytes(const sj_kvarn_layout * l);
+void   sj_kvarn_seal_group(const sj_kvarn_layout * l, const uint16_t * K, const uint16_t * V,
+                           size_t row_stride, int iters, uint8_t * rec, void * work);
+void   sj_kvarn_decode_k_row(const sj_kvarn_layout * l, const uint8_t * rec, int t, float * out);
+void   sj_kvarn_decode_v_row(const sj_kvarn_layout * l, const uint8_t * rec, int t, float * out);
+void   sj_kvarn_tq6_quantize_row(const float * x, sj_kvarn_tq6_block * y, int n);
+void   sj_kvarn_tq6_dequantize_row(const sj_kvarn_tq6_block * y, float * x, int n);
+size_t sj_kvarn_stage_row_bytes(int staging, int D);
+void   sj_kvarn_stage_row(int staging, const float * x_rot, void * dst, int D);
+void   sj_kvarn_unstage_row(int staging, const void * src, float * x_rot, int D);
+
+/* ---- adaptive tail / journal policy (host; sj_kvarn.h:224-274) ---- */
+typedef struct sj_kvarn_policy {
+    uint32_t sink, tail, tail_max, group, flush_chunk;
+    uint32_t B;
+    uint32_t B_prev;
+    uint32_t B_pending;
+    int      draining;
+} sj_kvarn_policy;
+
+void     sj_kvarn_policy_init(sj_kvarn_policy * p, uint32_t sink, uint32_t tail, uint32_t tail_max,
+                              uint32_t group, uint32_t flush_chunk);
+void     sj_kvarn_policy_reset(sj_kvarn_policy * p);
+uint32_t sj_kvarn_policy_begin_ubatch(sj_kvarn_policy * p, uint32_t pos0, uint32_t n_tokens);
+void     sj_kvarn_policy_commit(sj_kvarn_policy * p);
+uint32_t sj_kvarn_policy_idle(sj_kvarn_policy * p, uint32_t end, uint32_t keep_recent);
+
+#define SJKVARN_NO_POS UINT32_MAX
+uint32_t sj_kvarn_group_floor(uint32_t sink, uint32_t group, uint32_t pos);
+uint32_t sj_kvarn_policy_trunc_floor(const sj_kvarn_policy * p, uint32_t pos);
+uint32_t sj_kvarn_policy_truncate(sj_kvarn_policy * p, uint32_t pos, uint32_t * n_dropped);
+uint32_t sj_kvarn_ring_capacity(uint32_t tail, uint32_t tail_max, uint32_t group, uint32_t n_ubatch);
+uint32_t sj_kvarn_ring_slot(uint32_t sink, uint32_t cap, uint32_t pos);
+
+/* ---- per-layer cache (sj_kvarn.h:276-330); buffers in DEVICE memory ---- */
+typedef struct sj_kvarn_config {
+    int      head_dim;
+    int      n_head_kv;
+    int      group;
+    int      bits_k, bits_v;
+    int      body;
+    int      iters;
+    int      staging;
+    int      sink_type;
+    uint32_t sink, tail, tail_max, flush_chunk;
+    uint32_t n_ubatch;
+    uint32_t n_ctx;
+} sj_kvarn_config;
+
+typedef struct sj_kvarn_layer {
+    sj_kvarn_config cfg;
+    sj_kvarn_layout lay;
+    uint32_t cap;
+    uint32_t n_groups;
+    size_t   stage_bytes;
+    uint8_t * ring;            /* device [cap][n_head_kv][K row | V row] */
+    uint8_t * sink;            /* device, f16: [sink][n_head_kv][K D | V D]; inherit: staging rows */
+    uint8_t * body;            /* device [n_groups][n_head_kv][record] or a pool slab */
+    const uint32_t * blocks;   /* host block table (pool mode), NULL = contiguous body */
+    const uint32_t * d_blocks; /* device copy of the block table (pool mode) */
+    int       owns_body;
+    void    * work;            /* device attention scratch (split partials) */
+    size_t    work_bytes;
+    sjk_stream stream;         /* stream of the layer's calls (0 = legacy default stream) */
+} sj_kvarn_layer;
+
+sj_kvarn_config sj_kvarn_config_default(int head_dim, int n_head_kv, uint32_t n_ctx, uint32_t n_ubatch);
+int      sj_kvarn_layer_init(sj_kvarn_layer * L, const sj_kvarn_config * cfg);
+void     sj_kvarn_layer_free(sj_kvarn_layer * L);
+/* k_rot / v_rot: DEVICE [n_head_kv][D] rotated floats of position pos */
+void     sj_kvarn_layer_store(sj_kvarn_layer * L, uint32_t pos, const float * k_rot, const float * v_rot);
+void     sj_kvarn_layer_seal(sj_kvarn_layer * L, uint32_t B_from, uint32_t B_to);
+/* k, v: DEVICE [D] outputs */
+void     sj_kvarn_layer_kv_row(const sj_kvarn_layer * L, uint32_t B, uint32_t pos, int h, float * k, float * v);
+/* q_rot, out_rot: DEVICE [D] */
+void     sj_kvarn_layer_attend_row(const sj_kvarn_layer * L, uint32_t B, uint32_t N, const float * q_rot,
+                                   int h, uint32_t qpos, float scale, float * out_rot);
+/* DEVICE address of record (g, h) */
+uint8_t * sj_kvarn_layer_record(const sj_kvarn_layer * L, uint32_t g, int h);
+void     sj_kvarn_layer_truncate(sj_kvarn_layer * L, uint32_t B_old, uint32_t B_new, uint32_t n_old, uint32_t resume);
+
+/* ---- status codes (sj_kvarn.h:332-361) ---- */
+enum {
+    SJKVARN_OK                = 0,
+    SJKVARN_ERR_ARG           = -100,
+    SJKVARN_ERR_NOMEM         = -101,
+    SJKVARN_ERR_BUFFER        = -102,
+    SJKVARN_ERR_TRUNCATED     = -103,
+    SJKVARN_ERR_MAGIC         = -104,
+    SJKVARN_ERR_VERSION       = -105,
+    SJKVARN_ERR_FORMAT        = -106,
+    SJKVARN_ERR_CORRUPT       = -107,
+    SJKVARN_ERR_PENDING       = -108,
+    SJKVARN_ERR_CAPACITY      = -109,
+    SJKVARN_ERR_POOL_FULL     = -110,
+    SJKVARN_ERR_HEAD_DIM      = -120,
+    SJKVARN_ERR_N_HEAD_KV     = -121,
+    SJKVARN_ERR_GROUP         = -122,
+    SJKVARN_ERR_SINK          = -123,
+    SJKVARN_ERR_BITS          = -124,
+    SJKVARN_ERR_BODY          = -125,
+    SJKVARN_ERR_ITERS         = -126,
+    SJKVARN_ERR_STAGING       = -127,
+    SJKVARN_ERR_TAIL          = -128,
+    SJKVARN_ERR_ROTATION      = -129,
+    SJKVARN_ERR_CODEBOOK      = -130,
+    SJKVARN_ERR_N_LAYERS      = -131,
+    /* B200 build only: a CUDA call failed (the CUDA error is in sjk_last_cuda_error()) */
+    SJK_ERR_DEVICE            = -200,
+    /* B200 build only: a shape the device kernels do not implement (e.g. head_dim > 256) */
+    SJK_ERR_UNSUPPORTED       = -201
+};
+const char * sj_kvarn_strerror(int code);
+
+/* ---- paged record pool (sj_kvarn.h:363-381); slab in DEVICE memory ---- */
+#define SJKVARN_NO_BLOCK UINT32_MAX
+typedef struct sj_kvarn_pool {
+    sj_kvarn_config cfg;
+    sj_kvarn_layout lay;
+    int       n_layers;
+    uint32_t  n_blocks;
+    uint8_t * body;            /* device [n_layers][n_blocks][n_head_kv][lay.bytes] */
+    uint32_t * free_ids;       /* host stack of free block ids */
+    uint32_t  n_free;
+} sj_kvarn_pool;
+
+int      sj_kvarn_pool_init(sj_kvarn_pool * pool, const sj_kvarn_config * cfg, int n_layers, uint32_t n_blocks);
+void     sj_kvarn_pool_free(sj_kvarn_pool * pool);
+uint32_t sj_kvarn_pool_alloc(sj_kvarn_pool * pool);
+void     sj_kvarn_pool_release(sj_kvarn_pool * pool, uint32_t id);
+
+/* ---- sequence (sj_kvarn.h:383-415) ---- */
+typedef struct sj_kvarn_seq {
+    sj_kvarn_config  cfg;
+    int              n_layers;
+    sj_kvarn_layer * layers;
+    sj_kvarn_policy  pol;
+    uint32_t         n;
+    sj_kvarn_pool  * pool;
+    uint32_t       * blocks;   /* host block table (pool mode) */
+    uint32_t       * d_blocks; /* device mirror of blocks */
+    sjk_stream       stream;
+} sj_kvarn_seq;
+
+int      sj_kvarn_seq_init(sj_kvarn_seq * s, const sj_kvarn_config * cfg, int n_layers, sj_kvarn_pool * pool);
+void     sj_kvarn_seq_free(sj_kvarn_seq * s);
+void     sj_kvarn_seq_reset(sj_kvarn_seq * s);
+int      sj_kvarn_seq_begin_ubatch(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_tokens);
+/* k_rot / v_rot: DEVICE [n_layers][n_head_kv][D] rotated floats */
+void     sj_kvarn_seq_store(sj_kvarn_seq * s, uint32_t pos, const float * k_rot, const float * v_rot);
+int      sj_kvarn_seq_idle(sj_kvarn_seq * s, uint32_t keep_recent);
+uint32_t sj_kvarn_seq_truncate(sj_kvarn_seq * s, uint32_t pos);
+void     sj_kvarn_seq_attend_row(const sj_kvarn_seq * s, int il, const float * q_rot, int h, uint32_t qpos,
+                                 float scale, float * out_rot);
+
+/* ---- sequence state (sj_kvarn.h:417-453); streams are HOST buffers ---- */
+#define SJKVARN_STATE_HEADER_BYTES 128
+#define SJKVARN_ROTATION_HADAMARD  1
+
+typedef struct sj_kvarn_state_info {
+    uint32_t state_version, format_version;
+    sj_kvarn_config cfg;
+    uint32_t rotation, rotation_n;
+    uint64_t codebook_id;
+    int      n_layers;
+    uint32_t n, B, B_prev, draining;
+    size_t   total_bytes;
+} sj_kvarn_state_info;
+
+size_t sj_kvarn_seq_state_size(const sj_kvarn_seq * s);
+size_t sj_kvarn_state_size_max(const sj_kvarn_config * cfg, int n_layers);
+int    sj_kvarn_seq_state_write(const sj_kvarn_seq * s, void * dst, size_t dst_size, size_t * written);
+int    sj_kvarn_state_peek(const void * src, size_t size, sj_kvarn_state_info * info);
+int    sj_kvarn_seq_state_read(sj_kvarn_seq * s, const void * src, size_t size);
+
+/* =====================================================================================
+ * Device layer (sjk_*): explicit streams, batched shapes, DEVICE pointers. Every call
+ * returns 0 or a negative status (SJK_ERR_DEVICE with the CUDA error in
+ * sjk_last_cuda_error(), SJKVARN_ERR_ARG, SJK_ERR_UNSUPPORTED).
+ * ===================================================================================== */
+
+/* Device view of one layer's cache (sj_kvarn_cuda.cuh:27-42), plus an optional device
+ * block table: record (g, h) is at body + ((blocks ? blocks[g] : g)*n_head_kv + h)*lay.bytes. */
+typedef struct sjk_view {
+    sj_kvarn_layout lay;
+    int      n_head_kv;
+    int      staging;
+    int      sink_type;
+    uint32_t S, cap;
+    size_t   stage_bytes;
+    const uint8_t * sink;
+    const uint8_t * ring;
+    const uint8_t * body;
+    const uint32_t * blocks;
+} sjk_view;
+
+int          sjk_last_error(void);          /* sticky status of the void-returning calls; clears it */
+int          sjk_last_cuda_error(void);     /* cudaError_t of the last failed CUDA call */
+const char * sjk_version(void);
+
+/* In-place orthonormal FWHT of n_rows rows of n floats (n a power of two, 32..1024). */
+int sjk_hadamard(float * x, int n_rows, int n, sjk_stream st);
+
+/* Stage n_rows rotated rows of D floats (sj_kvarn_cuda.cuh:68-74). */
+int sjk_stage_rows(int staging, const float * x_rot, uint8_t * dst, size_t dst_row_bytes, int D, int n_rows, sjk_stream st);
+/* Widen n_rows staged rows back to floats (sj_kvarn_cuda.cuh:76-80). */
+int sjk_unstage_rows(int staging, const uint8_t * src, size_t src_row_bytes, float * x, int D, int n_rows, sjk_stream st);
+
+/* Store n_pos consecutive positions pos0.. of one layer: k, v are [n_pos][n_head_kv][D]
+ * floats, rotated (rotate = 0) or in the model basis (rotate = 1: the per-head Hadamard
+ * runs inside the kernel). Positions below the sink go to the sink (fp16 or staging rows),
+ * the rest to ring slot (pos - S) % cap as tq6_0 / fp16 rows (sj_kvarn.h:1475-1492). */
+int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos,
+              const float * k, const float * vv, int rotate, sjk_stream st);
+
+/* Seal n_groups x n_head_kv records from fp16 rows (sj_kvarn_cuda.cuh:136-152): record
+ * r = g*n_head_kv + h reads rows k + g*G*row_stride + h*D. work is ignored (may be NULL). */
+int sjk_seal(const sj_kvarn_layout * lay, const uint16_t * k, const uint16_t * v, size_t row_stride,
+             int n_head_kv, int n_groups, int iters, uint8_t * body, void * work, sjk_stream st);
+
+/* Seal positions [B_from, B_to) of a layer straight out of its staging ring: each row is
+ * widened, rounded to fp16 and sealed in one kernel (sj_kvarn.h:1494-1514). Record
+ * addresses follow v->blocks. iters: balancing iterations. */
+int sjk_seal_ring(const sjk_view * v, uint8_t * body, uint32_t B_from, uint32_t B_to, int iters, sjk_stream st);
+
+/* Decode n_rec records to [n_rec][G][D] floats (sj_kvarn_cuda.cuh:57-66). */
+int sjk_decode(const sj_kvarn_layout * lay, const uint8_t * body, int n_rec, float * out_k, float * out_v, sjk_stream st);
+
+/* Causal attention of n_q query rows (positions qpos0..) x n_head query heads over [0, N)
+ * of one layer (sj_kvarn_cuda.cuh:103-134; GQA head hq reads KV head hq/(n_head/n_head_kv)).
+ * q, out: [n_q][n_head][D] rotated floats. scratch: sjk_attend_scratch_bytes() bytes. */
+size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head);
+int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
+               float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st);
+
+/* Whole-layer helpers over a device-backed sj_kvarn_layer (its stream is ignored; st used). */
+int sjk_layer_store(sj_kvarn_layer * L, uint32_t pos0, uint32_t n_pos, const float * k, const float * v, int rotate,
+                    sjk_stream st);
+int sjk_layer_seal(sj_kvarn_layer * L, uint32_t B_from, uint32_t B_to, sjk_stream st);
+int sjk_layer_attend(const sj_kvarn_layer * L, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                     const float * q, float scale, float * out, sjk_stream st);
+void sjk_layer_view(const sj_kvarn_layer * L, sjk_view * v);
+/* copy record (g, h) to host memory (synchronous) */
+int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * host_dst);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SJK_H */

@@ -1,0 +1,18 @@
+// sjk_internal.h - entry points shared between the library's translation units (not exported API).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "../../include/sjk.h"
+
+void sjk_set_cuda_error(cudaError_t e);
+void sjk_set_sticky(int status);
+
+// attention over KV heads [kv_head0, kv_head0 + n_kv) only (query heads kv*grp.. of those)
+int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0,
+                     int n_kv, const float * q, float scale, float * out, void * scratch, size_t scratch_bytes,
+                     sjk_stream st);
+size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv);
+// decode the K and V rows of position pos, KV head h, to k[D], v[D] (device)
+int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, float * vo, sjk_stream st);
+// decode row t of one record (is_v selects V) to out[D] (device)
+int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st);

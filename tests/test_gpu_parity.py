@@ -1,0 +1,245 @@
+"""Parity of the B200 kernels (through the C-ABI) with the oracle and the reference's golden vectors.
+
+Bit-exact: seal records, decoded rows, tq6_0 / fp16 staging bytes, ring and sink bytes, state streams.
+Attention: max relative L2 error per (row, head) <= 1e-3 against the oracle's reference loop (the
+contract); the measured error is also held to 1e-5, the bound of the reference's own device test
+(tests/test_cuda.cu:135)."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+import gpu_util as gu
+import inputs
+import seqbuild
+import sjk
+import synth
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+ATTN_TOL = 1e-3           # north-star contract (fp32 accumulate)
+ATTN_TOL_TIGHT = 1e-5     # reference device test bound
+
+
+@pytest.fixture(scope="module")
+def L():
+    import build
+    build.build()
+    import torch
+    assert torch.cuda.is_available()
+    return sjk.lib()
+
+
+def _vector_lines():
+    out = []
+    for ln in open(os.path.join(GOLDEN, "expected_vectors.txt")):
+        m = re.match(r"seal D=(\d+) bk=(\d) bv=(\d) body=(\d) bytes=(\d+) rec=([0-9a-f]+) dec=([0-9a-f]+)", ln)
+        if m:
+            out.append(tuple(map(int, m.groups()[:5])) + (int(m.group(6), 16), int(m.group(7), 16)))
+    return out
+
+
+_IN = {}
+
+
+def _group(D):
+    if D not in _IN:
+        _IN[D] = inputs.fill_group(D, 128, 1)
+    return _IN[D]
+
+
+@pytest.mark.parametrize("D,bk,bv,body,nbytes,erec,edec", _vector_lines())
+def test_seal_and_decode_golden(L, oracle_lib, D, bk, bv, body, nbytes, erec, edec):
+    K, V = _group(D)
+    lay = sjk.layout(D, bk, bv, body)
+    assert lay.bytes == nbytes
+    dk, dv = gu.dev(K), gu.dev(V)
+    rec = gu.dev_zeros(lay.bytes)
+    sjk.check(L.sjk_seal(C.byref(lay), gu.ptr(dk), gu.ptr(dv), D, 1, 1, 16, gu.ptr(rec), None, None), "seal")
+    got = gu.host(rec)
+    assert oracle_lib.fnv(got) == erec
+    ok = gu.dev_zeros(128 * D * 4)
+    ov = gu.dev_zeros(128 * D * 4)
+    sjk.check(L.sjk_decode(C.byref(lay), gu.ptr(rec), 1, gu.ptr(ok), gu.ptr(ov), None), "decode")
+    k = gu.host(ok, np.float32, (128, D))
+    v = gu.host(ov, np.float32, (128, D))
+    assert oracle_lib.fnv(np.stack([k, v], axis=1)) == edec
+
+
+def test_tq6_golden(L, oracle_lib):
+    for ln in open(os.path.join(GOLDEN, "expected_vectors.txt")):
+        m = re.match(r"tq6 rows=(\d+) n=(\d+) enc=([0-9a-f]+) dec=([0-9a-f]+)", ln)
+        if not m:
+            continue
+        rows, n = int(m.group(1)), int(m.group(2))
+        x = inputs.fill_rows(rows, n)
+        rb = n // 128 * 98
+        dx, dst = gu.dev(x), gu.dev_zeros(rows * rb)
+        sjk.check(L.sjk_stage_rows(0, gu.ptr(dx), gu.ptr(dst), rb, n, rows, None))
+        enc = gu.host(dst)
+        assert oracle_lib.fnv(enc) == int(m.group(3), 16)
+        dy = gu.dev_zeros(rows * n * 4)
+        sjk.check(L.sjk_unstage_rows(0, gu.ptr(dst), rb, gu.ptr(dy), n, rows, None))
+        assert oracle_lib.fnv(gu.host(dy)) == int(m.group(4), 16)
+
+
+def test_hadamard_bit_exact(L, oracle_lib):
+    rng = np.random.default_rng(3)
+    for n in (128, 256, 512):
+        x = rng.standard_normal((64, n)).astype(np.float32) * 3
+        ref = oracle_lib.fwht_rows(x.copy())
+        dx = gu.dev(x)
+        sjk.check(L.sjk_hadamard(gu.ptr(dx), 64, n, None))
+        assert np.array_equal(gu.host(dx, np.float32, (64, n)).view(np.uint32), ref.view(np.uint32))
+
+
+def _build_pair(L, oracle_lib, D, H, bk, bv, body, staging, sink_f16, npos, tail, tail_max, n_ub, seed, rotate=True,
+                heavy=False, n_ctx=None):
+    """Build the same cache with the product (layer API, raw K/V rotated in the store kernel) and the oracle
+    (CPU rotation + store), sealing through the policy. Returns (layer, oracle cache, B, host rows)."""
+    import oracle
+    n_ctx = n_ctx or npos + 256
+    cfg = sjk.config(D, H, n_ctx, n_ub, bits_k=bk, bits_v=bv, body=body, staging=staging,
+                     sink_type=0 if sink_f16 else 1, tail=tail, tail_max=tail_max)
+    layer = sjk.Layer()
+    sjk.check(L.sj_kvarn_layer_init(C.byref(layer), C.byref(cfg)), "layer_init")
+    body_r = L.sj_kvarn_body_resolve(body, bk, bv)
+    oc = oracle.OracleCache(D, H, bk, bv, body_r == 1, 16, staging, sink_f16, 128, tail, tail_max, n_ub, n_ctx)
+    pol = sjk.Policy()
+    L.sj_kvarn_policy_init(C.byref(pol), 128, tail, tail_max, 128, 0)
+    st = synth.KVStream(seed, 1, H, D, heavy=heavy)
+    pos = 0
+    while pos < npos:
+        n = min(n_ub, npos - pos)
+        L.sj_kvarn_policy_begin_ubatch(C.byref(pol), pos, n)
+        if pol.B_pending > pol.B:
+            sjk.check(L.sjk_layer_seal(C.byref(layer), pol.B, pol.B_pending, None), "seal")
+            oc.seal(pol.B, pol.B_pending)
+        L.sj_kvarn_policy_commit(C.byref(pol))
+        k, v = st.rows(pos, n, layer=0)
+        dk, dv = gu.dev(k), gu.dev(v)
+        sjk.check(L.sjk_layer_store(C.byref(layer), pos, n, gu.ptr(dk), gu.ptr(dv), 1 if rotate else 0, None), "store")
+        kr = oracle_lib.fwht_rows(k.copy()) if rotate else k
+        vr = oracle_lib.fwht_rows(v.copy()) if rotate else v
+        for i in range(n):
+            oc.store(pos + i, kr[i], vr[i])
+        pos += n
+    gu.torch().cuda.synchronize()
+    return layer, oc, pol.B, cfg
+
+
+@pytest.mark.parametrize("bk,bv,body,staging,sink_f16", [
+    (4, 4, 0, 0, True), (3, 3, 1, 0, True), (3, 2, 1, 0, True), (4, 4, 0, 1, False), (4, 2, 0, 0, True)])
+def test_cache_build_bit_exact(L, oracle_lib, bk, bv, body, staging, sink_f16):
+    """Store (FWHT + staging) and seal-from-ring through the policy: sink, ring and body bytes identical."""
+    D, H = 256, 2
+    layer, oc, B, cfg = _build_pair(L, oracle_lib, D, H, bk, bv, body, staging, sink_f16, 1500, 256, 512, 64, seed=5)
+    assert B > 128 + 3 * 128
+    sink_b = 128 * H * (D * 4 if sink_f16 else 2 * layer.stage_bytes)
+    assert np.array_equal(gu.d2h_ptr(layer.sink, sink_b), oc.sink_bytes())
+    ring_b = layer.cap * H * 2 * layer.stage_bytes
+    assert np.array_equal(gu.d2h_ptr(layer.ring, ring_b), oc.ring_bytes())
+    ng = (B - 128) // 128
+    body_b = gu.d2h_ptr(layer.body, ng * H * layer.lay.bytes)
+    ref = oc.body_bytes(ng)
+    bad = [(g, h) for g in range(ng) for h in range(H)
+           if not np.array_equal(body_b[(g * H + h) * layer.lay.bytes:(g * H + h + 1) * layer.lay.bytes],
+                                 ref[(g * H + h) * layer.lay.bytes:(g * H + h + 1) * layer.lay.bytes])]
+    assert bad == []
+    # kv_row of a body, sink and ring position equals the oracle's (device pointers in and out)
+    kk, vv = gu.dev_zeros(D * 4), gu.dev_zeros(D * 4)
+    for p in (3, 128 + 77, B - 1, B, 1499):
+        L.sj_kvarn_layer_kv_row(C.byref(layer), B, p, 1, gu.ptr(kk), gu.ptr(vv))
+        sjk.check_sticky()
+        rk, rv = oc.kv_row(B, p, 1)
+        assert np.array_equal(gu.host(kk, np.float32), rk) and np.array_equal(gu.host(vv, np.float32), rv), p
+    # attention over the three regions: 4 query rows x 4 query heads (GQA 2)
+    n_q, n_head = 4, 4
+    q = synth.queries(9, 1, n_q, n_head, D)[0]
+    qr = oracle_lib.fwht_rows(q.copy())
+    dq, dout = gu.dev(qr), gu.dev_zeros(n_q * n_head * D * 4)
+    scale = np.float32(1.0 / 16.0)
+    sjk.check(L.sjk_layer_attend(C.byref(layer), B, 1500, 1500 - n_q, n_q, n_head, gu.ptr(dq), scale, gu.ptr(dout), None))
+    out = gu.host(dout, np.float32, (n_q, n_head, D))
+    ref = oc.attend(B, 1500, 1500 - n_q, qr, scale)
+    err = gu.rel_err_rows(out, ref)
+    assert err <= ATTN_TOL_TIGHT, err
+    # one row through the reference-named single-row call
+    dq1, do1 = gu.dev(qr[2, 3]), gu.dev_zeros(D * 4)
+    L.sj_kvarn_layer_attend_row(C.byref(layer), B, 1500, gu.ptr(dq1), 1, 1000, scale, gu.ptr(do1))
+    sjk.check_sticky()
+    r1 = np.zeros(D, np.float32)
+    oracle_lib.lib().ora_attend_row(C.byref(oc.c), B, 1500, np.ascontiguousarray(qr[2, 3]), 1, 1000, scale, r1)
+    assert gu.rel_err_rows(gu.host(do1, np.float32)[None], r1[None]) <= ATTN_TOL_TIGHT
+    L.sj_kvarn_layer_free(C.byref(layer))
+    oc.close()
+
+
+def _expected_states():
+    exp = {}
+    for ln in open(os.path.join(GOLDEN, "expected_state.txt")):
+        m = re.match(r"state (\S+) v1 hash=([0-9a-f]+)", ln)
+        if m:
+            exp[m.group(1)] = int(m.group(2), 16)
+    return exp
+
+
+@pytest.mark.parametrize("name,bk,bv,tr,st,sf,fc", seqbuild.GOLDEN_CFGS)
+def test_state_stream_golden(L, oracle_lib, name, bk, bv, tr, st, sf, fc):
+    """The reference's 5 golden state streams (tests/expected_state.txt), built through the product's
+    sequence API on the GPU: sink, ring and record bytes through the policy, pinned end to end."""
+    cfg = sjk.config(seqbuild.D, seqbuild.H, seqbuild.NCTX, 64, bits_k=bk, bits_v=bv, body=tr, staging=st,
+                     sink_type=0 if sf else 1, tail=seqbuild.TAIL, tail_max=seqbuild.TAILMAX, flush_chunk=fc)
+    s = gu.DevSeq(cfg, seqbuild.NL)
+    assert seqbuild.grow(s, 23, 0, 1500, 4) == 0
+    assert oracle_lib.fnv(s.state()) == _expected_states()[name]
+    s.close()
+
+
+def test_state_roundtrip_pool_and_truncate(L, oracle_lib):
+    """write -> read -> write is byte-identical, also into a pooled sequence with shifted block ids;
+    truncation then re-prefill equals a fresh build (reference tests/test_state.c:125-240)."""
+    cfg = sjk.config(seqbuild.D, seqbuild.H, seqbuild.NCTX, 64, bits_k=3, bits_v=2, body=1,
+                     tail=seqbuild.TAIL, tail_max=seqbuild.TAILMAX)
+    a = gu.DevSeq(cfg, seqbuild.NL)
+    seqbuild.grow(a, 23, 0, 1500, 4)
+    s1 = a.state()
+    cfg2 = sjk.config(seqbuild.D, seqbuild.H, seqbuild.NCTX + 1000, 512, bits_k=3, bits_v=2, body=1,
+                      tail=seqbuild.TAIL, tail_max=seqbuild.TAILMAX)
+    b = gu.DevSeq(cfg2, seqbuild.NL)
+    assert b.read_state(s1) == 0
+    assert np.array_equal(b.state(), s1)
+    pool = sjk.Pool()
+    sjk.check(L.sj_kvarn_pool_init(C.byref(pool), C.byref(cfg), seqbuild.NL, 40))
+    L.sj_kvarn_pool_alloc(C.byref(pool))                      # shift block ids
+    p = gu.DevSeq(cfg, seqbuild.NL, pool)
+    assert p.read_state(s1) == 0
+    assert np.array_equal(p.state(), s1)
+    # continuation after restore stays identical
+    for q in (a, b, p):
+        seqbuild.grow(q, 23, 1500, 1800, 5)
+    sa = a.state()
+    assert np.array_equal(b.state(), sa) and np.array_equal(p.state(), sa)
+    # truncate inside a group + regrow an edited suffix == fresh build of the edited stream
+    cut = a.pol.B - 128 - 5
+    r = a.truncate(cut)
+    assert r == 128 + 128 * ((cut - 128) // 128)
+    seqbuild.grow(a, 23, a.n, 1760, 3, edit_from=cut, edit_variant=1)
+    f = gu.DevSeq(cfg, seqbuild.NL)
+    seqbuild.grow(f, 23, 0, 1760, 2, edit_from=cut, edit_variant=1)
+    a.idle(0); f.idle(0)
+    assert a.pol.B == f.pol.B
+    sa, sf = a.state(), f.state()
+    assert np.array_equal(sa[128:-8], sf[128:-8])
+    # a damaged stream is rejected and leaves the target unchanged
+    before = b.state()
+    bad = s1.copy(); bad[len(bad) // 2] ^= 0x10
+    assert b.read_state(bad) == -107
+    assert np.array_equal(b.state(), before)
+    for q in (a, b, p, f):
+        q.close()
+    assert pool.n_free == pool.n_blocks - 1
+    L.sj_kvarn_pool_free(C.byref(pool))
