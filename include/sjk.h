@@ -297,6 +297,9 @@ typedef struct sjk_view {
 } sjk_view;
 
 int          sjk_last_error(void);          /* sticky status of the void-returning calls; clears it */
+/* Device status word of the kernels (synchronizes the device): 0 = fine, 1 = a bounded in-kernel wait ran
+ * out (the kernel skipped its remaining work and released its resources). Reading clears it. */
+int          sjk_device_status(void);
 int          sjk_last_cuda_error(void);     /* cudaError_t of the last failed CUDA call */
 const char * sjk_version(void);
 

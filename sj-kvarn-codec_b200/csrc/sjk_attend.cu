@@ -27,8 +27,10 @@ struct AttnParams {
     const float * q;
     float scale;
     float * part;                   // [splits][n_q*n_head][D + 2]: m, l, o[D]
+    int split0;                     // partial slot of this kernel's first split
     int chunks_per_split, n_chunks;
     uint32_t n_sink_chunks, n_body_chunks;
+    uint32_t body_skip;             // leading body records handled by the tensor-core kernel
 };
 
 struct Chunk { int region; uint32_t p0, len, g; };   // region 0 sink, 1 body, 2 ring
@@ -41,7 +43,7 @@ SJK_DEV Chunk chunk_of(const AttnParams & p, uint32_t ci) {
         c.region = 0; c.p0 = ci * 128u; c.len = min(128u, s_end - c.p0); c.g = 0;
     } else if (ci < p.n_sink_chunks + p.n_body_chunks) {
         const uint32_t b_end = p.B < p.N ? p.B : p.N;      // a query over a prefix may end inside a record
-        c.region = 1; c.g = ci - p.n_sink_chunks; c.p0 = S + c.g * 128u; c.len = min(128u, b_end - c.p0);
+        c.region = 1; c.g = p.body_skip + ci - p.n_sink_chunks; c.p0 = S + c.g * 128u; c.len = min(128u, b_end - c.p0);
     } else {
         const uint32_t k = ci - p.n_sink_chunks - p.n_body_chunks;
         const uint32_t b0 = p.B > S ? p.B : S;
@@ -216,31 +218,41 @@ __global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
     __syncthreads();
     if (r_own < R) {
         const int iq = r_own / p.grp, hq = hl * p.grp + r_own % p.grp;
-        float * dst = p.part + ((size_t) split * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
+        float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
         if (g_own == 0) { dst[0] = rowm[r_own]; dst[1] = rowl[r_own]; }
 #pragma unroll
         for (int i = 0; i < D / 16; ++i) dst[2 + g_own + 16 * i] = acc[i];
     }
 }
 
-// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m)
+// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m); one CTA per (query row, query head),
+// the split weights are computed once into shared memory
 __global__ void attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out) {
+    extern __shared__ float wts[];                     // [splits]
+    __shared__ float s_m, s_inv;
     const int row = blockIdx.x;
-    float m = -__int_as_float(0x7F800000);
-    for (int i = 0; i < splits; ++i) m = fmaxf(m, part[((size_t) i * n_rows + row) * (D + 2)]);
-    float den = 0.0f;
-    for (int i = 0; i < splits; ++i) {
-        const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
-        if (pp[0] != -__int_as_float(0x7F800000)) den += pp[1] * expf(pp[0] - m);
+    if (threadIdx.x < 32) {
+        float m = -__int_as_float(0x7F800000);
+        for (int i = threadIdx.x; i < splits; i += 32) m = fmaxf(m, part[((size_t) i * n_rows + row) * (D + 2)]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        float den = 0.0f;
+        for (int i = threadIdx.x; i < splits; i += 32) {
+            const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
+            const float w = pp[0] == -__int_as_float(0x7F800000) ? 0.0f : expf(pp[0] - m);
+            wts[i] = w;
+            den += pp[1] * w;
+        }
+        for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+        if (threadIdx.x == 0) { s_m = m; s_inv = den == 0.0f ? 0.0f : 1.0f / den; }
     }
-    const float inv = den == 0.0f ? 0.0f : 1.0f / den;
+    __syncthreads();
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float o = 0.0f;
         for (int i = 0; i < splits; ++i) {
-            const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
-            if (pp[0] != -__int_as_float(0x7F800000)) o += pp[2 + d] * expf(pp[0] - m);
+            const float w = wts[i];
+            if (w != 0.0f) o += part[((size_t) i * n_rows + row) * (D + 2) + 2 + d] * w;
         }
-        out[(size_t) row * D + d] = o * inv;
+        out[(size_t) row * D + d] = o * s_inv;
     }
 }
 
@@ -253,13 +265,14 @@ int split_target(int n_kv) {
     return t < 1 ? 1 : t;
 }
 
-Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv) {
+Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip) {
     Plan pl;
     const uint32_t S = v->S;
     const uint32_t s_end = S < N ? S : N;
     pl.n_sink = (s_end + 127u) / 128u;
     const uint32_t b_end = B < N ? B : N;
     pl.n_body = b_end > S ? (b_end - S + 127u) / 128u : 0u;
+    pl.n_body = pl.n_body > body_skip ? pl.n_body - body_skip : 0u;
     const uint32_t t0 = B > S ? B : S;
     const uint32_t n_tail = N > t0 ? (N - t0 + 127u) / 128u : 0u;
     pl.n_chunks = (int) (pl.n_sink + pl.n_body + n_tail);
@@ -279,7 +292,8 @@ size_t split_smem() {
 
 size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv) {
     if (!v || n_q <= 0 || n_head <= 0) return 0;
-    return (size_t) split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    // CUDA-core splits plus tensor-core splits, each bounded by the per-call target
+    return (size_t) 2 * split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
 }
 
 extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head) {
@@ -296,34 +310,49 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (B < v->S) return SJKVARN_ERR_ARG;
     const int grp = n_head / n_kv;
     if (n_q * grp > MAXROWS) return SJK_ERR_UNSUPPORTED;
-    const Plan pl = make_plan(v, B, N, n_kv);
-    const size_t need = (size_t) pl.splits * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    // sealed records [0, n_tc) go to the tensor-core kernel when it supports the body format
+    const uint32_t b_end = B < N ? B : N;
+    const uint32_t n_tc = (sjk_tc_body_supported(v, n_q, grp) && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
+    int rps = 1;
+    const int splits_tc = sjk_tc_body_splits(n_tc, n_kv, &rps);
+    const Plan pl = make_plan(v, B, N, n_kv, n_tc);
+    const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
+    const int splits = splits_tc + splits_v1;
+    const size_t need = (size_t) splits * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
-    if (pl.n_chunks == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
+    if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
+    if (splits_tc) {
+        const int rc = sjk_tc_body_launch(v, n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch, 0,
+                                          splits_tc, rps, st);
+        if (rc) return rc;
+    }
     AttnParams p;
     p.v = *v; p.kv0 = kv_head0; p.B = B; p.N = N; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = grp;
-    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch;
+    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch; p.split0 = splits_tc;
     p.chunks_per_split = pl.chunks_per_split; p.n_chunks = pl.n_chunks; p.n_sink_chunks = pl.n_sink; p.n_body_chunks = pl.n_body;
-    const dim3 grid((unsigned) pl.splits, (unsigned) n_kv);
-    cudaError_t e = cudaSuccess;
-    switch (v->lay.D) {
-        case 128: {
-            const size_t sm = split_smem<128>();
-            e = cudaFuncSetAttribute(attend_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
-            if (e == cudaSuccess) attend_split_kernel<128><<<grid, NT, sm, st>>>(p);
-            break;
+    p.body_skip = n_tc;
+    if (splits_v1) {
+        const dim3 grid((unsigned) splits_v1, (unsigned) n_kv);
+        cudaError_t e = cudaSuccess;
+        switch (v->lay.D) {
+            case 128: {
+                const size_t sm = split_smem<128>();
+                e = cudaFuncSetAttribute(attend_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_kernel<128><<<grid, NT, sm, st>>>(p);
+                break;
+            }
+            case 256: {
+                const size_t sm = split_smem<256>();
+                e = cudaFuncSetAttribute(attend_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_kernel<256><<<grid, NT, sm, st>>>(p);
+                break;
+            }
+            default: return SJK_ERR_UNSUPPORTED;
         }
-        case 256: {
-            const size_t sm = split_smem<256>();
-            e = cudaFuncSetAttribute(attend_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
-            if (e == cudaSuccess) attend_split_kernel<256><<<grid, NT, sm, st>>>(p);
-            break;
-        }
-        default: return SJK_ERR_UNSUPPORTED;
+        if (sjk_check(e)) return SJK_ERR_DEVICE;
+        if (sjk_check_launch()) return SJK_ERR_DEVICE;
     }
-    if (sjk_check(e)) return SJK_ERR_DEVICE;
-    if (sjk_check_launch()) return SJK_ERR_DEVICE;
-    attend_merge_kernel<<<n_q * n_head, 128, 0, st>>>(p.part, pl.splits, n_q * n_head, v->lay.D, out);
+    attend_merge_kernel<<<n_q * n_head, 256, (size_t) splits * sizeof(float), st>>>(p.part, splits, n_q * n_head, v->lay.D, out);
     return sjk_check_launch();
 }
 

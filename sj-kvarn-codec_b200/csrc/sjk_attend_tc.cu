@@ -1,0 +1,502 @@
+// sjk_attend_tc.cu - tensor-core (tcgen05, kind::i8) attention over the sealed body of a 4-bit scalar layer.
+//
+// One CTA = one KV head x a contiguous range of records, 256 threads (8 warps); warp w owns TMEM lane
+// quarter w % 4, and the two warps of a quarter split the columns (half = w / 4). The query rows of the
+// KV head (decode width x GQA group, padded to N = 16) are the MMA's N dimension, the 128 tokens (K side)
+// or 128 channels (V side, two tiles) its M dimension:
+//
+//   K side  S^T[t, r] = sum_d code_K[t, d] * Q'[r, d],   Q'[r, d] = q[r, d] * Kscale[d]
+//           dot[t, r] = Ktok[t] * (S^T[t, r] + sum_d q[r, d] * Kzero[d])
+//   V side  O^T[d, r] = sum_t code_V[d, t] * P'[r, t],   P'[r, t] = p[r, t] * Vscale[t]
+//           out[d, r] = Vch[d] * (O^T[d, r] + sum_t p[r, t] * Vzero[t])
+//
+// i.e. the reference reconstruction K = (q*Ks + Kz)*Kt, V = (q*Vs + Vz)*Vc (sj_kvarn.h:1187-1207) regrouped
+// so the 4-bit codes enter the tensor core as exact signed 8-bit integers (A operand in TMEM, unpacked from
+// the fragment-ordered payload with LOP3/PRMT). Q' and P' are each rounded to a 21-bit integer after an
+// exact power-of-two rescale (per query row; P' by the row's largest weight in the record) and split into
+// three signed 8-bit digits (B operands in shared memory); each digit is its own exact s32 accumulation
+// and the digits recombine in fp32. Integer <-> float conversions use the 1.5 * 2^23 magic constant, so the XU pipe is left to exp2.
+//
+// Records stream in through a double-buffered 1-D bulk copy (cp.async.bulk, no multicast). All waits are
+// bounded (sjk_tc.cuh); the kernel always waits for its own copies and MMAs and releases its TMEM.
+#include "sjk_common.cuh"
+#include "sjk_internal.h"
+#include "sjk_tc.cuh"
+
+namespace {
+
+constexpr int NT = 256;
+constexpr int NR = 16;                  // MMA N: query rows per KV head, padded
+constexpr int D = 256;
+constexpr int G = 128;
+constexpr uint32_t TM_COLS = 256;
+constexpr uint32_t COL_AK = 0;          // A for K: 128 lanes x 256 s8 = 64 columns (dead once the K MMAs end)
+constexpr uint32_t COL_O = 0;           // O^T: 2 tiles x 3 digits x 16 columns, written after A_K is dead
+constexpr uint32_t COL_AV = 96;         // A for V: 2 tiles x 128 lanes x 128 s8 = 2 x 32 columns
+constexpr uint32_t COL_S = 160;         // S^T digits: 3 x 16 columns
+constexpr float MAGIC = 12582912.0f;    // 1.5 * 2^23
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+struct TcParams {
+    sj_kvarn_layout lay;
+    const uint8_t * body;
+    const uint32_t * blocks;
+    int H, kv0;
+    uint32_t S;                 // sink length: record g covers positions S + 128 g ..
+    uint32_t n_rec;             // sealed records per head in [S, B)
+    uint32_t qpos0;
+    int n_q, n_head, grp, rows;
+    const float * q;
+    float scale;
+    float * part;               // [splits][n_q*n_head][D + 2]
+    int split0;                 // partial slot of this kernel's first split
+    int recs_per_split;
+};
+
+// shared memory (bytes)
+constexpr uint32_t REC_MAX = 35072;
+constexpr uint32_t OFF_REC0 = 0;
+constexpr uint32_t OFF_REC1 = REC_MAX;
+constexpr uint32_t OFF_BK = 2 * REC_MAX;            // 3 digits x [16 rows x 256] s8
+constexpr uint32_t OFF_BV = OFF_BK + 3 * 4096;      // 3 digits x [16 rows x 128] s8
+constexpr uint32_t OFF_RED = OFF_BV + 3 * 2048;     // 4 reduction areas x 128 floats
+constexpr uint32_t OFF_ROW = OFF_RED + 4 * 128 * 4;
+constexpr uint32_t OFF_BAR = OFF_ROW + 12 * 16 * 4;
+constexpr uint32_t OFF_TMEM = OFF_BAR + 32;
+constexpr uint32_t SMEM_TOTAL = OFF_TMEM + 16;
+// per-row broadcast arrays (16 floats each) inside OFF_ROW
+enum { ROW_C = 0, ROW_KINV = 16, ROW_M2 = 32, ROW_MNEW = 48, ROW_ALPHA = 64, ROW_L = 80, ROW_Z = 96, ROW_MAXK = 112,
+       ROW_MAXV = 128, ROW_VSCL = 144, ROW_VINV = 160 };
+enum { RED_C = 0, RED_MAX = 128, RED_L = 256, RED_Z = 384 };
+
+// element (row n, k) of a K-major, no-swizzle s8 B operand with 16 rows: 8-row x 16-byte core matrices,
+// 256 bytes per 16-element K chunk (an MMA's 32-element K step is 512 bytes: LBO 256, SBO 128)
+__device__ __forceinline__ uint32_t b_off(int n, int k) { return (uint32_t) ((k >> 4) * 256 + n * 16 + (k & 15)); }
+
+__device__ __forceinline__ int pow2_exp(float x) { return (int) ((__float_as_uint(x) >> 23) & 0xFF) - 126; }  // x < 2^e
+__device__ __forceinline__ float pow2f(int e) {
+    e = e < -126 ? -126 : (e > 127 ? 127 : e);
+    return __uint_as_float((uint32_t) (e + 127) << 23);
+}
+// exact fp16 -> fp32 for every finite half (scales of sealed records are finite)
+__device__ __forceinline__ float h2f(uint16_t h) {
+    const float mag = __uint_as_float(((uint32_t) h & 0x7FFFu) << 13) * 5.192296858534828e33f;   // x 2^112
+    return __uint_as_float(__float_as_uint(mag) | (((uint32_t) h & 0x8000u) << 16));
+}
+__device__ __forceinline__ float h2f_at(const uint8_t * p) { return h2f(*reinterpret_cast<const uint16_t *>(p)); }
+// float -> nearest integer and back (|v| < 2^22) without the conversion pipe
+__device__ __forceinline__ int f2i(float v) { return (int) (__float_as_uint(v + MAGIC) - MAGIC_BITS); }
+__device__ __forceinline__ float i2f(uint32_t x) { return __uint_as_float(x + MAGIC_BITS) - MAGIC; }
+__device__ __forceinline__ int sext8(int x) { return (x << 24) >> 24; }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Reduce 8 per-thread values across the 32 lanes; afterwards lanes 4r..4r+3 hold row r.
+template <bool MAX>
+__device__ __forceinline__ float warp_rows8(const float (&v)[8], int lane) {
+    float a[4], b[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? v[i] : v[i + 4], keep = up ? v[i + 4] : v[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+        a[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+        b[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+    const bool up = lane & 4;
+    const float send = up ? b[0] : b[1], keep = up ? b[1] : b[0];
+    float r = __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+    float c = MAX ? fmaxf(keep, r) : keep + r;
+    r = __shfl_xor_sync(0xFFFFFFFFu, c, 2);
+    c = MAX ? fmaxf(c, r) : c + r;
+    r = __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+    return MAX ? fmaxf(c, r) : c + r;
+}
+
+// 16 consecutive K elements of one 16x16 tile from its 4 fragment-order words (the thread's row is in the
+// nibbles selected by `shift`): word j holds elements {2j, 2j+8, 2j+1, 2j+9} -> 4 columns of 4 bytes
+__device__ __forceinline__ void unpack16(uint4 w, int shift, uint32_t * col) {
+    const uint32_t b0 = (w.x >> shift) & 0x0F0F0F0Fu, b1 = (w.y >> shift) & 0x0F0F0F0Fu;
+    const uint32_t b2 = (w.z >> shift) & 0x0F0F0F0Fu, b3 = (w.w >> shift) & 0x0F0F0F0Fu;
+    col[0] = prmt(b0, b1, 0x6420u);      // elements 0..3
+    col[1] = prmt(b2, b3, 0x6420u);      // 4..7
+    col[2] = prmt(b0, b1, 0x7531u);      // 8..11
+    col[3] = prmt(b2, b3, 0x7531u);      // 12..15
+}
+
+__global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;   // tl: this thread's TMEM lane
+    const int hl = blockIdx.y, h = p.kv0 + hl, split = blockIdx.x;
+    const sj_kvarn_layout & l = p.lay;
+    uint8_t * rec_buf[2] = {sm + OFF_REC0, sm + OFF_REC1};
+    uint8_t * bk = sm + OFF_BK;
+    uint8_t * bv = sm + OFF_BV;
+    float * red = reinterpret_cast<float *>(sm + OFF_RED);
+    float * row = reinterpret_cast<float *>(sm + OFF_ROW);
+    uint64_t * bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);    // [0],[1] record loads, [2] MMAs
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
+
+    const uint32_t r_begin = (uint32_t) split * (uint32_t) p.recs_per_split;
+    const uint32_t r_end = min(r_begin + (uint32_t) p.recs_per_split, p.n_rec);
+
+    if (warp == 0) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
+    if (tid == 0) {
+        tc::mbar_init(&bars[0], 1); tc::mbar_init(&bars[1], 1); tc::mbar_init(&bars[2], 1);
+        tc::mbar_fence_init();
+    }
+    if (tid < NR) { row[ROW_M2 + tid] = -INFINITY; row[ROW_L + tid] = 0.0f; }
+
+    // B_K builder role: channels 4bg..4bg+3 x rows 4brg..4brg+3 per thread, query values kept in registers
+    const int bg = tid & 63, brg = tid >> 6;
+    float qv[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 4 * brg + i;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float v = 0.0f;
+            if (r < p.rows) {
+                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
+                v = p.q[((size_t) iq * p.n_head + hq) * D + 4 * bg + j];
+            }
+            qv[i][j] = v;
+        }
+    }
+    int kcol[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kcol[j] = sjk_k_ch(l, 4 * bg + j);
+    const int vcol = sjk_v_ch(l, 128 * half + tl);
+    // per-row max |q| over the 256 channels (rows 4brg.. live in warps 2brg and 2brg + 1)
+    float qmax[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float m = fmaxf(fmaxf(fabsf(qv[i][0]), fabsf(qv[i][1])), fmaxf(fabsf(qv[i][2]), fabsf(qv[i][3])));
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        qmax[i] = m;
+    }
+    if (lane == 0) for (int i = 0; i < 4; ++i) red[RED_C + warp * 4 + i] = qmax[i];
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qmax[i] = fmaxf(red[RED_C + (2 * brg) * 4 + i], red[RED_C + (2 * brg + 1) * 4 + i]);
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
+    const uint32_t idesc = tc::idesc_s8(128, NR);
+    const float sl2 = p.scale * LOG2E;
+
+    float acc[NR];                                    // running output of channel 128 half + tl, all rows
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+    bool ok = true;
+    uint32_t mma_phase = 0;
+    int load_pending = -1;
+    bool mma_pending = false;
+
+    auto rec_ptr = [&](uint32_t g) -> const uint8_t * {
+        const uint32_t blk = p.blocks ? p.blocks[g] : g;
+        return p.body + ((size_t) blk * p.H + h) * l.bytes;
+    };
+    __syncthreads();                                  // red[] reused below
+    if (r_begin < r_end) {
+        if (tid == 0) { tc::mbar_expect_tx(&bars[0], l.bytes); tc::bulk_g2s(rec_buf[0], rec_ptr(r_begin), l.bytes, &bars[0]); }
+        load_pending = 0;
+    }
+
+    for (uint32_t g = r_begin; g < r_end; ++g) {
+        const uint32_t it = g - r_begin, buf = it & 1u;
+        const uint8_t * rec = rec_buf[buf];
+        ok = __syncthreads_and(tc::mbar_wait(&bars[buf], (it >> 1) & 1u));
+        if (!ok) break;
+        load_pending = -1;
+        if (g + 1 < r_end) {
+            if (tid == 0) {
+                tc::mbar_expect_tx(&bars[buf ^ 1u], l.bytes);
+                tc::bulk_g2s(rec_buf[buf ^ 1u], rec_ptr(g + 1), l.bytes, &bars[buf ^ 1u]);
+            }
+            load_pending = (int) it + 1;
+        }
+        // ---- A: scales, record-wide maxima, A_K (token tl, channel tiles 8 half .. 8 half + 7) ----
+        float ks[4], kz[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { ks[j] = h2f_at(rec + l.k_scale + 2 * kcol[j]); kz[j] = h2f_at(rec + l.k_zero + 2 * kcol[j]); }
+        const float kt = h2f_at(rec + l.k_tok + 2 * tl);
+        const float vsc = h2f_at(rec + l.v_scale + 2 * tl);
+        const float vz = h2f_at(rec + l.v_zero + 2 * tl);
+        const float vc = h2f_at(rec + l.v_ch + 2 * vcol);
+        {
+            float mk = fmaxf(fmaxf(fabsf(ks[0]), fabsf(ks[1])), fmaxf(fabsf(ks[2]), fabsf(ks[3])));
+            float mv = fabsf(vsc);
+            for (int o = 16; o; o >>= 1) {
+                mk = fmaxf(mk, __shfl_xor_sync(0xFFFFFFFFu, mk, o));
+                mv = fmaxf(mv, __shfl_xor_sync(0xFFFFFFFFu, mv, o));
+            }
+            if (lane == 0) { row[ROW_MAXK + warp] = mk; row[ROW_MAXV + warp] = mv; }
+        }
+        {
+            const int t = tl, shift = (t & 8) ? 4 : 0;
+            const uint8_t * kp = rec + l.k_payload;
+            uint32_t colv[16];
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) {
+                const int c = 8 * half + c8;
+                const uint4 w = *reinterpret_cast<const uint4 *>(kp + ((((t >> 4) * 16 + c) * 32) + 4 * (t & 7)) * 4);
+                unpack16(w, shift, colv + 4 * (c8 & 3));
+                if ((c8 & 3) == 3) tc::st_x16(tmem + lane_base + COL_AK + 32 * half + 16 * (c8 >> 2), colv);
+            }
+        }
+        __syncthreads();                                                          // S1
+        // ---- B: B_K = three s8 digits of round(Q' 2^e), zero-point partials ----
+        {
+            float maxk = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) maxk = fmaxf(maxk, row[ROW_MAXK + w]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = 4 * brg + i;
+                const float bound = qmax[i] * maxk;
+                const int e = (bound > 0.0f && bound < INFINITY) ? 21 - pow2_exp(bound) : 0;
+                const float sc = pow2f(e);
+                if (bg == 0) row[ROW_KINV + r] = pow2f(-e);
+                uint32_t dg0 = 0, dg1 = 0, dg2 = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int x = f2i((qv[i][j] * ks[j]) * sc);
+                    const int d0 = sext8(x), x1 = (x - d0) >> 8, d1 = sext8(x1), d2 = (x1 - d1) >> 8;
+                    dg0 |= ((uint32_t) d0 & 0xFFu) << (8 * j);
+                    dg1 |= ((uint32_t) d1 & 0xFFu) << (8 * j);
+                    dg2 |= ((uint32_t) d2 & 0xFFu) << (8 * j);
+                }
+                const uint32_t off = b_off(r, 4 * bg);
+                *reinterpret_cast<uint32_t *>(bk + off) = dg0;
+                *reinterpret_cast<uint32_t *>(bk + 4096 + off) = dg1;
+                *reinterpret_cast<uint32_t *>(bk + 8192 + off) = dg2;
+                float c = (qv[i][0] * kz[0] + qv[i][1] * kz[1]) + (qv[i][2] * kz[2] + qv[i][3] * kz[3]);
+                for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+                if (lane == 0) red[RED_C + warp * 4 + i] = c;
+            }
+        }
+        tc::wait_st();
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        __syncthreads();                                                          // S2
+        tc::fence_after_sync();
+        if (tid == 0) {
+#pragma unroll 1
+            for (int dg = 0; dg < 3; ++dg)
+                for (int k = 0; k < D / 32; ++k)
+                    tc::mma_ts_i8(tmem + COL_S + 16 * dg, tmem + COL_AK + 8 * k,
+                                  tc::smem_desc(bk + 4096 * dg + 512 * k, 256, 128), idesc, k ? 1u : 0u);
+            tc::mma_commit(&bars[2]);
+        }
+        mma_pending = true;
+        if (tid < NR) row[ROW_C + tid] = red[RED_C + (2 * (tid >> 2)) * 4 + (tid & 3)] + red[RED_C + (2 * (tid >> 2) + 1) * 4 + (tid & 3)];
+        // ---- C: A_V (channel 128 half + tl over the 8 token tiles), overlapping the K MMAs ----
+        {
+            const int d = 128 * half + tl, shift = (d & 8) ? 4 : 0;
+            const uint8_t * vp = rec + l.v_payload;
+            uint32_t colv[16];
+#pragma unroll
+            for (int s8 = 0; s8 < 8; ++s8) {
+                const uint4 w = *reinterpret_cast<const uint4 *>(vp + (((s8 * 16 + (d >> 4)) * 32) + 4 * (d & 7)) * 4);
+                unpack16(w, shift, colv + 4 * (s8 & 3));
+                if ((s8 & 3) == 3) tc::st_x16(tmem + lane_base + COL_AV + 32 * half + 16 * (s8 >> 2), colv);
+            }
+        }
+        tc::wait_st();
+        ok = __syncthreads_and(tc::mbar_wait(&bars[2], mma_phase));              // S3: K MMAs done
+        if (!ok) break;
+        mma_phase ^= 1u;
+        mma_pending = false;
+        tc::fence_after_sync();
+        // ---- D: scores of token tl for rows 8 half .. 8 half + 7, log2 domain; row maxima ----
+        float s2[8];
+        {
+            uint32_t a0[8], a1[8], a2[8];
+            tc::ld_x8_u(tmem + lane_base + COL_S + 8 * half, a0);
+            tc::ld_x8_u(tmem + lane_base + COL_S + 16 + 8 * half, a1);
+            tc::ld_x8_u(tmem + lane_base + COL_S + 32 + 8 * half, a2);
+            tc::wait_ld();
+            const uint32_t pos = p.S + g * (uint32_t) G + (uint32_t) tl;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = 8 * half + i;
+                const float S = fmaf(65536.0f, i2f(a2[i]), fmaf(256.0f, i2f(a1[i]), i2f(a0[i])));
+                const uint32_t qpos = p.qpos0 + (uint32_t) (r / p.grp);
+                const float dot = kt * fmaf(S, row[ROW_KINV + r], row[ROW_C + r]);
+                s2[i] = (r < p.rows && pos <= qpos) ? dot * sl2 : -INFINITY;
+            }
+            const float mw = warp_rows8<true>(s2, lane);
+            if ((lane & 3) == 0) red[RED_MAX + half * 32 + quarter * 8 + (lane >> 2)] = mw;
+        }
+        __syncthreads();                                                          // S4
+        if (tid < NR) {
+            const int hh = tid >> 3, rr = tid & 7;
+            const float * mr = red + RED_MAX + hh * 32 + rr;
+            const float mrec = fmaxf(fmaxf(mr[0], mr[8]), fmaxf(mr[16], mr[24]));
+            const float mold = row[ROW_M2 + tid], mnew = fmaxf(mold, mrec);
+            row[ROW_MNEW + tid] = mnew;
+            row[ROW_ALPHA + tid] = mnew == -INFINITY ? 1.0f : ex2(mold - mnew);
+            row[ROW_M2 + tid] = mnew;
+            // P' = p Vscale of this row is at most ex2(mrec - mnew) * max Vscale: rescale it to < 2^21
+            float maxv = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) maxv = fmaxf(maxv, row[ROW_MAXV + w]);
+            const float bound = (mrec == -INFINITY ? 0.0f : ex2(mrec - mnew)) * maxv;
+            const int ev = (bound > 0.0f && bound < INFINITY) ? 21 - pow2_exp(bound) : 0;
+            row[ROW_VSCL + tid] = pow2f(ev);
+            row[ROW_VINV + tid] = pow2f(-ev);
+        }
+        __syncthreads();                                                          // S5
+        // ---- E: weights p, B_V = two s8 digits of round(P' 2^ev), row sums ----
+        {
+            float ls[8], zs[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = 8 * half + i;
+                const float mnew = row[ROW_MNEW + r];
+                const float pw = mnew == -INFINITY ? 0.0f : ex2(s2[i] - mnew);
+                ls[i] = pw;
+                zs[i] = pw * vz;
+                const int x = f2i((pw * vsc) * row[ROW_VSCL + r]);
+                const int d0 = sext8(x), x1 = (x - d0) >> 8, d1 = sext8(x1), d2 = (x1 - d1) >> 8;
+                const uint32_t off = b_off(r, tl);
+                bv[off] = (uint8_t) d0;
+                bv[2048 + off] = (uint8_t) d1;
+                bv[4096 + off] = (uint8_t) d2;
+            }
+            const float lw = warp_rows8<false>(ls, lane);
+            const float zw = warp_rows8<false>(zs, lane);
+            if ((lane & 3) == 0) {
+                red[RED_L + half * 32 + quarter * 8 + (lane >> 2)] = lw;
+                red[RED_Z + half * 32 + quarter * 8 + (lane >> 2)] = zw;
+            }
+        }
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        __syncthreads();                                                          // S6
+        tc::fence_after_sync();
+        if (tid == 0) {
+#pragma unroll 1
+            for (int tile = 0; tile < 2; ++tile)
+                for (int dg = 0; dg < 3; ++dg)
+                    for (int k = 0; k < G / 32; ++k)
+                        tc::mma_ts_i8(tmem + COL_O + 48 * tile + 16 * dg, tmem + COL_AV + 32 * tile + 8 * k,
+                                      tc::smem_desc(bv + 2048 * dg + 512 * k, 256, 128), idesc, k ? 1u : 0u);
+            tc::mma_commit(&bars[2]);
+        }
+        mma_pending = true;
+        if (tid < NR) {
+            const int hh = tid >> 3, rr = tid & 7;
+            const float * lr = red + RED_L + hh * 32 + rr;
+            const float * zr = red + RED_Z + hh * 32 + rr;
+            row[ROW_L + tid] = row[ROW_L + tid] * row[ROW_ALPHA + tid] + ((lr[0] + lr[8]) + (lr[16] + lr[24]));
+            row[ROW_Z + tid] = (zr[0] + zr[8]) + (zr[16] + zr[24]);
+        }
+        ok = __syncthreads_and(tc::mbar_wait(&bars[2], mma_phase));              // S7: V MMAs done
+        if (!ok) break;
+        mma_phase ^= 1u;
+        mma_pending = false;
+        tc::fence_after_sync();
+        // ---- F: epilogue, channel 128 half + tl ----
+        {
+            uint32_t o0[16], o1[16], o2[16];
+            tc::ld_x16_u(tmem + lane_base + COL_O + 48 * half, o0);
+            tc::ld_x16_u(tmem + lane_base + COL_O + 48 * half + 16, o1);
+            tc::ld_x16_u(tmem + lane_base + COL_O + 48 * half + 32, o2);
+            tc::wait_ld();
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const float O = fmaf(65536.0f, i2f(o2[r]), fmaf(256.0f, i2f(o1[r]), i2f(o0[r]))) * row[ROW_VINV + r];
+                acc[r] = fmaf(acc[r], row[ROW_ALPHA + r], vc * (O + row[ROW_Z + r]));
+            }
+        }
+        tc::fence_before_sync();
+        __syncthreads();                                                          // S8
+        tc::fence_after_sync();
+    }
+
+    // ---- drain: a timed-out CTA still waits (bounded) for its own copies and MMAs before releasing TMEM ----
+    if (!ok) {
+        if (load_pending >= 0) tc::mbar_wait(&bars[load_pending & 1], ((uint32_t) load_pending >> 1) & 1u);
+        if (mma_pending) tc::mbar_wait(&bars[2], mma_phase);
+    }
+    // ---- partials (m in the natural-log domain, l, o[D]) per real query row ----
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        if (r < p.rows) {
+            const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
+            float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
+            if (tid == 0) {
+                const float m2 = row[ROW_M2 + r];
+                dst[0] = ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
+                dst[1] = ok ? row[ROW_L + r] : 0.0f;
+            }
+            dst[2 + 128 * half + tl] = ok ? acc[r] : 0.0f;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) tc::tmem_dealloc(tmem, TM_COLS);
+}
+
+}  // namespace
+
+// ---- host side ---------------------------------------------------------------------------------------------
+
+// Whether the tensor-core body path applies: 4-bit scalar records (fragment-ordered payload), D = 256,
+// at most 16 query rows per KV head.
+int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp) {
+    const sj_kvarn_layout & l = v->lay;
+    return l.D == 256 && l.G == 128 && l.body == SJKVARN_BODY_SCALAR && l.bits_k == 4 && l.bits_v == 4 &&
+           n_q * grp <= NR && l.bytes == REC_MAX;
+}
+
+int sjk_tc_body_splits(uint32_t n_rec, int n_kv, int * recs_per_split) {
+    if (n_rec == 0) { *recs_per_split = 1; return 0; }
+    const int target = (2 * 148 + n_kv - 1) / n_kv;            // two CTAs per SM over the call's KV heads
+    int rps = (int) ((n_rec + (uint32_t) target - 1) / (uint32_t) target);
+    if (rps < 1) rps = 1;
+    *recs_per_split = rps;
+    return (int) ((n_rec + (uint32_t) rps - 1) / (uint32_t) rps);
+}
+
+int sjk_tc_body_launch(const sjk_view * v, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
+                       const float * q, float scale, float * part, int split0, int splits, int recs_per_split,
+                       sjk_stream st) {
+    TcParams p;
+    p.lay = v->lay; p.body = v->body; p.blocks = v->blocks; p.H = v->n_head_kv; p.kv0 = kv0; p.S = v->S;
+    p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
+    p.q = q; p.scale = scale; p.part = part; p.split0 = split0; p.recs_per_split = recs_per_split;
+    cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    if (e != cudaSuccess) return sjk_check(e);
+    attend_body_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
+    return sjk_check_launch();
+}
+
+extern "C" int sjk_device_status(void) {
+    int v = 0, zero = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    if (cudaMemcpyFromSymbol(&v, sjk_dev_status, sizeof v) != cudaSuccess) return -1;
+    cudaMemcpyToSymbol(sjk_dev_status, &zero, sizeof zero);
+    return v;
+}

@@ -16,3 +16,10 @@ size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, i
 int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, float * vo, sjk_stream st);
 // decode row t of one record (is_v selects V) to out[D] (device)
 int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st);
+
+// tensor-core body attention (sjk_attend_tc.cu)
+int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp);
+int sjk_tc_body_splits(uint32_t n_rec, int n_kv, int * recs_per_split);
+int sjk_tc_body_launch(const sjk_view * v, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
+                       const float * q, float scale, float * part, int split0, int splits, int recs_per_split,
+                       sjk_stream st);

@@ -124,6 +124,7 @@ SIGNATURES = {
     # device layer
     "sjk_last_error": (C.c_int, []),
     "sjk_last_cuda_error": (C.c_int, []),
+    "sjk_device_status": (C.c_int, []),
     "sjk_version": (C.c_char_p, []),
     "sjk_hadamard": (C.c_int, [vp, C.c_int, C.c_int, vp]),
     "sjk_stage_rows": (C.c_int, [C.c_int, vp, vp, C.c_size_t, C.c_int, C.c_int, vp]),

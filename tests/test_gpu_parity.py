@@ -2,8 +2,9 @@
 
 Bit-exact: seal records, decoded rows, tq6_0 / fp16 staging bytes, ring and sink bytes, state streams.
 Attention: max relative L2 error per (row, head) <= 1e-3 against the oracle's reference loop (the
-contract); the measured error is also held to 1e-5, the bound of the reference's own device test
-(tests/test_cuda.cu:135)."""
+contract); the measured error is also held to 1e-4. (The reference's own device test uses 1e-5,
+tests/test_cuda.cu:135, for a kernel that sums each dot in the reference's sequential order; the
+tensor-core path sums in another order, which moves scores of magnitude ~10 by ~1e-5.)"""
 import ctypes as C
 import os
 import re
@@ -21,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 ATTN_TOL = 1e-3           # north-star contract (fp32 accumulate)
-ATTN_TOL_TIGHT = 1e-5     # reference device test bound
+ATTN_TOL_TIGHT = 1e-4     # internal bound, 10x inside the contract
 
 
 @pytest.fixture(scope="module")
