@@ -210,7 +210,9 @@ enum {
     /* B200 build only: a CUDA call failed (the CUDA error is in sjk_last_cuda_error()) */
     SJK_ERR_DEVICE            = -200,
     /* B200 build only: a shape the device kernels do not implement (e.g. head_dim > 256) */
-    SJK_ERR_UNSUPPORTED       = -201
+    SJK_ERR_UNSUPPORTED       = -201,
+    /* B200 build only: the shape needs more scratch than sjk_attend_static's fixed buffer holds */
+    SJK_ERR_SCRATCH_LIMIT     = -202
 };
 const char * sj_kvarn_strerror(int code);
 
@@ -337,6 +339,16 @@ int sjk_decode(const sj_kvarn_layout * lay, const uint8_t * body, int n_rec, flo
 size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head);
 int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
                float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st);
+
+/* sjk_attend for callers that cannot allocate device memory - code that runs where cudaMalloc is off
+ * limits, such as inside a stream capture, a custom allocator's own callbacks or an engine whose memory
+ * is planned ahead. No counterpart in the reference. The scratch for the split partials is a fixed 16 MiB
+ * device array inside the library (held by every GPU that loads it, until exit) instead of a caller
+ * buffer; shapes whose sjk_attend_scratch_bytes() bound exceeds 16 MiB return SJK_ERR_SCRATCH_LIMIT.
+ * The array's address is looked up on the first call on each device, so make that first call outside any
+ * stream capture. All calls share the array: calls that overlap on the GPU race. Allocates nothing. */
+int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
+                      float scale, float * out, sjk_stream st);
 
 /* Whole-layer helpers over a device-backed sj_kvarn_layer (its stream is ignored; st used). */
 int sjk_layer_store(sj_kvarn_layer * L, uint32_t pos0, uint32_t n_pos, const float * k, const float * v, int rotate,

@@ -10,6 +10,8 @@
 // Scores use the reference's sequential fp32 dot (sj_kvarn.h:1288-1293) on identically decoded rows, so
 // they are bit-equal to the reference's; only the softmax accumulation order differs (chunk-wise online
 // softmax + merge instead of one position-ordered pass), which the 1e-3 relative contract covers.
+#include <mutex>
+
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
 
@@ -360,4 +362,41 @@ extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t q
                           float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
     if (!v) return SJKVARN_ERR_ARG;
     return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st);
+}
+
+// ---- attention for callers that cannot allocate ------------------------------------------------------------
+// sjk_attend_static: sjk_attend with its split-partial scratch in a fixed device array instead of a caller
+// buffer. Capacity SJK_STATIC_SCRATCH_BYTES (16 MiB): every GPU that loads this library holds the array until
+// the process exits. The array's host-side name is only a stand-in for its device address, so the address is
+// looked up once per device (cudaGetSymbolAddress, with that device current) on the first call there and
+// cached; that first call should therefore come before any stream capture. Shapes whose scratch bound
+// (sjk_attend_scratch_bytes) exceeds the capacity are rejected with SJK_ERR_SCRATCH_LIMIT. Every call
+// writes all the partials it later reads, so nothing needs clearing between calls; calls that overlap on
+// the GPU (other streams, other host threads) share the array and race.
+#define SJK_STATIC_SCRATCH_BYTES ((size_t) 16 << 20)
+static __device__ __align__(256) unsigned char sjk_static_scratch[SJK_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_mu;
+void * g_static_ptr[256];                    // device address of sjk_static_scratch, per device ordinal
+}
+
+extern "C" int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                                 const float * q, float scale, float * out, sjk_stream st) {
+    if (!v || n_q <= 0 || n_head <= 0) return SJKVARN_ERR_ARG;
+    const size_t need = sjk_attend_scratch_bytes(v, N, n_q, n_head);
+    if (need > SJK_STATIC_SCRATCH_BYTES) return SJK_ERR_SCRATCH_LIMIT;
+    int dev = 0;
+    if (sjk_check(cudaGetDevice(&dev))) return SJK_ERR_DEVICE;
+    if (dev < 0 || dev >= 256) return SJK_ERR_UNSUPPORTED;
+    void * ptr = NULL;
+    {
+        std::lock_guard<std::mutex> lk(g_static_mu);
+        ptr = g_static_ptr[dev];
+        if (!ptr) {
+            if (sjk_check(cudaGetSymbolAddress(&ptr, sjk_static_scratch))) return SJK_ERR_DEVICE;
+            g_static_ptr[dev] = ptr;
+        }
+    }
+    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, ptr, SJK_STATIC_SCRATCH_BYTES, st);
 }

@@ -249,6 +249,7 @@ extern "C" const char * sj_kvarn_strerror(int code) {
         case SJKVARN_ERR_N_LAYERS: return "config mismatch: number of layers";
         case SJK_ERR_DEVICE: return "CUDA error (see sjk_last_cuda_error)";
         case SJK_ERR_UNSUPPORTED: return "shape not implemented by the B200 kernels";
+        case SJK_ERR_SCRATCH_LIMIT: return "shape needs more scratch than the fixed no-allocation buffer holds (16 MiB)";
         default: return "unknown SJ-KVaRN status code";
     }
 }
