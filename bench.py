@@ -514,7 +514,7 @@ def main():
     abytes = attn_bytes_per_call(res["B"], c["N"])
     peak, peak_kind = hbm_peak()
     achieved = abytes / (per_call_ms * 1e-3) / 1e9
-    traffic = profile_traffic("attend_config1.md")
+    traffic = profile_traffic("attend_config1_launches.md")
     seal_mtoks = 4096 / (seal["ms"] * 1e-3) / 1e6
     seal_bytes = seal["records"] * (128 * 392 + 35072)
     store_bytes = 8320 * (2 * 4 * 256 * 4) + 128 * 4 * 1024 + 8192 * 4 * 392
@@ -532,7 +532,7 @@ def main():
         "clocks": res["clocks"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind, "frac_of_8tbs": achieved / 8000.0,
-                     "kernel": "attend_split_kernel (+ merge) per layer call",
+                     "kernel": "one sjk_attend call: attend_body_tc_kernel + attend_dense_tc_kernel + attend_merge_kernel",
                      "algorithmic_bytes_per_launch": abytes},
         "seal": {"metric": "seal Mtok/s (4096 commit)", "value": seal_mtoks, "unit": "Mtok/s", "ms": seal["ms"],
                  "workload": "config 0: 1 layer, 4 KV heads, D=256, 4/4, 32 groups x 4 heads from an 8,320-row tq6_0 ring",

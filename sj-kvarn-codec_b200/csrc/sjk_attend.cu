@@ -227,35 +227,52 @@ __global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
     }
 }
 
-// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m); one CTA per (query row, query head),
-// the split weights are computed once into shared memory
-__global__ void attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out) {
+// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m). Grid (query row x head, channel tiles of
+// 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
+__global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out) {
     extern __shared__ float wts[];                     // [splits]
-    __shared__ float s_m, s_inv;
-    const int row = blockIdx.x;
-    if (threadIdx.x < 32) {
-        float m = -__int_as_float(0x7F800000);
-        for (int i = threadIdx.x; i < splits; i += 32) m = fmaxf(m, part[((size_t) i * n_rows + row) * (D + 2)]);
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-        float den = 0.0f;
-        for (int i = threadIdx.x; i < splits; i += 32) {
-            const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
-            const float w = pp[0] == -__int_as_float(0x7F800000) ? 0.0f : expf(pp[0] - m);
-            wts[i] = w;
-            den += pp[1] * w;
-        }
-        for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
-        if (threadIdx.x == 0) { s_m = m; s_inv = den == 0.0f ? 0.0f : 1.0f / den; }
+    __shared__ float s_inv;
+    __shared__ float s_red[8];
+    const int row = blockIdx.x, d0 = blockIdx.y * 64;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float m = -__int_as_float(0x7F800000);
+    for (int i = tid; i < splits; i += blockDim.x) m = fmaxf(m, part[((size_t) i * n_rows + row) * (D + 2)]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    if (lane == 0) s_red[warp] = m;
+    __syncthreads();
+    m = s_red[0];
+    for (int w = 1; w < (int) (blockDim.x >> 5); ++w) m = fmaxf(m, s_red[w]);
+    __syncthreads();
+    float den = 0.0f;
+    for (int i = tid; i < splits; i += blockDim.x) {
+        const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
+        const float w = pp[0] == -__int_as_float(0x7F800000) ? 0.0f : expf(pp[0] - m);
+        wts[i] = w;
+        den += pp[1] * w;
+    }
+    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+    if (lane == 0) s_red[warp] = den;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int) (blockDim.x >> 5); ++w) t += s_red[w];
+        s_inv = t == 0.0f ? 0.0f : 1.0f / t;
     }
     __syncthreads();
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float o = 0.0f;
-        for (int i = 0; i < splits; ++i) {
+    // 4 groups of 64 threads walk the splits in strides of 4; partial sums meet in shared memory
+    const int dl = tid & 63, grp4 = tid >> 6;
+    float o = 0.0f;
+    if (d0 + dl < D)
+        for (int i = grp4; i < splits; i += 4) {
             const float w = wts[i];
-            if (w != 0.0f) o += part[((size_t) i * n_rows + row) * (D + 2) + 2 + d] * w;
+            if (w != 0.0f) o += part[((size_t) i * n_rows + row) * (D + 2) + 2 + d0 + dl] * w;
         }
-        out[(size_t) row * D + d] = o * s_inv;
-    }
+    __syncthreads();
+    float * acc = wts + splits;                        // [4][64]
+    acc[grp4 * 64 + dl] = o;
+    __syncthreads();
+    if (tid < 64 && d0 + tid < D)
+        out[(size_t) row * D + d0 + tid] = ((acc[tid] + acc[64 + tid]) + (acc[128 + tid] + acc[192 + tid])) * s_inv;
 }
 
 struct Plan { int splits, chunks_per_split, n_chunks; uint32_t n_sink, n_body; };
@@ -267,16 +284,18 @@ int split_target(int n_kv) {
     return t < 1 ? 1 : t;
 }
 
-Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip) {
+// chunks left to the CUDA-core kernel: the body after the first body_skip records, plus the sink and the
+// staging ring unless the dense tensor-core kernel takes them (no_staged)
+Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip, bool no_staged) {
     Plan pl;
     const uint32_t S = v->S;
     const uint32_t s_end = S < N ? S : N;
-    pl.n_sink = (s_end + 127u) / 128u;
+    pl.n_sink = no_staged ? 0u : (s_end + 127u) / 128u;
     const uint32_t b_end = B < N ? B : N;
     pl.n_body = b_end > S ? (b_end - S + 127u) / 128u : 0u;
     pl.n_body = pl.n_body > body_skip ? pl.n_body - body_skip : 0u;
     const uint32_t t0 = B > S ? B : S;
-    const uint32_t n_tail = N > t0 ? (N - t0 + 127u) / 128u : 0u;
+    const uint32_t n_tail = (N > t0 && !no_staged) ? (N - t0 + 127u) / 128u : 0u;
     pl.n_chunks = (int) (pl.n_sink + pl.n_body + n_tail);
     const int target = split_target(n_kv);
     pl.chunks_per_split = (pl.n_chunks + target - 1) / target;
@@ -294,8 +313,8 @@ size_t split_smem() {
 
 size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv) {
     if (!v || n_q <= 0 || n_head <= 0) return 0;
-    // CUDA-core splits plus tensor-core splits, each bounded by the per-call target
-    return (size_t) 2 * split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    // CUDA-core, tensor-core body and tensor-core staged-row splits, each bounded by the per-call target
+    return (size_t) 3 * split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
 }
 
 extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head) {
@@ -317,9 +336,19 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     const uint32_t n_tc = (sjk_tc_body_supported(v, n_q, grp) && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
     int rps = 1;
     const int splits_tc = sjk_tc_body_splits(n_tc, n_kv, &rps);
-    const Plan pl = make_plan(v, B, N, n_kv, n_tc);
+    // the sink and the staging ring go to the dense tensor-core kernel when it supports the row formats
+    const bool dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
+    uint32_t n_sink_d = 0, n_dense = 0;
+    if (dense) {
+        const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
+        n_sink_d = (s_end + 127u) / 128u;
+        n_dense = n_sink_d + (N > t0 ? (N - t0 + 127u) / 128u : 0u);
+    }
+    int cps_d = 1;
+    const int splits_d = dense ? sjk_tc_dense_splits(n_dense, n_kv, &cps_d) : 0;
+    const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense);
     const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
-    const int splits = splits_tc + splits_v1;
+    const int splits = splits_tc + splits_d + splits_v1;
     const size_t need = (size_t) splits * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
     if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
@@ -328,9 +357,14 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
                                           splits_tc, rps, st);
         if (rc) return rc;
     }
+    if (splits_d) {
+        const int rc = sjk_tc_dense_launch(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch,
+                                           splits_tc, splits_d, n_sink_d, n_dense, cps_d, st);
+        if (rc) return rc;
+    }
     AttnParams p;
     p.v = *v; p.kv0 = kv_head0; p.B = B; p.N = N; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = grp;
-    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch; p.split0 = splits_tc;
+    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch; p.split0 = splits_tc + splits_d;
     p.chunks_per_split = pl.chunks_per_split; p.n_chunks = pl.n_chunks; p.n_sink_chunks = pl.n_sink; p.n_body_chunks = pl.n_body;
     p.body_skip = n_tc;
     if (splits_v1) {
@@ -354,7 +388,8 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
         if (sjk_check(e)) return SJK_ERR_DEVICE;
         if (sjk_check_launch()) return SJK_ERR_DEVICE;
     }
-    attend_merge_kernel<<<n_q * n_head, 256, (size_t) splits * sizeof(float), st>>>(p.part, splits, n_q * n_head, v->lay.D, out);
+    attend_merge_kernel<<<dim3((unsigned) (n_q * n_head), (unsigned) ((v->lay.D + 63) / 64)), 256,
+                          (size_t) (splits + 256) * sizeof(float), st>>>(p.part, splits, n_q * n_head, v->lay.D, out);
     return sjk_check_launch();
 }
 

@@ -25,6 +25,8 @@
 
 namespace {
 
+using namespace tc::num;
+
 constexpr int NT = 256;
 constexpr int NR = 16;                  // MMA N: query rows per KV head, padded
 constexpr int D = 256;
@@ -34,10 +36,6 @@ constexpr uint32_t COL_AK = 0;          // A for K: 128 lanes x 256 s8 = 64 colu
 constexpr uint32_t COL_O = 0;           // O^T: 2 tiles x 3 digits x 16 columns, written after A_K is dead
 constexpr uint32_t COL_AV = 96;         // A for V: 2 tiles x 128 lanes x 128 s8 = 2 x 32 columns
 constexpr uint32_t COL_S = 160;         // S^T digits: 3 x 16 columns
-constexpr float MAGIC = 12582912.0f;    // 1.5 * 2^23
-constexpr uint32_t MAGIC_BITS = 0x4B400000u;
-constexpr float LOG2E = 1.4426950408889634f;
-constexpr float LN2 = 0.6931471805599453f;
 
 struct TcParams {
     sj_kvarn_layout lay;
@@ -74,60 +72,6 @@ enum { RED_C = 0, RED_MAX = 128, RED_L = 256, RED_Z = 384 };
 // element (row n, k) of a K-major, no-swizzle s8 B operand with 16 rows: 8-row x 16-byte core matrices,
 // 256 bytes per 16-element K chunk (an MMA's 32-element K step is 512 bytes: LBO 256, SBO 128)
 __device__ __forceinline__ uint32_t b_off(int n, int k) { return (uint32_t) ((k >> 4) * 256 + n * 16 + (k & 15)); }
-
-__device__ __forceinline__ int pow2_exp(float x) { return (int) ((__float_as_uint(x) >> 23) & 0xFF) - 126; }  // x < 2^e
-__device__ __forceinline__ float pow2f(int e) {
-    e = e < -126 ? -126 : (e > 127 ? 127 : e);
-    return __uint_as_float((uint32_t) (e + 127) << 23);
-}
-// exact fp16 -> fp32 for every finite half (scales of sealed records are finite)
-__device__ __forceinline__ float h2f(uint16_t h) {
-    const float mag = __uint_as_float(((uint32_t) h & 0x7FFFu) << 13) * 5.192296858534828e33f;   // x 2^112
-    return __uint_as_float(__float_as_uint(mag) | (((uint32_t) h & 0x8000u) << 16));
-}
-__device__ __forceinline__ float h2f_at(const uint8_t * p) { return h2f(*reinterpret_cast<const uint16_t *>(p)); }
-// float -> nearest integer and back (|v| < 2^22) without the conversion pipe
-__device__ __forceinline__ int f2i(float v) { return (int) (__float_as_uint(v + MAGIC) - MAGIC_BITS); }
-__device__ __forceinline__ float i2f(uint32_t x) { return __uint_as_float(x + MAGIC_BITS) - MAGIC; }
-__device__ __forceinline__ int sext8(int x) { return (x << 24) >> 24; }
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-__device__ __forceinline__ float ex2(float x) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
-// Reduce 8 per-thread values across the 32 lanes; afterwards lanes 4r..4r+3 hold row r.
-template <bool MAX>
-__device__ __forceinline__ float warp_rows8(const float (&v)[8], int lane) {
-    float a[4], b[2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const bool up = lane & 16;
-        const float send = up ? v[i] : v[i + 4], keep = up ? v[i + 4] : v[i];
-        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
-        a[i] = MAX ? fmaxf(keep, r) : keep + r;
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const bool up = lane & 8;
-        const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
-        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 8);
-        b[i] = MAX ? fmaxf(keep, r) : keep + r;
-    }
-    const bool up = lane & 4;
-    const float send = up ? b[0] : b[1], keep = up ? b[1] : b[0];
-    float r = __shfl_xor_sync(0xFFFFFFFFu, send, 4);
-    float c = MAX ? fmaxf(keep, r) : keep + r;
-    r = __shfl_xor_sync(0xFFFFFFFFu, c, 2);
-    c = MAX ? fmaxf(c, r) : c + r;
-    r = __shfl_xor_sync(0xFFFFFFFFu, c, 1);
-    return MAX ? fmaxf(c, r) : c + r;
-}
 
 // 16 consecutive K elements of one 16x16 tile from its 4 fragment-order words (the thread's row is in the
 // nibbles selected by `shift`): word j holds elements {2j, 2j+8, 2j+1, 2j+9} -> 4 columns of 4 bytes
@@ -202,6 +146,13 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
     const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
     const uint32_t idesc = tc::idesc_s8(128, NR);
     const float sl2 = p.scale * LOG2E;
+    // causal bound of this thread's 8 score rows (8 half + i); rows past p.rows are padding (never valid)
+    uint32_t qlim[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = 8 * half + i;
+        qlim[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;     // positions < qlim are visible
+    }
 
     float acc[NR];                                    // running output of channel 128 half + tl, all rows
 #pragma unroll
@@ -340,9 +291,8 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
             for (int i = 0; i < 8; ++i) {
                 const int r = 8 * half + i;
                 const float S = fmaf(65536.0f, i2f(a2[i]), fmaf(256.0f, i2f(a1[i]), i2f(a0[i])));
-                const uint32_t qpos = p.qpos0 + (uint32_t) (r / p.grp);
                 const float dot = kt * fmaf(S, row[ROW_KINV + r], row[ROW_C + r]);
-                s2[i] = (r < p.rows && pos <= qpos) ? dot * sl2 : -INFINITY;
+                s2[i] = pos < qlim[i] ? dot * sl2 : -INFINITY;
             }
             const float mw = warp_rows8<true>(s2, lane);
             if ((lane & 3) == 0) red[RED_MAX + half * 32 + quarter * 8 + (lane >> 2)] = mw;

@@ -23,3 +23,10 @@ int sjk_tc_body_splits(uint32_t n_rec, int n_kv, int * recs_per_split);
 int sjk_tc_body_launch(const sjk_view * v, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
                        const float * q, float scale, float * part, int split0, int splits, int recs_per_split,
                        sjk_stream st);
+
+// tensor-core attention over the staged rows: the sink [0, S) and the staging ring [B, N) (sjk_attend_dense.cu)
+int sjk_tc_dense_supported(const sjk_view * v, int n_q, int grp);
+int sjk_tc_dense_splits(uint32_t n_chunks, int n_kv, int * chunks_per_split);
+int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
+                        const float * q, float scale, float * part, int split0, int splits, uint32_t n_sink_chunks,
+                        uint32_t n_chunks, int chunks_per_split, sjk_stream st);

@@ -144,4 +144,76 @@ __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t 
                  : "memory");
 }
 
+// asynchronous global -> shared copies of 4 / 16 bytes; src_bytes = 0 writes zeros (src is not read)
+__device__ __forceinline__ void cp_async4(void * dst, const void * src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void * dst, const void * src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// ---- numeric helpers shared by the tensor-core kernels ------------------------------------------------
+namespace num {
+constexpr float MAGIC = 12582912.0f;    // 1.5 * 2^23: v + MAGIC holds round(v) in the low mantissa bits
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+__device__ __forceinline__ int pow2_exp(float x) { return (int) ((__float_as_uint(x) >> 23) & 0xFF) - 126; }  // x < 2^e
+__device__ __forceinline__ float pow2f(int e) {
+    e = e < -126 ? -126 : (e > 127 ? 127 : e);
+    return __uint_as_float((uint32_t) (e + 127) << 23);
+}
+// exact fp16 -> fp32 for every finite half (scales of sealed records are finite)
+__device__ __forceinline__ float h2f(uint16_t h) {
+    const float mag = __uint_as_float(((uint32_t) h & 0x7FFFu) << 13) * 5.192296858534828e33f;   // x 2^112
+    return __uint_as_float(__float_as_uint(mag) | (((uint32_t) h & 0x8000u) << 16));
+}
+__device__ __forceinline__ float h2f_at(const uint8_t * p) { return h2f(*reinterpret_cast<const uint16_t *>(p)); }
+// float -> nearest integer and back (|v| < 2^22) without the conversion pipe
+__device__ __forceinline__ int f2i(float v) { return (int) (__float_as_uint(v + MAGIC) - MAGIC_BITS); }
+__device__ __forceinline__ float i2f(uint32_t x) { return __uint_as_float(x + MAGIC_BITS) - MAGIC; }
+__device__ __forceinline__ int sext8(int x) { return (x << 24) >> 24; }
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Reduce 8 per-thread values across the 32 lanes; afterwards lanes 4r..4r+3 hold row r.
+template <bool MAX>
+__device__ __forceinline__ float warp_rows8(const float (&v)[8], int lane) {
+    float a[4], b[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? v[i] : v[i + 4], keep = up ? v[i + 4] : v[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+        a[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+        b[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+    const bool up = lane & 4;
+    const float send = up ? b[0] : b[1], keep = up ? b[1] : b[0];
+    float r = __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+    float c = MAX ? fmaxf(keep, r) : keep + r;
+    r = __shfl_xor_sync(0xFFFFFFFFu, c, 2);
+    c = MAX ? fmaxf(c, r) : c + r;
+    r = __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+    return MAX ? fmaxf(c, r) : c + r;
+}
+
+}  // namespace num
+
 }  // namespace tc

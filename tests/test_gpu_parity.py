@@ -179,6 +179,33 @@ def test_cache_build_bit_exact(L, oracle_lib, bk, bv, body, staging, sink_f16):
     oc.close()
 
 
+@pytest.mark.parametrize("D,staging,sink_f16", [(256, 0, True), (256, 0, False), (256, 1, True), (256, 1, False),
+                                                 (128, 0, True)])
+def test_attend_regions_and_shapes(L, oracle_lib, D, staging, sink_f16):
+    """Attention over every staged-row format (tq6_0 / fp16 ring, fp16 / inherited sink) and query shape the
+    kernels take (up to 16 rows per KV head), with N inside the sink, inside the body, at B and past B
+    in a wrapped ring, the query rows causal inside the last chunk."""
+    H = 2
+    layer, oc, B, cfg = _build_pair(L, oracle_lib, D, H, 4, 4, 0, staging, sink_f16, 1500, 256, 512, 64, seed=11)
+    assert B >= 128 + 5 * 128 and layer.cap < 1500 - 128
+    scale = np.float32(1.0 / np.sqrt(D))
+    cases = [(1500, 1, 2), (1500, 1, 8), (1500, 4, 8), (1500, 16, 2), (B + 70, 4, 4), (B, 2, 4), (B - 50, 3, 2),
+             (100, 2, 4), (128 + 1, 1, 2)]
+    for N, n_q, n_head in cases:
+        qpos0 = N - n_q - (3 if N > 200 else 0)
+        q = synth.queries(N, 1, n_q, n_head, D)[0]
+        qr = oracle_lib.fwht_rows(q.reshape(-1, D).copy()).reshape(n_q, n_head, D)
+        dq, dout = gu.dev(qr), gu.dev_zeros(n_q * n_head * D * 4)
+        sjk.check(L.sjk_layer_attend(C.byref(layer), B, N, qpos0, n_q, n_head, gu.ptr(dq), scale, gu.ptr(dout), None))
+        out = gu.host(dout, np.float32, (n_q, n_head, D))
+        ref = oc.attend(B, N, qpos0, qr, scale)
+        err = gu.rel_err_rows(out, ref)
+        assert err <= ATTN_TOL_TIGHT, (N, n_q, n_head, err)
+    assert L.sjk_device_status() == 0
+    L.sj_kvarn_layer_free(C.byref(layer))
+    oc.close()
+
+
 def _expected_states():
     exp = {}
     for ln in open(os.path.join(GOLDEN, "expected_state.txt")):
