@@ -57,9 +57,9 @@ struct TcParams {
 constexpr uint32_t REC_MAX = 35072;
 constexpr uint32_t OFF_REC0 = 0;
 constexpr uint32_t OFF_REC1 = REC_MAX;
-constexpr uint32_t OFF_BK = 2 * REC_MAX;            // 3 digits x [16 rows x 256] s8
-constexpr uint32_t OFF_BV = OFF_BK + 3 * 4096;      // 3 digits x [16 rows x 128] s8
-constexpr uint32_t OFF_RED = OFF_BV + 3 * 2048;     // 4 reduction areas x 128 floats
+constexpr uint32_t OFF_BK = 2 * REC_MAX;            // B_K: 16 K chunks (256 channels) x 48 rows
+constexpr uint32_t OFF_BV = OFF_BK + 16 * 784;      // B_V: 8 K chunks (128 tokens) x 48 rows
+constexpr uint32_t OFF_RED = OFF_BV + 8 * 784;      // 4 reduction areas x 128 floats
 constexpr uint32_t OFF_ROW = OFF_RED + 4 * 128 * 4;
 constexpr uint32_t OFF_BAR = OFF_ROW + 12 * 16 * 4;
 constexpr uint32_t OFF_TMEM = OFF_BAR + 32;
@@ -69,9 +69,13 @@ enum { ROW_C = 0, ROW_KINV = 16, ROW_M2 = 32, ROW_MNEW = 48, ROW_ALPHA = 64, ROW
        ROW_MAXV = 128, ROW_VSCL = 144, ROW_VINV = 160 };
 enum { RED_C = 0, RED_MAX = 128, RED_L = 256, RED_Z = 384 };
 
-// element (row n, k) of a K-major, no-swizzle s8 B operand with 16 rows: 8-row x 16-byte core matrices,
-// 256 bytes per 16-element K chunk (an MMA's 32-element K step is 512 bytes: LBO 256, SBO 128)
-__device__ __forceinline__ uint32_t b_off(int n, int k) { return (uint32_t) ((k >> 4) * 256 + n * 16 + (k & 15)); }
+// element (n, k) of a K-major, no-swizzle s8 B operand with N = 48 rows, n = 16 digit + query row: 8-row x
+// 16-byte core matrices (SBO 128), one 16-element K chunk every BCH = 784 bytes (768 + 16: consecutive chunks
+// start 4 banks apart, so the builders' stores are conflict-free); an MMA's 32-element K step spans two
+// chunks (LBO = BCH). The three digit planes side by side in N let one MMA produce all three digit sums.
+constexpr int NB = 3 * NR;
+constexpr uint32_t BCH = 784;
+__device__ __forceinline__ uint32_t b_off(int n, int k) { return (uint32_t) (k >> 4) * BCH + (uint32_t) (n * 16 + (k & 15)); }
 
 // 16 consecutive K elements of one 16x16 tile from its 4 fragment-order words (the thread's row is in the
 // nibbles selected by `shift`): word j holds elements {2j, 2j+8, 2j+1, 2j+9} -> 4 columns of 4 bytes
@@ -90,7 +94,7 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
     const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;   // tl: this thread's TMEM lane
     const int hl = blockIdx.y, h = p.kv0 + hl, split = blockIdx.x;
     const sj_kvarn_layout & l = p.lay;
-    uint8_t * rec_buf[2] = {sm + OFF_REC0, sm + OFF_REC1};
+    auto rec_buf = [&](uint32_t b) -> uint8_t * { return sm + OFF_REC0 + b * REC_MAX; };
     uint8_t * bk = sm + OFF_BK;
     uint8_t * bv = sm + OFF_BV;
     float * red = reinterpret_cast<float *>(sm + OFF_RED);
@@ -144,7 +148,7 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
     for (int i = 0; i < 4; ++i) qmax[i] = fmaxf(red[RED_C + (2 * brg) * 4 + i], red[RED_C + (2 * brg + 1) * 4 + i]);
     const uint32_t tmem = *tmem_slot;
     const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
-    const uint32_t idesc = tc::idesc_s8(128, NR);
+    const uint32_t idesc = tc::idesc_s8(128, NB);
     const float sl2 = p.scale * LOG2E;
     // causal bound of this thread's 8 score rows (8 half + i); rows past p.rows are padding (never valid)
     uint32_t qlim[8];
@@ -168,20 +172,20 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
     };
     __syncthreads();                                  // red[] reused below
     if (r_begin < r_end) {
-        if (tid == 0) { tc::mbar_expect_tx(&bars[0], l.bytes); tc::bulk_g2s(rec_buf[0], rec_ptr(r_begin), l.bytes, &bars[0]); }
+        if (tid == 0) { tc::mbar_expect_tx(&bars[0], l.bytes); tc::bulk_g2s(rec_buf(0), rec_ptr(r_begin), l.bytes, &bars[0]); }
         load_pending = 0;
     }
 
     for (uint32_t g = r_begin; g < r_end; ++g) {
         const uint32_t it = g - r_begin, buf = it & 1u;
-        const uint8_t * rec = rec_buf[buf];
+        const uint8_t * rec = rec_buf(buf);
         ok = __syncthreads_and(tc::mbar_wait(&bars[buf], (it >> 1) & 1u));
         if (!ok) break;
         load_pending = -1;
         if (g + 1 < r_end) {
             if (tid == 0) {
                 tc::mbar_expect_tx(&bars[buf ^ 1u], l.bytes);
-                tc::bulk_g2s(rec_buf[buf ^ 1u], rec_ptr(g + 1), l.bytes, &bars[buf ^ 1u]);
+                tc::bulk_g2s(rec_buf(buf ^ 1u), rec_ptr(g + 1), l.bytes, &bars[buf ^ 1u]);
             }
             load_pending = (int) it + 1;
         }
@@ -217,7 +221,7 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
         __syncthreads();                                                          // S1
         // ---- B: B_K = three s8 digits of round(Q' 2^e), zero-point partials ----
         {
-            float maxk = 0.0f;
+            float maxk = 0.0f, cz[4];
 #pragma unroll
             for (int w = 0; w < 8; ++w) maxk = fmaxf(maxk, row[ROW_MAXK + w]);
 #pragma unroll
@@ -227,23 +231,18 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
                 const int e = (bound > 0.0f && bound < INFINITY) ? 21 - pow2_exp(bound) : 0;
                 const float sc = pow2f(e);
                 if (bg == 0) row[ROW_KINV + r] = pow2f(-e);
-                uint32_t dg0 = 0, dg1 = 0, dg2 = 0;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int x = f2i((qv[i][j] * ks[j]) * sc);
-                    const int d0 = sext8(x), x1 = (x - d0) >> 8, d1 = sext8(x1), d2 = (x1 - d1) >> 8;
-                    dg0 |= ((uint32_t) d0 & 0xFFu) << (8 * j);
-                    dg1 |= ((uint32_t) d1 & 0xFFu) << (8 * j);
-                    dg2 |= ((uint32_t) d2 & 0xFFu) << (8 * j);
-                }
+                // digits of the 4 channels (bytes 0..2 of z_j) transposed into one word per digit plane
+                const uint32_t z0 = digits3(qv[i][0] * ks[0], sc), z1 = digits3(qv[i][1] * ks[1], sc);
+                const uint32_t z2 = digits3(qv[i][2] * ks[2], sc), z3 = digits3(qv[i][3] * ks[3], sc);
+                const uint32_t a = prmt(z0, z1, 0x5140u), b = prmt(z2, z3, 0x5140u);   // [z0.0 z1.0 z0.1 z1.1]
                 const uint32_t off = b_off(r, 4 * bg);
-                *reinterpret_cast<uint32_t *>(bk + off) = dg0;
-                *reinterpret_cast<uint32_t *>(bk + 4096 + off) = dg1;
-                *reinterpret_cast<uint32_t *>(bk + 8192 + off) = dg2;
-                float c = (qv[i][0] * kz[0] + qv[i][1] * kz[1]) + (qv[i][2] * kz[2] + qv[i][3] * kz[3]);
-                for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
-                if (lane == 0) red[RED_C + warp * 4 + i] = c;
+                *reinterpret_cast<uint32_t *>(bk + off) = prmt(a, b, 0x5410u);
+                *reinterpret_cast<uint32_t *>(bk + off + 256) = prmt(a, b, 0x7632u);
+                *reinterpret_cast<uint32_t *>(bk + off + 512) = prmt(prmt(z0, z1, 0x0062u), prmt(z2, z3, 0x0062u), 0x5410u);
+                cz[i] = (qv[i][0] * kz[0] + qv[i][1] * kz[1]) + (qv[i][2] * kz[2] + qv[i][3] * kz[3]);
             }
+            const float c = warp_sum_rows4(cz[0], cz[1], cz[2], cz[3], lane);
+            if ((lane & 7) == 0) red[RED_C + warp * 4 + (lane >> 3)] = c;
         }
         tc::wait_st();
         tc::fence_proxy_async();
@@ -252,10 +251,8 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
         tc::fence_after_sync();
         if (tid == 0) {
 #pragma unroll 1
-            for (int dg = 0; dg < 3; ++dg)
-                for (int k = 0; k < D / 32; ++k)
-                    tc::mma_ts_i8(tmem + COL_S + 16 * dg, tmem + COL_AK + 8 * k,
-                                  tc::smem_desc(bk + 4096 * dg + 512 * k, 256, 128), idesc, k ? 1u : 0u);
+            for (int k = 0; k < D / 32; ++k)
+                tc::mma_ts_i8(tmem + COL_S, tmem + COL_AK + 8 * k, tc::smem_desc(bk + 2 * BCH * k, BCH, 128), idesc, k ? 1u : 0u);
             tc::mma_commit(&bars[2]);
         }
         mma_pending = true;
@@ -326,12 +323,11 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
                 const float pw = mnew == -INFINITY ? 0.0f : ex2(s2[i] - mnew);
                 ls[i] = pw;
                 zs[i] = pw * vz;
-                const int x = f2i((pw * vsc) * row[ROW_VSCL + r]);
-                const int d0 = sext8(x), x1 = (x - d0) >> 8, d1 = sext8(x1), d2 = (x1 - d1) >> 8;
+                const uint32_t z = digits3(pw * vsc, row[ROW_VSCL + r]);
                 const uint32_t off = b_off(r, tl);
-                bv[off] = (uint8_t) d0;
-                bv[2048 + off] = (uint8_t) d1;
-                bv[4096 + off] = (uint8_t) d2;
+                bv[off] = (uint8_t) z;
+                bv[off + 256] = (uint8_t) (z >> 8);
+                bv[off + 512] = (uint8_t) (z >> 16);
             }
             const float lw = warp_rows8<false>(ls, lane);
             const float zw = warp_rows8<false>(zs, lane);
@@ -347,10 +343,9 @@ __global__ void __launch_bounds__(NT, 2) attend_body_tc_kernel(TcParams p) {
         if (tid == 0) {
 #pragma unroll 1
             for (int tile = 0; tile < 2; ++tile)
-                for (int dg = 0; dg < 3; ++dg)
-                    for (int k = 0; k < G / 32; ++k)
-                        tc::mma_ts_i8(tmem + COL_O + 48 * tile + 16 * dg, tmem + COL_AV + 32 * tile + 8 * k,
-                                      tc::smem_desc(bv + 2048 * dg + 512 * k, 256, 128), idesc, k ? 1u : 0u);
+                for (int k = 0; k < G / 32; ++k)
+                    tc::mma_ts_i8(tmem + COL_O + 48 * tile, tmem + COL_AV + 32 * tile + 8 * k,
+                                  tc::smem_desc(bv + 2 * BCH * k, BCH, 128), idesc, k ? 1u : 0u);
             tc::mma_commit(&bars[2]);
         }
         mma_pending = true;

@@ -214,6 +214,25 @@ __device__ __forceinline__ float warp_rows8(const float (&v)[8], int lane) {
     return MAX ? fmaxf(c, r) : c + r;
 }
 
+// Sum 4 per-thread values (rows 0..3) across the 32 lanes; afterwards lanes 8r..8r+7 hold row r.
+__device__ __forceinline__ float warp_sum_rows4(float v0, float v1, float v2, float v3, int lane) {
+    const bool u16 = lane & 16, u8 = lane & 8;
+    const float a0 = (u16 ? v2 : v0) + __shfl_xor_sync(0xFFFFFFFFu, u16 ? v0 : v2, 16);
+    const float a1 = (u16 ? v3 : v1) + __shfl_xor_sync(0xFFFFFFFFu, u16 ? v1 : v3, 16);
+    float c = (u8 ? a1 : a0) + __shfl_xor_sync(0xFFFFFFFFu, u8 ? a0 : a1, 8);
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, 4);
+    c += __shfl_xor_sync(0xFFFFFFFFu, c, 2);
+    return c + __shfl_xor_sync(0xFFFFFFFFu, c, 1);
+}
+
+// Balanced base-256 digits of round(v * sc), |v * sc| < 2^22: byte i (i = 0, 1, 2) of the result is the signed
+// digit d_i in [-128, 127] with round(v * sc) = d0 + 256 d1 + 65536 d2. fmaf(v, sc, MAGIC) holds the rounded
+// integer x in its low mantissa bits (bits = MAGIC_BITS + x); adding 128 to every digit position maps the digits
+// to the bytes of x + 0x808080 (each in [0, 255]), and flipping bit 7 of each byte maps them back to signed.
+__device__ __forceinline__ uint32_t digits3(float v, float sc) {
+    return (__float_as_uint(fmaf(v, sc, MAGIC)) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u;
+}
+
 }  // namespace num
 
 }  // namespace tc
