@@ -260,7 +260,7 @@ def run_gpu_arm(args, torch, dist, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
     res = dict(ms=ms, ms_e2e=ms_e2e, B=B, build_s=build_s, clocks=clk.summary(), h2d=q.numel() * 4, d2h=out.numel() * 4,
-               launches_per_step=2 * c["LAYERS"], sealed_records=m.sealed_records)
+               launches_per_step=3 * c["LAYERS"], sealed_records=m.sealed_records)
     m.free()
     return res
 

@@ -393,6 +393,14 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     return sjk_check_launch();
 }
 
+// status words of every kernel with bounded waits: 1 if any wait ran out since the last call
+extern "C" int sjk_device_status(void) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take();
+    if (a < 0 || b < 0) return -1;
+    return a | b;
+}
+
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
                           float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
     if (!v) return SJKVARN_ERR_ARG;

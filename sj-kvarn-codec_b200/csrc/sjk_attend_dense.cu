@@ -437,3 +437,5 @@ int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpo
     attend_dense_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
     return sjk_check_launch();
 }
+
+SJK_STATUS_READER(sjk_tc_dense_status_take)

@@ -30,3 +30,7 @@ int sjk_tc_dense_splits(uint32_t n_chunks, int n_kv, int * chunks_per_split);
 int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
                         const float * q, float scale, float * part, int split0, int splits, uint32_t n_sink_chunks,
                         uint32_t n_chunks, int chunks_per_split, sjk_stream st);
+
+// device status words of the tensor-core translation units (read and cleared; -1 on a CUDA error)
+int sjk_tc_body_status_take(void);
+int sjk_tc_dense_status_take(void);

@@ -12,6 +12,15 @@
 // device status word of the including translation unit (read and cleared by sjk_device_status())
 static __device__ int sjk_dev_status;
 
+// defines `int name(void)` returning and clearing this translation unit's device status word (-1: CUDA error)
+#define SJK_STATUS_READER(name)                                                          \
+    int name(void) {                                                                     \
+        int v_ = 0, zero_ = 0;                                                           \
+        if (cudaMemcpyFromSymbol(&v_, sjk_dev_status, sizeof v_) != cudaSuccess) return -1; \
+        if (cudaMemcpyToSymbol(sjk_dev_status, &zero_, sizeof zero_) != cudaSuccess) return -1; \
+        return v_;                                                                       \
+    }
+
 namespace tc {
 
 __device__ __forceinline__ uint32_t smem_addr(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
@@ -137,6 +146,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     atomicExch(&sjk_dev_status, SJK_DEV_TIMEOUT);
     return false;
 }
+// plain arrival (count 1) on an mbarrier, release semantics at CTA scope
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// named barrier over `n` threads (a multiple of 32; every warp arrives whole)
+__device__ __forceinline__ void nbar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// named barrier that also returns the AND of `v` over the `n` participating threads
+__device__ __forceinline__ bool nbar_and(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r)
+                 : "r"((uint32_t) v), "r"(id), "r"(n)
+                 : "memory");
+    return r != 0;
+}
 // 1-D bulk copy global -> own shared memory, completion counted in bytes on `bar` (no multicast)
 __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
@@ -185,6 +209,15 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
+// 8 consecutive floats of shared memory (16-byte aligned) into / from registers
+__device__ __forceinline__ void ld8(const float * p, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void st8(float * p, const float (&v)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
 
 // Reduce 8 per-thread values across the 32 lanes; afterwards lanes 4r..4r+3 hold row r.
 template <bool MAX>
@@ -212,6 +245,39 @@ __device__ __forceinline__ float warp_rows8(const float (&v)[8], int lane) {
     c = MAX ? fmaxf(c, r) : c + r;
     r = __shfl_xor_sync(0xFFFFFFFFu, c, 1);
     return MAX ? fmaxf(c, r) : c + r;
+}
+
+// Reduce 16 per-thread values (rows 0..15) across the 32 lanes; afterwards lanes 2r, 2r+1 hold row r.
+template <bool MAX>
+__device__ __forceinline__ float warp_rows16(const float (&v)[16], int lane) {
+    float a[8], b[4], c[2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? v[i] : v[i + 8], keep = up ? v[i + 8] : v[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 16);
+        a[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? a[i] : a[i + 4], keep = up ? a[i + 4] : a[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 8);
+        b[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 4;
+        const float send = up ? b[i] : b[i + 2], keep = up ? b[i + 2] : b[i];
+        const float r = __shfl_xor_sync(0xFFFFFFFFu, send, 4);
+        c[i] = MAX ? fmaxf(keep, r) : keep + r;
+    }
+    const bool up = lane & 2;
+    const float send = up ? c[0] : c[1], keep = up ? c[1] : c[0];
+    float r = __shfl_xor_sync(0xFFFFFFFFu, send, 2);
+    const float d = MAX ? fmaxf(keep, r) : keep + r;
+    r = __shfl_xor_sync(0xFFFFFFFFu, d, 1);
+    return MAX ? fmaxf(d, r) : d + r;
 }
 
 // Sum 4 per-thread values (rows 0..3) across the 32 lanes; afterwards lanes 8r..8r+7 hold row r.
