@@ -8,11 +8,13 @@
 //   K side, block b   S_b^T[t, r] = sum_{d in b} cent[code_K(t, d)] * q[r, d];   dot = sum_b normK(t, b) S_b
 //   V side, tile b    O_b^T[d, r] = sum_t cent[code_V(t, d)] * P'_b[r, t],       P'_b = p * normV(t, b)
 //
-// The centroids enter as exact fp16 hi + lo halves (a 64-entry table), q and P' as fp16 hi + lo halves
-// (q with an exact power-of-two row rescale), and the products hi*hi + hi*lo + lo*hi accumulate in fp32
-// (the dropped lo*lo term is below 2^-22 relative). fp16 rows (fp16 sink, fp16 staging) enter exactly
-// with lo = 0. Rows of a chunk are staged in shared memory with coalesced loads; softmax is online per
-// chunk; partials go to the same split buffer as the other attention kernels. Waits are bounded.
+// The centroids enter as fp16 hi + lo halves (a 64-entry table), q and P' as fp16 hi + lo halves side by
+// side in the MMA's N dimension (B = [hi | lo], N = 32). Two MMAs per k step, A_hi x [hi | lo] and
+// A_lo x hi, accumulate hi*hi + lo*hi in columns 0..15 and hi*lo in columns 16..31 (the dropped lo*lo
+// term is below 2^-22 relative); the result is the sum of the two column groups. fp16 rows (fp16 sink,
+// fp16 staging) enter exactly with lo = 0 and skip the second MMA. Rows of a chunk are staged in shared
+// memory with asynchronous copies (tq6_0: K and V rows at once); softmax is online per chunk; partials go to
+// the same split buffer as the other attention kernels. Waits are bounded.
 #include <cuda_fp16.h>
 
 #include "sjk_common.cuh"
@@ -25,10 +27,11 @@ using namespace tc::num;
 
 constexpr int NT = 256;
 constexpr int NR = 16;
+constexpr int NB = 2 * NR;              // B operands: hi rows 0..15, lo rows 16..31
 constexpr int D = 256;
 constexpr int CH = 128;
 constexpr uint32_t TM_COLS = 256;
-constexpr uint32_t COL_AH = 0, COL_AL = 64, COL_S = 128, COL_O = 160;   // A hi | A lo | S0 S1 | O0 O1
+constexpr uint32_t COL_AH = 0, COL_AL = 64, COL_S = 128, COL_O = 192;   // A hi | A lo | S0 S1 (2 x 32) | O0 O1
 
 struct DenseParams {
     sjk_view v;
@@ -43,11 +46,19 @@ struct DenseParams {
     int chunks_per_split;
 };
 
+// B operand (K-major, no swizzle, 32 rows): element (n, k) at (k / 8) * HCH + n * 16 + (k % 8) * 2 with an 8-element
+// K chunk every HCH = 528 bytes (512 + 16: consecutive chunks start 4 banks apart, so the builders' stores are
+// conflict-free); one MMA k step (16 elements) is two chunks (LBO = HCH, SBO 128 between 8-row groups)
+constexpr uint32_t HCH = 528;
+__device__ __forceinline__ uint32_t h_off(int n, int k) { return (uint32_t) (k >> 3) * HCH + (uint32_t) (n * 16 + (k & 7) * 2); }
+
 constexpr uint32_t STG_F16 = 528;       // staged fp16 row stride (512 B + 16: 16-byte rows, conflict-free LDS.128)
-constexpr uint32_t STG_TQ6 = 2 * SJKVARN_TQ6_BLOCK_BYTES;      // 196 B = 49 words: conflict-free row walks
-constexpr uint32_t OFF_BQ = 0;                                  // q hi [16][256] fp16, then lo
-constexpr uint32_t OFF_BV = OFF_BQ + 2 * 8192;                  // P' tile0 hi, tile0 lo, tile1 hi, tile1 lo
-constexpr uint32_t OFF_STG = OFF_BV + 4 * 4096;                 // 128 staged rows of one side
+constexpr uint32_t TQ6_ROW = 2 * SJKVARN_TQ6_BLOCK_BYTES;      // 196 B: one K or V row of tq6_0 blocks
+constexpr uint32_t STG_TQ6 = 2 * TQ6_ROW;                       // staged K row + V row of a token (392 B = 49 x 8)
+constexpr uint32_t TILE_B = 16 * HCH;                          // one B operand over 128 k (8 k steps)
+constexpr uint32_t OFF_BQ = 0;                                  // [q hi | q lo] for 256 channels: 2 x TILE_B
+constexpr uint32_t OFF_BV = OFF_BQ + 2 * TILE_B;                // [P' hi | P' lo] per tile: 2 x TILE_B
+constexpr uint32_t OFF_STG = OFF_BV + 2 * TILE_B;               // staged rows: fp16 one side, tq6_0 both sides
 constexpr uint32_t OFF_CENT = OFF_STG + CH * STG_F16;           // u32[64]: fp16 hi | lo << 16 of each centroid
 constexpr uint32_t OFF_RED = OFF_CENT + 64 * 4;                 // [2 quantities][64] floats
 constexpr uint32_t OFF_ROW = OFF_RED + 2 * 64 * 4;              // per-row arrays
@@ -56,14 +67,18 @@ constexpr uint32_t OFF_ROWP = OFF_NRM + 4 * CH * 4;             // global addres
 constexpr uint32_t OFF_BAR = OFF_ROWP + CH * 8;
 constexpr uint32_t OFF_TMEM = OFF_BAR + 16;
 constexpr uint32_t SMEM_TOTAL = OFF_TMEM + 16;
-enum { ROW_QINV = 0, ROW_M2 = 16, ROW_MNEW = 32, ROW_ALPHA = 48, ROW_L = 64 };
+static_assert(CH * STG_TQ6 <= CH * STG_F16, "staging area holds both tq6_0 sides");
+enum { ROW_M2 = 16, ROW_MNEW = 32, ROW_ALPHA = 48, ROW_L = 64 };
 enum { RED_MAX = 0, RED_L = 64 };
 
-// fp16 K-major no-swizzle operand with 16 rows: element (row n, k) at (k/8)*256 + n*16 + (k%8)*2 bytes;
-// an MMA's 16-element K step is 512 bytes (LBO 256, SBO 128)
-__device__ __forceinline__ uint32_t h_off(int n, int k) { return (uint32_t) ((k >> 3) * 256 + n * 16 + (k & 7) * 2); }
-
-__device__ __forceinline__ uint32_t f2h_bits(float v) { return (uint32_t) __half_as_ushort(__float2half_rn(v)); }
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {    // fp16 pair, a in the low half
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ float2 unpack_h2(uint32_t w) {
+    const __half2 h = *reinterpret_cast<const __half2 *>(&w);
+    return __half22float2(h);
+}
 
 __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -78,7 +93,7 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     uint32_t * cent2 = reinterpret_cast<uint32_t *>(sm + OFF_CENT);
     float * red = reinterpret_cast<float *>(sm + OFF_RED);
     float * row = reinterpret_cast<float *>(sm + OFF_ROW);
-    float * nrm = reinterpret_cast<float *>(sm + OFF_NRM);           // [0,256): normK b*128+t; [256,512): normV
+    float * nrm = reinterpret_cast<float *>(sm + OFF_NRM);           // normK b*128+t, then normV at 256 + b*128+t
     const uint8_t ** rowp = reinterpret_cast<const uint8_t **>(sm + OFF_ROWP);
     uint64_t * bar = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
@@ -90,53 +105,13 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_fence_init(); }
     if (tid < 64) {
         const float c = sjk_tq6_cent[tid];
-        const uint32_t hi = f2h_bits(c);
-        const uint32_t lo = f2h_bits(c - __half2float(__ushort_as_half((unsigned short) hi)));
-        cent2[tid] = hi | (lo << 16);
+        const __half hi = __float2half_rn(c);
+        cent2[tid] = pack_h2(__half2float(hi), c - __half2float(hi));
     }
     if (tid < NR) { row[ROW_M2 + tid] = -INFINITY; row[ROW_L + tid] = 0.0f; }
-    // ---- B_Q: q rows (rotated) as fp16 hi + lo, each row rescaled by a power of two to max |q| < 2^13 ----
-    {
-        const int d = tid;                               // one channel per thread, all 16 rows
-        float qv[NR];
-        float qm = 0.0f;
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            float x = 0.0f;
-            if (r < p.rows) {
-                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                x = p.q[((size_t) iq * p.n_head + hq) * D + d];
-            }
-            qv[r] = x;
-        }
-        // row maxima across the 256 threads
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            float m = fabsf(qv[r]);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-            if (lane == 0) red[warp * NR + r] = m;      // 8 warps x 16 rows = 128 floats (both red areas)
-        }
-        __syncthreads();
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            qm = 0.0f;
-            for (int w = 0; w < 8; ++w) qm = fmaxf(qm, red[w * NR + r]);
-            const int e = (qm > 0.0f && qm < INFINITY) ? 13 - pow2_exp(qm) : 0;
-            const float x = qv[r] * pow2f(e);
-            const uint32_t hi = f2h_bits(x);
-            const uint32_t lo = f2h_bits(x - __half2float(__ushort_as_half((unsigned short) hi)));
-            const uint32_t off = h_off(r, d);
-            *reinterpret_cast<uint16_t *>(bq + off) = (uint16_t) hi;
-            *reinterpret_cast<uint16_t *>(bq + 8192 + off) = (uint16_t) lo;
-            if (d == 0) row[ROW_QINV + r] = pow2f(-e);
-        }
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
-    const uint32_t idesc = tc::idesc_f16(128, NR);
+    const uint32_t S_eff = v.S < p.N ? v.S : p.N;
+    const uint32_t t0_ring = p.B > v.S ? p.B : v.S;
+    const uint32_t idesc32 = tc::idesc_f16(128, NB), idesc16 = tc::idesc_f16(128, NR);
     const float sl2 = p.scale * LOG2E;
     uint32_t qlim[8];
 #pragma unroll
@@ -149,9 +124,33 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
     bool ok = true;
     uint32_t mma_phase = 0;
-    bool mma_pending = false;
-    const uint32_t S_eff = v.S < p.N ? v.S : p.N;
-    const uint32_t t0_ring = p.B > v.S ? p.B : v.S;
+    bool mma_pending = false, bq_done = false;
+    uint32_t tmem = 0;
+    const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
+    // issue the MMAs of one side (thread 0): D (32 columns) += A_hi x B[hi | lo] (+ A_lo x B_hi), 8 k steps
+    auto mma_side = [&](uint32_t d_col, const uint8_t * b_base, bool f16) {
+        const uint64_t db = tc::smem_desc(b_base, HCH, 128);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            tc::mma_ts(tmem + d_col, tmem + COL_AH + 8 * k, db + (uint64_t) ((2 * HCH * k) >> 4), idesc32, k ? 1u : 0u);
+            if (!f16) tc::mma_ts(tmem + d_col, tmem + COL_AL + 8 * k, db + (uint64_t) ((2 * HCH * k) >> 4), idesc16, 1u);
+        }
+        tc::mma_commit(bar);
+    };
+    // all threads: A stores visible to the MMA, thread 0 issues, everyone waits for the commit (bounded)
+    auto run_mma = [&](uint32_t d_col, const uint8_t * b_base, bool f16) -> bool {
+        tc::wait_st();
+        tc::fence_proxy_async();
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        if (tid == 0) mma_side(d_col, b_base, f16);
+        mma_pending = true;
+        const bool got = __syncthreads_and(tc::mbar_wait(bar, mma_phase));
+        if (got) { mma_phase ^= 1u; mma_pending = false; }
+        tc::fence_after_sync();
+        return got;
+    };
 
     for (uint32_t ci = c_begin; ci < c_end && ok; ++ci) {
         // ---- chunk geometry and row kind ----
@@ -172,33 +171,62 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
             rowp[tid] = r;
         }
         __syncthreads();
-        // stage the chunk's rows of one side (asynchronous copies; zeros past len)
+        // stage the chunk's rows (asynchronous copies, zeros past len), one warp per token: tq6_0 K and V rows
+        // together (392 contiguous bytes, 49 x 8 bytes); fp16 rows one side at a time (512 bytes, 32 x 16)
         auto stage = [&](int side) {
-            const uint32_t so = side ? side_off : 0u;
             if (f16) {
+                const uint32_t so = side ? side_off : 0u;
 #pragma unroll 4
-                for (int i = tid; i < CH * 32; i += NT) {
-                    const int t = i >> 5, u = i & 31;
-                    tc::cp_async16(stg + t * STG_F16 + 16 * u, rowp[t] + so + 16 * u, (uint32_t) t < len ? 16u : 0u);
-                }
+                for (int t = warp; t < CH; t += NT / 32)
+                    tc::cp_async16(stg + t * STG_F16 + 16 * lane, rowp[t] + so + 16 * lane, (uint32_t) t < len ? 16u : 0u);
             } else {
 #pragma unroll 4
-                for (int i = tid; i < CH * 49; i += NT) {
-                    const int t = i / 49, u = i - 49 * t;
-                    tc::cp_async4(stg + t * STG_TQ6 + 4 * u, rowp[t] + so + 4 * u, (uint32_t) t < len ? 4u : 0u);
+                for (int t = warp; t < CH; t += NT / 32) {
+                    const uint8_t * src = rowp[t];
+                    const uint32_t n = (uint32_t) t < len ? 8u : 0u;
+                    tc::cp_async8(stg + t * STG_TQ6 + 8 * lane, src + 8 * lane, n);
+                    if (lane < 17) tc::cp_async8(stg + t * STG_TQ6 + 256 + 8 * lane, src + 256 + 8 * lane, n);
                 }
             }
         };
         stage(0);
+        if (!bq_done) {
+            // ---- B_Q = [q hi | q lo] (rotated rows), built while the first chunk's rows stream in ----
+            const int d = tid;
+            const float * __restrict__ qg = p.q;
+            float x[NR];                                         // all loads first: the stores below are shared
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const int rr = r < p.rows ? r : 0;
+                const int iq = rr / p.grp, hq = hl * p.grp + rr % p.grp;
+                x[r] = __ldg(qg + ((size_t) iq * p.n_head + hq) * D + d);
+            }
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                const float xr = r < p.rows ? x[r] : 0.0f;
+                const __half hi = __float2half_rn(xr);
+                *reinterpret_cast<__half *>(bq + h_off(r, d)) = hi;
+                *reinterpret_cast<__half *>(bq + h_off(NR + r, d)) = __float2half_rn(xr - __half2float(hi));
+            }
+            bq_done = true;
+        }
         tc::cp_async_wait_all();
+        tc::fence_before_sync();
         __syncthreads();
+        tc::fence_after_sync();
+        tmem = *tmem_slot;
         if (tid < CH) {
             const uint8_t * r0 = stg + tid * sstride;
             nrm[tid] = f16 ? 1.0f : h2f(*reinterpret_cast<const uint16_t *>(r0));
             nrm[CH + tid] = f16 ? 1.0f : h2f(*reinterpret_cast<const uint16_t *>(r0 + SJKVARN_TQ6_BLOCK_BYTES));
+            if (!f16) {
+                const uint8_t * v0 = stg + tid * STG_TQ6 + TQ6_ROW;
+                nrm[2 * CH + tid] = h2f(*reinterpret_cast<const uint16_t *>(v0));
+                nrm[3 * CH + tid] = h2f(*reinterpret_cast<const uint16_t *>(v0 + SJKVARN_TQ6_BLOCK_BYTES));
+            }
         }
-        // ---- K side: block by block, A (token tl, 64 channels of this half) -> TMEM, then 24 MMAs ----
-        for (int b = 0; b < 2; ++b) {
+        // ---- K side, block by block: A (token tl, channels 128 b + 64 half ..) -> TMEM, then the MMAs ----
+        for (int b = 0; b < 2 && ok; ++b) {
             {
                 uint32_t ch[32], cl[32];
                 const uint8_t * r0 = stg + tl * sstride;
@@ -209,13 +237,11 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
                         const uint4 x = src[c];
                         ch[4 * c] = x.x; ch[4 * c + 1] = x.y; ch[4 * c + 2] = x.z; ch[4 * c + 3] = x.w;
                     }
-#pragma unroll
-                    for (int c = 0; c < 32; ++c) cl[c] = 0u;
                 } else {
                     const uint8_t * blk = r0 + SJKVARN_TQ6_BLOCK_BYTES * b;
 #pragma unroll
                     for (int g = 0; g < 8; ++g) {
-                        const int j0 = 64 * half + 8 * g;
+                        const int j0 = 64 * half + 8 * g;                  // elements j0 .. j0 + 7 of the block
                         const uint32_t qs = (uint32_t) *reinterpret_cast<const uint16_t *>(blk + 2 + j0 / 2) |
                                             ((uint32_t) *reinterpret_cast<const uint16_t *>(blk + 4 + j0 / 2) << 16);
                         const uint32_t qh = *reinterpret_cast<const uint16_t *>(blk + 66 + j0 / 4);
@@ -228,61 +254,31 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
                             cl[4 * g + pp] = prmt(e0, e1, 0x7632u);
                         }
                     }
+                    tc::st_x16(tmem + lane_base + COL_AL + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
+                    tc::st_x16(tmem + lane_base + COL_AL + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
                 }
                 tc::st_x16(tmem + lane_base + COL_AH + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(ch));
                 tc::st_x16(tmem + lane_base + COL_AH + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(ch + 16));
-                tc::st_x16(tmem + lane_base + COL_AL + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
-                tc::st_x16(tmem + lane_base + COL_AL + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
             }
-            tc::wait_st();
-            tc::fence_proxy_async();
-            tc::fence_before_sync();
-            __syncthreads();
-            tc::fence_after_sync();
-            if (tid == 0) {
-#pragma unroll 1
-                for (int k = 0; k < 8; ++k) {
-                    const int kq = 8 * b + k;
-                    const uint32_t a_hi = tmem + COL_AH + 8 * k, a_lo = tmem + COL_AL + 8 * k;
-                    tc::mma_ts(tmem + COL_S + 16 * b, a_hi, tc::smem_desc(bq + 512 * kq, 256, 128), idesc, k ? 1u : 0u);
-                    tc::mma_ts(tmem + COL_S + 16 * b, a_hi, tc::smem_desc(bq + 8192 + 512 * kq, 256, 128), idesc, 1u);
-                    if (!f16) tc::mma_ts(tmem + COL_S + 16 * b, a_lo, tc::smem_desc(bq + 512 * kq, 256, 128), idesc, 1u);
-                }
-                tc::mma_commit(bar);
-            }
-            mma_pending = true;
-            if (b == 1) stage(1);                         // V rows replace K rows in the staging buffer meanwhile
-            const bool got = tc::mbar_wait(bar, mma_phase);
-            if (b == 1) tc::cp_async_wait_all();
-            ok = __syncthreads_and(got);
-            if (!ok) break;
-            mma_phase ^= 1u;
-            mma_pending = false;
-            tc::fence_after_sync();
+            ok = run_mma(COL_S + 32 * b, bq + TILE_B * b, f16);
         }
         if (!ok) break;
-        if (tid < CH) {
-            const uint8_t * r0 = stg + tid * sstride;
-            nrm[2 * CH + tid] = f16 ? 1.0f : h2f(*reinterpret_cast<const uint16_t *>(r0));
-            nrm[3 * CH + tid] = f16 ? 1.0f : h2f(*reinterpret_cast<const uint16_t *>(r0 + SJKVARN_TQ6_BLOCK_BYTES));
-        }
         // ---- scores of token tl, rows 8 half .. 8 half + 7 (log2 domain), row maxima ----
         float s2[8];
         {
-            float a0[8], a1[8];
-            uint32_t u0[8], u1[8];
-            tc::ld_x8_u(tmem + lane_base + COL_S + 8 * half, u0);
-            tc::ld_x8_u(tmem + lane_base + COL_S + 16 + 8 * half, u1);
+            uint32_t a0[8], a0l[8], a1[8], a1l[8];
+            tc::ld_x8_u(tmem + lane_base + COL_S + 8 * half, a0);
+            tc::ld_x8_u(tmem + lane_base + COL_S + 16 + 8 * half, a0l);
+            tc::ld_x8_u(tmem + lane_base + COL_S + 32 + 8 * half, a1);
+            tc::ld_x8_u(tmem + lane_base + COL_S + 48 + 8 * half, a1l);
             tc::wait_ld();
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { a0[i] = __uint_as_float(u0[i]); a1[i] = __uint_as_float(u1[i]); }
-            const float nk0 = nrm[tl], nk1 = nrm[CH + tl];
+            const float nk0 = nrm[tl] * sl2, nk1 = nrm[CH + tl] * sl2;
             const uint32_t pos = p0 + (uint32_t) tl;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const int r = 8 * half + i;
-                const float dot = (nk0 * a0[i] + nk1 * a1[i]) * row[ROW_QINV + r];
-                s2[i] = ((uint32_t) tl < len && pos < qlim[i]) ? dot * sl2 : -INFINITY;
+                const float dot = nk0 * (__uint_as_float(a0[i]) + __uint_as_float(a0l[i])) +
+                                  nk1 * (__uint_as_float(a1[i]) + __uint_as_float(a1l[i]));
+                s2[i] = ((uint32_t) tl < len && pos < qlim[i]) ? dot : -INFINITY;
             }
             const float mw = warp_rows8<true>(s2, lane);
             if ((lane & 3) == 0) red[RED_MAX + half * 32 + quarter * 8 + (lane >> 2)] = mw;
@@ -297,93 +293,86 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
             row[ROW_ALPHA + tid] = mnew == -INFINITY ? 1.0f : ex2(mold - mnew);
             row[ROW_M2 + tid] = mnew;
         }
+        // fp16 rows: the V rows replace the K rows in the staging area now (the K side is done with them)
+        if (f16) stage(1);
         __syncthreads();
-        // ---- P'_b = p * normV(t, b) as fp16 hi + lo (B of the V MMAs), row sums ----
+        // ---- P'_b = p * normV(t, b) as [hi | lo] (B of the V MMAs), row sums ----
         {
-            const float nv0 = nrm[2 * CH + tl], nv1 = nrm[3 * CH + tl];
             float ls[8];
+            if (f16) {
+                tc::cp_async_wait_all();
+            }
+            const float nv0 = f16 ? 1.0f : nrm[2 * CH + tl], nv1 = f16 ? 1.0f : nrm[3 * CH + tl];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const int r = 8 * half + i;
                 const float mnew = row[ROW_MNEW + r];
                 const float pw = mnew == -INFINITY ? 0.0f : ex2(s2[i] - mnew);
                 ls[i] = pw;
-                const uint32_t off = h_off(r, tl);
                 const float x0 = pw * nv0, x1 = pw * nv1;
-                const uint32_t h0 = f2h_bits(x0), h1 = f2h_bits(x1);
-                *reinterpret_cast<uint16_t *>(bvp + off) = (uint16_t) h0;
-                *reinterpret_cast<uint16_t *>(bvp + 4096 + off) = (uint16_t) f2h_bits(x0 - __half2float(__ushort_as_half((unsigned short) h0)));
-                *reinterpret_cast<uint16_t *>(bvp + 8192 + off) = (uint16_t) h1;
-                *reinterpret_cast<uint16_t *>(bvp + 12288 + off) = (uint16_t) f2h_bits(x1 - __half2float(__ushort_as_half((unsigned short) h1)));
+                const uint32_t hh = pack_h2(x0, x1);
+                const float2 hf = unpack_h2(hh);
+                const uint32_t ll = pack_h2(x0 - hf.x, x1 - hf.y);
+                const uint32_t o = h_off(r, tl);
+                *reinterpret_cast<uint16_t *>(bvp + o) = (uint16_t) hh;                   // tile 0 hi
+                *reinterpret_cast<uint16_t *>(bvp + o + 256) = (uint16_t) ll;             // tile 0 lo (row 16 + r)
+                *reinterpret_cast<uint16_t *>(bvp + TILE_B + o) = (uint16_t) (hh >> 16);  // tile 1 hi
+                *reinterpret_cast<uint16_t *>(bvp + TILE_B + o + 256) = (uint16_t) (ll >> 16);
             }
             const float lw = warp_rows8<false>(ls, lane);
             if ((lane & 3) == 0) red[RED_L + half * 32 + quarter * 8 + (lane >> 2)] = lw;
         }
-        // ---- V side: tile by tile, A (channel 128 b + tl, 64 tokens of this half) -> TMEM, then 24 MMAs ----
-        for (int b = 0; b < 2; ++b) {
+        __syncthreads();                                  // staged V rows and P' complete
+        if (tid < NR) {
+            const int hh = tid >> 3, rr = tid & 7;
+            const float * lr = red + RED_L + hh * 32 + rr;
+            row[ROW_L + tid] = row[ROW_L + tid] * row[ROW_ALPHA + tid] + ((lr[0] + lr[8]) + (lr[16] + lr[24]));
+        }
+        // ---- V side, tile by tile: A (channel 128 b + tl, tokens 64 half ..) -> TMEM, then the MMAs ----
+        const uint8_t * vbase = f16 ? stg : stg + TQ6_ROW;      // tq6_0: the V row follows the K row
+        for (int b = 0; b < 2 && ok; ++b) {
             {
                 uint32_t ch[32], cl[32];
                 const int d = 128 * b + tl;
+                if (f16) {
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const int t0 = 64 * half + 2 * c;
-                    const uint8_t * ra = stg + t0 * sstride, * rb = ra + sstride;
-                    if (f16) {
+                    for (int c = 0; c < 32; ++c) {
+                        const uint8_t * ra = vbase + (64 * half + 2 * c) * STG_F16;
                         const uint32_t x0 = *reinterpret_cast<const uint16_t *>(ra + 2 * d);
-                        const uint32_t x1 = *reinterpret_cast<const uint16_t *>(rb + 2 * d);
+                        const uint32_t x1 = *reinterpret_cast<const uint16_t *>(ra + STG_F16 + 2 * d);
                         ch[c] = x0 | (x1 << 16);
-                        cl[c] = 0u;
-                    } else {
-                        const int j = d & 127;
-                        const uint8_t * ba = ra + SJKVARN_TQ6_BLOCK_BYTES * b, * bb = rb + SJKVARN_TQ6_BLOCK_BYTES * b;
-                        const uint32_t c0 = ((ba[2 + (j >> 1)] >> (4 * (j & 1))) & 15) | (((ba[66 + (j >> 2)] >> (2 * (j & 3))) & 3) << 4);
-                        const uint32_t c1 = ((bb[2 + (j >> 1)] >> (4 * (j & 1))) & 15) | (((bb[66 + (j >> 2)] >> (2 * (j & 3))) & 3) << 4);
+                    }
+                } else {
+                    // the thread's channel: qs byte j/2 (nibble j%2), qh byte j/4 (2 bits at 2 (j%4)) of block b
+                    const int j = d & 127;
+                    const uint8_t * base = vbase + SJKVARN_TQ6_BLOCK_BYTES * b;
+                    const int oqs = 2 + (j >> 1), sqs = 4 * (j & 1), oqh = 66 + (j >> 2), sqh = 2 * (j & 3);
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const uint8_t * ra = base + (64 * half + 2 * c) * STG_TQ6, * rb = ra + STG_TQ6;
+                        const uint32_t c0 = ((ra[oqs] >> sqs) & 15) | (((ra[oqh] >> sqh) & 3) << 4);
+                        const uint32_t c1 = ((rb[oqs] >> sqs) & 15) | (((rb[oqh] >> sqh) & 3) << 4);
                         const uint32_t e0 = cent2[c0], e1 = cent2[c1];
                         ch[c] = prmt(e0, e1, 0x5410u);
                         cl[c] = prmt(e0, e1, 0x7632u);
                     }
+                    tc::st_x16(tmem + lane_base + COL_AL + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
+                    tc::st_x16(tmem + lane_base + COL_AL + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
                 }
                 tc::st_x16(tmem + lane_base + COL_AH + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(ch));
                 tc::st_x16(tmem + lane_base + COL_AH + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(ch + 16));
-                tc::st_x16(tmem + lane_base + COL_AL + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
-                tc::st_x16(tmem + lane_base + COL_AL + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
             }
-            tc::wait_st();
-            tc::fence_proxy_async();
-            tc::fence_before_sync();
-            __syncthreads();
-            tc::fence_after_sync();
-            if (tid == 0) {
-                const uint8_t * bhi = bvp + 8192 * b, * blo = bhi + 4096;
-#pragma unroll 1
-                for (int k = 0; k < 8; ++k) {
-                    const uint32_t a_hi = tmem + COL_AH + 8 * k, a_lo = tmem + COL_AL + 8 * k;
-                    tc::mma_ts(tmem + COL_O + 16 * b, a_hi, tc::smem_desc(bhi + 512 * k, 256, 128), idesc, k ? 1u : 0u);
-                    tc::mma_ts(tmem + COL_O + 16 * b, a_hi, tc::smem_desc(blo + 512 * k, 256, 128), idesc, 1u);
-                    if (!f16) tc::mma_ts(tmem + COL_O + 16 * b, a_lo, tc::smem_desc(bhi + 512 * k, 256, 128), idesc, 1u);
-                }
-                tc::mma_commit(bar);
-            }
-            mma_pending = true;
-            if (b == 0 && tid < NR) {
-                const int hh = tid >> 3, rr = tid & 7;
-                const float * lr = red + RED_L + hh * 32 + rr;
-                row[ROW_L + tid] = row[ROW_L + tid] * row[ROW_ALPHA + tid] + ((lr[0] + lr[8]) + (lr[16] + lr[24]));
-            }
-            ok = __syncthreads_and(tc::mbar_wait(bar, mma_phase));
-            if (!ok) break;
-            mma_phase ^= 1u;
-            mma_pending = false;
-            tc::fence_after_sync();
+            ok = run_mma(COL_O + 32 * b, bvp + TILE_B * b, f16);
         }
         if (!ok) break;
-        // ---- epilogue: channel 128 half + tl ----
+        // ---- epilogue: channel 128 half + tl, all rows (column groups hi*hi + lo*hi and hi*lo) ----
         {
-            float o[16];
-            tc::ld_x16(tmem + lane_base + COL_O + 16 * half, o);
+            float o[16], ol[16];
+            tc::ld_x16(tmem + lane_base + COL_O + 32 * half, o);
+            tc::ld_x16(tmem + lane_base + COL_O + 32 * half + 16, ol);
             tc::wait_ld();
 #pragma unroll
-            for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], row[ROW_ALPHA + r], o[r]);
+            for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], row[ROW_ALPHA + r], o[r] + ol[r]);
         }
         tc::fence_before_sync();
         __syncthreads();
@@ -406,7 +395,7 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, TM_COLS);
+    if (warp == 0) tc::tmem_dealloc(*tmem_slot, TM_COLS);
 }
 
 }  // namespace

@@ -172,6 +172,9 @@ __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t 
 __device__ __forceinline__ void cp_async4(void * dst, const void * src, uint32_t src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
 }
+__device__ __forceinline__ void cp_async8(void * dst, const void * src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
 __device__ __forceinline__ void cp_async16(void * dst, const void * src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
 }
