@@ -229,46 +229,70 @@ __global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
 
 // out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m). Grid (query row x head, channel tiles of
 // 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
+constexpr int MERGE_SPLITS = 768;                     // >= the most splits a call can make (148 + 296 + 296)
+constexpr int MERGE_PRE = 24;                         // outputs per thread loaded ahead of the weights
+
 __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out) {
-    extern __shared__ float wts[];                     // [splits]
-    __shared__ float s_inv;
-    __shared__ float s_red[8];
+    extern __shared__ float wts[];                     // [splits] weights, then [4][64] partial sums
+    __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float m = -__int_as_float(0x7F800000);
-    for (int i = tid; i < splits; i += blockDim.x) m = fmaxf(m, part[((size_t) i * n_rows + row) * (D + 2)]);
+    // the outputs of the first MERGE_PRE splits of this thread's group go in flight with the (m, l) loads
+    const int dl = tid & 63, grp4 = tid >> 6;
+    const bool live = d0 + dl < D;
+    const float * src = part + (size_t) row * (D + 2) + 2 + d0 + (live ? dl : 0);
+    const size_t step = (size_t) n_rows * (D + 2);
+    float xo[MERGE_PRE];
+#pragma unroll
+    for (int k = 0; k < MERGE_PRE; ++k) {
+        const int i = grp4 + 4 * k;
+        xo[k] = i < splits ? src[(size_t) i * step] : 0.0f;
+    }
+    // one pass over (m, l) of the splits this thread owns (at most MERGE_SPLITS / 256)
+    float mi[MERGE_SPLITS / 256], li[MERGE_SPLITS / 256];
+#pragma unroll
+    for (int k = 0; k < MERGE_SPLITS / 256; ++k) {
+        const int i = tid + 256 * k;
+        mi[k] = -INFINITY; li[k] = 0.0f;
+        if (i < splits) {
+            const float2 ml = *reinterpret_cast<const float2 *>(part + ((size_t) i * n_rows + row) * (D + 2));
+            mi[k] = ml.x; li[k] = ml.y;
+        }
+    }
+    float m = fmaxf(fmaxf(mi[0], mi[1]), mi[2]);
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
     if (lane == 0) s_red[warp] = m;
     __syncthreads();
     m = s_red[0];
-    for (int w = 1; w < (int) (blockDim.x >> 5); ++w) m = fmaxf(m, s_red[w]);
-    __syncthreads();
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, s_red[w]);
     float den = 0.0f;
-    for (int i = tid; i < splits; i += blockDim.x) {
-        const float * pp = part + ((size_t) i * n_rows + row) * (D + 2);
-        const float w = pp[0] == -__int_as_float(0x7F800000) ? 0.0f : expf(pp[0] - m);
-        wts[i] = w;
-        den += pp[1] * w;
+#pragma unroll
+    for (int k = 0; k < MERGE_SPLITS / 256; ++k) {
+        const int i = tid + 256 * k;
+        if (i < splits) {
+            const float w = mi[k] == -INFINITY ? 0.0f : expf(mi[k] - m);
+            wts[i] = w;
+            den += li[k] * w;
+        }
     }
     for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
-    if (lane == 0) s_red[warp] = den;
+    if (lane == 0) s_red[8 + warp] = den;
     __syncthreads();
-    if (tid == 0) {
-        float t = 0.0f;
-        for (int w = 0; w < (int) (blockDim.x >> 5); ++w) t += s_red[w];
-        s_inv = t == 0.0f ? 0.0f : 1.0f / t;
-    }
-    __syncthreads();
-    // 4 groups of 64 threads walk the splits in strides of 4; partial sums meet in shared memory
-    const int dl = tid & 63, grp4 = tid >> 6;
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += s_red[8 + w];
+    const float s_inv = t == 0.0f ? 0.0f : 1.0f / t;
+    // 4 groups of 64 threads walk the splits in strides of 4; failed or empty splits carry weight 0 and zero
+    // outputs. The first MERGE_PRE splits of each group were loaded together with (m, l), before the barriers.
     float o = 0.0f;
-    if (d0 + dl < D)
-        for (int i = grp4; i < splits; i += 4) {
-            const float w = wts[i];
-            if (w != 0.0f) o += part[((size_t) i * n_rows + row) * (D + 2) + 2 + d0 + dl] * w;
-        }
-    __syncthreads();
-    float * acc = wts + splits;                        // [4][64]
+#pragma unroll
+    for (int k = 0; k < MERGE_PRE; ++k) {
+        const int i = grp4 + 4 * k;
+        if (i < splits) o = fmaf(xo[k], wts[i], o);
+    }
+    for (int i = grp4 + 4 * MERGE_PRE; i < splits; i += 4) o = fmaf(src[(size_t) i * step], wts[i], o);
+    float * acc = wts + splits;
     acc[grp4 * 64 + dl] = o;
     __syncthreads();
     if (tid < 64 && d0 + tid < D)
@@ -349,6 +373,7 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense);
     const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
     const int splits = splits_tc + splits_d + splits_v1;
+    if (splits > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
     const size_t need = (size_t) splits * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
     if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));

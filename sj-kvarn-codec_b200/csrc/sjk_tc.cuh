@@ -3,6 +3,7 @@
 // Every wait is bounded: a wait that runs out records SJK_DEV_TIMEOUT in the device status word and
 // returns false, so a kernel can skip its remaining work, release its TMEM and exit instead of hanging.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -192,11 +193,8 @@ __device__ __forceinline__ float pow2f(int e) {
     e = e < -126 ? -126 : (e > 127 ? 127 : e);
     return __uint_as_float((uint32_t) (e + 127) << 23);
 }
-// exact fp16 -> fp32 for every finite half (scales of sealed records are finite)
-__device__ __forceinline__ float h2f(uint16_t h) {
-    const float mag = __uint_as_float(((uint32_t) h & 0x7FFFu) << 13) * 5.192296858534828e33f;   // x 2^112
-    return __uint_as_float(__float_as_uint(mag) | (((uint32_t) h & 0x8000u) << 16));
-}
+// fp16 -> fp32 (exact for every half)
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ float h2f_at(const uint8_t * p) { return h2f(*reinterpret_cast<const uint16_t *>(p)); }
 // float -> nearest integer and back (|v| < 2^22) without the conversion pipe
 __device__ __forceinline__ int f2i(float v) { return (int) (__float_as_uint(v + MAGIC) - MAGIC_BITS); }
