@@ -355,33 +355,36 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (B < v->S) return SJKVARN_ERR_ARG;
     const int grp = n_head / n_kv;
     if (n_q * grp > MAXROWS) return SJK_ERR_UNSUPPORTED;
-    // sealed records [0, n_tc) go to the tensor-core kernel when it supports the body format
+    // sealed records [0, n_tc) go to the tensor-core kernel when it supports the body format; when it also supports
+    // the staged-row formats, the same kernel takes the sink and the staging ring, else the dense kernel does
     const uint32_t b_end = B < N ? B : N;
-    const uint32_t n_tc = (sjk_tc_body_supported(v, n_q, grp) && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
-    int rps = 1;
-    const int splits_tc = sjk_tc_body_splits(n_tc, n_kv, &rps);
-    // the sink and the staging ring go to the dense tensor-core kernel when it supports the row formats
+    const bool tc_body = sjk_tc_body_supported(v, n_q, grp) != 0;
     const bool dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
+    const bool fused = tc_body && dense;
+    const uint32_t n_tc = (tc_body && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
     uint32_t n_sink_d = 0, n_dense = 0;
-    if (dense) {
+    if (dense && !fused) {
         const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
         n_sink_d = (s_end + 127u) / 128u;
         n_dense = n_sink_d + (N > t0 ? (N - t0 + 127u) / 128u : 0u);
     }
     int cps_d = 1;
-    const int splits_d = dense ? sjk_tc_dense_splits(n_dense, n_kv, &cps_d) : 0;
+    const int splits_d = (dense && !fused) ? sjk_tc_dense_splits(n_dense, n_kv, &cps_d) : 0;
     const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense);
     const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
-    const int splits = splits_tc + splits_d + splits_v1;
-    if (splits > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
-    const size_t need = (size_t) splits * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    // the tensor-core kernel's split count is known after its launch plan; bound it for the scratch check
+    const int splits_tc_max = (tc_body && (n_tc > 0 || fused)) ? sjk_tc_body_max_splits(n_kv) : 0;
+    const size_t need = (size_t) (splits_tc_max + splits_d + splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
-    if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
-    if (splits_tc) {
-        const int rc = sjk_tc_body_launch(v, n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch, 0,
-                                          splits_tc, rps, st);
+    if (splits_tc_max + splits_d + splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
+    int splits_tc = 0;
+    if (splits_tc_max) {
+        const int rc = sjk_tc_body_launch(v, B, N, n_tc, fused ? 1 : 0, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
+                                          (float *) scratch, 0, &splits_tc, st);
         if (rc) return rc;
     }
+    const int splits = splits_tc + splits_d + splits_v1;
+    if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
     if (splits_d) {
         const int rc = sjk_tc_dense_launch(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch,
                                            splits_tc, splits_d, n_sink_d, n_dense, cps_d, st);

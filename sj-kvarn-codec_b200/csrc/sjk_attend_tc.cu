@@ -43,6 +43,8 @@ constexpr uint32_t NS = 3;              // record stages
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t COL_AK = 0, COL_AV = 128, COL_O = 256, COL_S = 448;
 
+constexpr int MAX_SPLITS = 148;
+
 struct TcParams {
     sj_kvarn_layout lay;
     const uint8_t * body;
@@ -56,7 +58,14 @@ struct TcParams {
     float scale;
     float * part;               // [splits][n_q*n_head][D + 2]
     int split0;                 // partial slot of this kernel's first split
-    int recs_per_split;
+    // staged rows, taken by the same CTAs before their records: the sink [0, min(S, N)) and the staging ring
+    // [max(B, S), N) in chunks of 128 positions (sink chunks first); chunk u of a head goes to split u % splits
+    const uint8_t * sink;
+    const uint8_t * ring;
+    int staging, sink_type;
+    uint32_t cap, stage_bytes, B, N;
+    uint32_t n_sink_chunks, n_dense;
+    uint32_t rec_bounds[MAX_SPLITS + 1];   // records of split s: [rec_bounds[s], rec_bounds[s + 1])
 };
 
 // B operands: K-major, no swizzle, N = 48 rows (n = 16 digit + query row), 8-row x 16-byte core matrices
@@ -89,10 +98,25 @@ enum : uint32_t {                                             // offsets in floa
 constexpr uint32_t OFF_BAR = OFF_F + F_END * 4;
 enum : uint32_t {                                             // mbarrier indices
     B_RFULL = 0, B_REMPTY = 3, B_AK = 6, B_AV = 8, B_SFULL = 10, B_SFREE = 11, B_BV = 12, B_VDONE = 14, B_OFREE = 16,
-    B_COUNT = 18
+    B_DENSE = 18, B_COUNT = 19
 };
 constexpr uint32_t OFF_TMEM = OFF_BAR + B_COUNT * 8;
-constexpr uint32_t SMEM_TOTAL = OFF_TMEM + 16;
+// staged-row (dense) phase: rows staged in record stages 1..2, [q hi | q lo] in the B_K area, and its own
+// [P' hi | P' lo] operands and bookkeeping
+constexpr uint32_t HCH = 528;                                 // fp16 B operand: 8-element K chunk stride
+constexpr uint32_t TILE_H = 16 * HCH;                         // one fp16 B operand over 128 k
+constexpr uint32_t D_STG = OFF_REC + REC_MAX;                 // up to 2 REC_MAX bytes of staged rows
+constexpr uint32_t D_STG_F16 = 528, D_STG_TQ6 = 2 * 2 * SJKVARN_TQ6_BLOCK_BYTES;   // staged row strides
+constexpr uint32_t OFF_DBV = (OFF_TMEM + 16 + 127) & ~127u;   // 2 x TILE_H
+constexpr uint32_t OFF_DM = OFF_DBV + 2 * TILE_H;             // dense bookkeeping (bytes below)
+enum : uint32_t { DM_ROWP = 256, DM_NRM = 1280, DM_RED = 3328, DM_RED_L = 3584, DM_ROW = 3840, DM_QH = 4096,
+                  DM_END = 5120 };
+constexpr uint32_t OFF_DCODE = OFF_DM + DM_END;               // V codes of a chunk, [token][channel] bytes
+constexpr uint32_t OFF_DCENT = OFF_DCODE + 128 * 256;        // centroid (fp16 hi | lo) table, one copy per bank
+constexpr uint32_t SMEM_TOTAL = OFF_DCENT + 64 * 32 * 4;
+constexpr uint32_t DCOL_A = 0, DCOL_S = 256, DCOL_O = 320;   // dense TMEM: A (2 blocks x hi|lo), S (2 x 32), O (2 x 32)
+static_assert(128 * D_STG_F16 <= 2 * REC_MAX && 128 * D_STG_TQ6 <= 2 * REC_MAX, "staged rows fit in stages 1..2");
+static_assert(2 * TILE_H <= 2 * 16 * BCH, "[q hi | q lo] fits in the B_K area");
 
 // The 4-bit payloads are in 16x16-tile fragment order: the 4 words of one tile row group hold, for rows
 // i and i + 8 (low / high nibbles), word j = elements {2j, 2j+8, 2j+1, 2j+9} of the tile's k index. The
@@ -115,6 +139,17 @@ __device__ __forceinline__ void warp_arrive(uint64_t * bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
+// The 6-bit codes of elements j0 .. j0 + 7 (j0 % 8 == 0) of a tq6_0 block (norm, qs[64] nibbles, qh[32] 2-bit
+// fields, sj_kvarn.h:1249-1284) as 8 bytes: nibble pairs spread with one PRMT, the high bits from a 256-entry
+// table qh_lut[y] = (2-bit fields of y) << 4 in bytes 0..3.
+__device__ __forceinline__ uint2 codes8(const uint8_t * blk, int j0, const uint32_t * qh_lut) {
+    const uint32_t qs = (uint32_t) *reinterpret_cast<const uint16_t *>(blk + 2 + j0 / 2) |
+                        ((uint32_t) *reinterpret_cast<const uint16_t *>(blk + 4 + j0 / 2) << 16);
+    const uint32_t qh = *reinterpret_cast<const uint16_t *>(blk + 66 + j0 / 4);
+    const uint32_t a = qs & 0x0F0F0F0Fu, b = (qs >> 4) & 0x0F0F0F0Fu;          // nibbles 0 2 4 6 / 1 3 5 7
+    return make_uint2(prmt(a, b, 0x5140u) | qh_lut[qh & 0xFFu], prmt(a, b, 0x7362u) | qh_lut[qh >> 8]);
+}
+
 __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -123,8 +158,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     float * F = reinterpret_cast<float *>(sm + OFF_F);
     uint64_t * bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
-    const uint32_t r_begin = (uint32_t) split * (uint32_t) p.recs_per_split;
-    const uint32_t r_end = min(r_begin + (uint32_t) p.recs_per_split, p.n_rec);
+    const uint32_t r_begin = p.rec_bounds[split], r_end = p.rec_bounds[split + 1];
     const uint32_t n = r_end > r_begin ? r_end - r_begin : 0u;
 
     if (warp == 2 * NW) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
@@ -135,15 +169,336 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             tc::mbar_init(&bars[B_VDONE + i], 1); tc::mbar_init(&bars[B_OFREE + i], NW);
         }
         tc::mbar_init(&bars[B_SFULL], 1); tc::mbar_init(&bars[B_SFREE], NW);
+        tc::mbar_init(&bars[B_DENSE], 1);
         tc::mbar_fence_init();
     }
     if (tid < 2 * NR) F[F_M2 + tid] = -INFINITY;
     if (tid < NR) F[F_LSUM + tid] = 0.0f;
+    // staged-row chunk u of this head: first position, length, row format and the global K row of each token
+    struct Chunk { uint32_t p0, len, side_off; bool f16, in_sink; };
+    auto chunk_of = [&](uint32_t u) -> Chunk {
+        Chunk c;
+        const uint32_t s_eff = p.S < p.N ? p.S : p.N, t0 = p.B > p.S ? p.B : p.S;
+        c.in_sink = u < p.n_sink_chunks;
+        c.p0 = c.in_sink ? u * 128u : t0 + (u - p.n_sink_chunks) * 128u;
+        c.len = min(128u, (c.in_sink ? s_eff : p.N) - c.p0);
+        c.f16 = (c.in_sink && p.sink_type == SJKVARN_SINK_F16) || p.staging == SJKVARN_STAGING_F16;
+        c.side_off = (c.in_sink && p.sink_type == SJKVARN_SINK_F16) ? 2u * D : p.stage_bytes;
+        return c;
+    };
+    const uint8_t ** rowp = reinterpret_cast<const uint8_t **>(sm + OFF_DM + DM_ROWP);
+    auto set_rowp = [&](const Chunk & c) {
+        if (tid < 128) {
+            const uint32_t pos = c.p0 + (uint32_t) min(tid, (int) c.len - 1);
+            const uint8_t * r;
+            if (c.in_sink && p.sink_type == SJKVARN_SINK_F16) r = p.sink + ((size_t) pos * p.H + h) * 4 * D;
+            else if (c.in_sink) r = p.sink + ((size_t) pos * p.H + h) * 2 * p.stage_bytes;
+            else r = p.ring + ((size_t) sjk_ring_slot(p.S, p.cap, pos) * p.H + h) * 2 * p.stage_bytes;
+            rowp[tid] = r;
+        }
+    };
+    float qx[8];                                        // staged rows: this thread's q values (channel tid % 256)
+    if ((uint32_t) split < p.n_dense) {
+        set_rowp(chunk_of((uint32_t) split));
+        const int d = tid & 255, r0 = (tid >> 8) * 8;
+        const float * __restrict__ qg = p.q;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = r0 + i, rr = r < p.rows ? r : 0;
+            qx[i] = tid < 512 ? __ldg(qg + ((size_t) (rr / p.grp) * p.n_head + hl * p.grp + rr % p.grp) * D + d) : 0.0f;
+        }
+    }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
+    float acc[NR];                                      // softmax warps: running output of their channel, all rows
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+    // record 0 streams into stage 0 while the staged rows (stages 1..2) are processed
+    const uint32_t pre_loaded = n >= 1 ? 1u : 0u;
+    if (tid == 2 * NW * 32 && pre_loaded) {
+        const uint32_t blk = p.blocks ? p.blocks[r_begin] : r_begin;
+        tc::mbar_expect_tx(&bars[B_RFULL], l.bytes);
+        tc::bulk_g2s(sm + OFF_REC, p.body + ((size_t) blk * p.H + h) * l.bytes, l.bytes, &bars[B_RFULL]);
+    }
+
+    if ((uint32_t) split < p.n_dense) {
+        // ====== staged rows (sink, staging ring): chunks split, split + splits, .. of this head, one at a time ======
+        // K side per block b:  S_b^T[t, r] = sum_{d in b} cent[code_K(t, d)] q[r, d],    dot = sum_b normK(t, b) S_b
+        // V side per tile b:   O_b^T[d, r] = sum_t cent[code_V(t, d)] P'_b[r, t],        P'_b = p normV(t, b)
+        // with fp16 hi + lo halves: A = centroid (hi | lo), B = [hi | lo] side by side in N (N = 32); two MMAs per
+        // k step (A_hi x [hi | lo], A_lo x hi) leave hi*hi + lo*hi in columns 0..15 and hi*lo in 16..31. fp16 rows
+        // enter with lo = 0. The chunk's scores join the CTA's running softmax state (m, l, acc) directly.
+        // Warps 0..15: quarter w % 4, group w / 4 (block / tile w / 8, half (w / 4) % 2; score rows 4 (w / 4) ..).
+        const int W = warp, quarter = W & 3, grp = W >> 2, tl = quarter * 32 + lane;
+        const bool worker = W < 2 * NW;
+        const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
+        uint8_t * stg = sm + D_STG;
+        uint8_t * dbq = sm + OFF_BK;
+        uint8_t * dbv = sm + OFF_DBV;
+        // centroid table, 32 copies interleaved by bank: entry c of lane L at word 32 c + L (conflict-free lookups)
+        uint32_t * centr = reinterpret_cast<uint32_t *>(sm + OFF_DCENT);
+        float * nrm = reinterpret_cast<float *>(sm + OFF_DM + DM_NRM);       // normK b*128+t, normV 256 + b*128+t
+        float * dred = reinterpret_cast<float *>(sm + OFF_DM + DM_RED);      // [4 groups][4 quarters][4 rows]
+        float * dredl = reinterpret_cast<float *>(sm + OFF_DM + DM_RED_L);
+        float * drow = reinterpret_cast<float *>(sm + OFF_DM + DM_ROW);      // mnew[16], alpha[16]
+        uint32_t * qh_lut = reinterpret_cast<uint32_t *>(sm + OFF_DM + DM_QH);
+        uint8_t * vcodes = sm + OFF_DCODE;                                    // [token][channel] V codes
+        auto hoff = [](int nn, int k) -> uint32_t { return (uint32_t) (k >> 3) * HCH + (uint32_t) (nn * 16 + (k & 7) * 2); };
+        const float sl2 = p.scale * LOG2E;
+        uint32_t qlim4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = 4 * grp + i;
+            qlim4[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
+        }
+        uint32_t dphase = 0;
+        bool d_pending = false;
+        // all threads: operand stores visible, warp 16 lane 0 issues both blocks / tiles; dense_wait: everyone waits
+        auto dense_issue = [&](const uint8_t * b_base, uint32_t d_col, bool f16) {
+            tc::wait_st();
+            tc::fence_proxy_async();
+            tc::fence_before_sync();
+            __syncthreads();
+            tc::fence_after_sync();
+            if (tid == 2 * NW * 32) {
+                const uint32_t idesc32 = tc::idesc_f16(128, 2 * NR), idesc16 = tc::idesc_f16(128, NR);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const uint64_t db = tc::smem_desc(b_base + TILE_H * b, HCH, 128);
+                    const uint32_t ah = tmem + DCOL_A + 128 * b, dc = tmem + d_col + 32 * b;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        tc::mma_ts(dc, ah + 8 * k, db + (uint64_t) ((2 * HCH * k) >> 4), idesc32, k ? 1u : 0u);
+                        if (!f16) tc::mma_ts(dc, ah + 64 + 8 * k, db + (uint64_t) ((2 * HCH * k) >> 4), idesc16, 1u);
+                    }
+                }
+                tc::mma_commit(&bars[B_DENSE]);
+            }
+            d_pending = true;
+        };
+        auto dense_wait = [&]() -> bool {
+            const bool got = __syncthreads_and(tc::mbar_wait(&bars[B_DENSE], dphase));
+            if (got) { dphase ^= 1u; d_pending = false; }
+            tc::fence_after_sync();
+            return got;
+        };
+        for (uint32_t u = (uint32_t) split; u < p.n_dense && ok; u += gridDim.x) {
+            const Chunk ck = chunk_of(u);
+            const uint32_t p0 = ck.p0, len = ck.len, side_off = ck.side_off;
+            const bool f16 = ck.f16;
+            const uint32_t sstride = f16 ? D_STG_F16 : D_STG_TQ6;
+            if (u != (uint32_t) split) {                       // the first chunk's row addresses were set up front
+                set_rowp(ck);
+                __syncthreads();
+            }
+            // rows of the chunk (asynchronous copies, zeros past len), one warp per token: tq6_0 K and V rows
+            // together (392 contiguous bytes, 49 x 8); fp16 rows one side at a time (512 bytes, 32 x 16)
+            auto stage = [&](int side) {
+                if (f16) {
+                    const uint32_t so = side ? side_off : 0u;
+                    for (int t = W; t < 128; t += 2 * NW)
+                        tc::cp_async16(stg + t * D_STG_F16 + 16 * lane, rowp[t] + so + 16 * lane, (uint32_t) t < len ? 16u : 0u);
+                } else {
+                    for (int t = W; t < 128; t += 2 * NW) {
+                        const uint8_t * src = rowp[t];
+                        const uint32_t nb = (uint32_t) t < len ? 8u : 0u;
+                        tc::cp_async8(stg + t * D_STG_TQ6 + 8 * lane, src + 8 * lane, nb);
+                        if (lane < 17) tc::cp_async8(stg + t * D_STG_TQ6 + 256 + 8 * lane, src + 256 + 8 * lane, nb);
+                    }
+                }
+            };
+            if (worker) stage(0);
+            if (u == (uint32_t) split) {
+                // tables and [q hi | q lo], built while the first chunk's rows stream in
+                if (tid < 256) {
+                    const uint32_t y = (uint32_t) tid;
+                    qh_lut[tid] = ((y & 3u) << 4) | (((y >> 2) & 3u) << 12) | (((y >> 4) & 3u) << 20) | (((y >> 6) & 3u) << 28);
+                }
+                for (int i = tid; i < 64 * 32; i += NT) {
+                    const float c = sjk_tq6_cent[i >> 5];
+                    const __half hi = __float2half_rn(c);
+                    const __half2 hl2 = __floats2half2_rn(__half2float(hi), c - __half2float(hi));
+                    centr[i] = *reinterpret_cast<const uint32_t *>(&hl2);
+                }
+                if (tid < 512) {                                   // [q hi | q lo]: channel tid % 256, rows 8 (tid / 256) ..
+                    const int d = tid & 255, r0 = (tid >> 8) * 8;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = r0 + i;
+                        const float xr = r < p.rows ? qx[i] : 0.0f;
+                        const __half hi = __float2half_rn(xr);
+                        *reinterpret_cast<__half *>(dbq + hoff(r, d)) = hi;
+                        *reinterpret_cast<__half *>(dbq + hoff(NR + r, d)) = __float2half_rn(xr - __half2float(hi));
+                    }
+                }
+            }
+            if (worker) tc::cp_async_wait_all();
+            tc::fence_before_sync();
+            __syncthreads();
+            tc::fence_after_sync();
+            if (tid < 128) {
+                const uint8_t * r0 = stg + tid * sstride;
+                nrm[tid] = f16 ? 1.0f : h2f_at(r0);
+                nrm[128 + tid] = f16 ? 1.0f : h2f_at(r0 + SJKVARN_TQ6_BLOCK_BYTES);
+                nrm[256 + tid] = f16 ? 1.0f : h2f_at(r0 + 2 * SJKVARN_TQ6_BLOCK_BYTES);
+                nrm[384 + tid] = f16 ? 1.0f : h2f_at(r0 + 3 * SJKVARN_TQ6_BLOCK_BYTES);
+            }
+            // ---- K side: block grp / 2, channels 64 ((grp % 2)) .. of token tl -> A (hi | lo) ----
+            if (worker) {
+                const int b = grp >> 1, half = grp & 1;
+                uint32_t ch[32], cl[32];
+                const uint8_t * r0 = stg + tl * sstride;
+                if (f16) {
+                    const uint4 * src = reinterpret_cast<const uint4 *>(r0 + 2 * (128 * b + 64 * half));
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 x = src[c];
+                        ch[4 * c] = x.x; ch[4 * c + 1] = x.y; ch[4 * c + 2] = x.z; ch[4 * c + 3] = x.w;
+                    }
+                } else {
+                    const uint8_t * blk = r0 + SJKVARN_TQ6_BLOCK_BYTES * b;
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const uint2 cw = codes8(blk, 64 * half + 8 * g, qh_lut);    // elements 64 half + 8 g ..
+#pragma unroll
+                        for (int pp = 0; pp < 4; ++pp) {
+                            const uint32_t w = pp < 2 ? cw.x : cw.y, sh = 16 * (pp & 1);
+                            const uint32_t e0 = centr[32 * ((w >> sh) & 0xFFu) + lane];
+                            const uint32_t e1 = centr[32 * ((w >> (sh + 8)) & 0xFFu) + lane];
+                            ch[4 * g + pp] = prmt(e0, e1, 0x5410u);
+                            cl[4 * g + pp] = prmt(e0, e1, 0x7632u);
+                        }
+                    }
+                    tc::st_x16(tmem + lane_base + DCOL_A + 128 * b + 64 + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
+                    tc::st_x16(tmem + lane_base + DCOL_A + 128 * b + 64 + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
+                }
+                tc::st_x16(tmem + lane_base + DCOL_A + 128 * b + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(ch));
+                tc::st_x16(tmem + lane_base + DCOL_A + 128 * b + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(ch + 16));
+            }
+            dense_issue(dbq, DCOL_S, f16);
+            // tq6_0 (while the K MMAs run): V codes of the chunk in natural order (token, 8 channels per item) for
+            // the channel-wise A build
+            if (!f16 && worker) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int it = tid + 512 * k, t = it >> 5, gch = it & 31;          // channels 8 gch ..
+                    const uint8_t * vblk = stg + t * D_STG_TQ6 + 2 * SJKVARN_TQ6_BLOCK_BYTES + SJKVARN_TQ6_BLOCK_BYTES * (gch >> 4);
+                    *reinterpret_cast<uint2 *>(vcodes + t * 256 + 8 * gch) = codes8(vblk, 8 * (gch & 15), qh_lut);
+                }
+            }
+            ok = dense_wait();
+            if (!ok) break;
+            // ---- scores of token tl for rows 4 grp .. 4 grp + 3 (log2 domain), row maxima ----
+            float s2[4];
+            if (worker) {
+                uint32_t a0[4], a0l[4], a1[4], a1l[4];
+                tc::ld_x4_u(tmem + lane_base + DCOL_S + 4 * grp, a0);
+                tc::ld_x4_u(tmem + lane_base + DCOL_S + 16 + 4 * grp, a0l);
+                tc::ld_x4_u(tmem + lane_base + DCOL_S + 32 + 4 * grp, a1);
+                tc::ld_x4_u(tmem + lane_base + DCOL_S + 48 + 4 * grp, a1l);
+                tc::wait_ld();
+                const float nk0 = nrm[tl] * sl2, nk1 = nrm[128 + tl] * sl2;
+                const uint32_t pos = p0 + (uint32_t) tl;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float dot = nk0 * (__uint_as_float(a0[i]) + __uint_as_float(a0l[i])) +
+                                      nk1 * (__uint_as_float(a1[i]) + __uint_as_float(a1l[i]));
+                    s2[i] = ((uint32_t) tl < len && pos < qlim4[i]) ? dot : -INFINITY;
+                }
+                const float mw = warp_rows4<true>(s2, lane);
+                if ((lane & 7) == 0) dred[(grp * 4 + quarter) * 4 + (lane >> 3)] = mw;
+            }
+            tc::fence_before_sync();
+            __syncthreads();
+            if (tid < NR) {
+                const int r = tid, gq = (r >> 2) * 16 + (r & 3);
+                const float mrec = fmaxf(fmaxf(dred[gq], dred[gq + 4]), fmaxf(dred[gq + 8], dred[gq + 12]));
+                const float mold = F[F_M2 + NR + r], mnew = fmaxf(mold, mrec);
+                drow[r] = mnew;
+                drow[NR + r] = mnew == -INFINITY ? 1.0f : ex2(mold - mnew);
+                F[F_M2 + NR + r] = mnew;
+            }
+            if (f16 && worker) stage(1);                          // fp16: the V rows replace the K rows
+            __syncthreads();
+            // ---- P'_b = p normV(t, b) as [hi | lo] per tile, row sums ----
+            if (worker) {
+                if (f16) tc::cp_async_wait_all();
+                const float nv0 = nrm[256 + tl], nv1 = nrm[384 + tl];
+                float ls[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int r = 4 * grp + i;
+                    const float mnew = drow[r];
+                    const float pw = mnew == -INFINITY ? 0.0f : ex2(s2[i] - mnew);
+                    ls[i] = pw;
+                    const float x0 = pw * nv0, x1 = pw * nv1;
+                    const __half2 hh = __floats2half2_rn(x0, x1);
+                    const float2 hf = __half22float2(hh);
+                    const __half2 ll = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+                    const uint32_t o = hoff(r, tl);
+                    *reinterpret_cast<__half *>(dbv + o) = __low2half(hh);
+                    *reinterpret_cast<__half *>(dbv + o + 256) = __low2half(ll);
+                    *reinterpret_cast<__half *>(dbv + TILE_H + o) = __high2half(hh);
+                    *reinterpret_cast<__half *>(dbv + TILE_H + o + 256) = __high2half(ll);
+                }
+                const float lw = warp_rows4<false>(ls, lane);
+                if ((lane & 7) == 0) dredl[(grp * 4 + quarter) * 4 + (lane >> 3)] = lw;
+            }
+            __syncthreads();
+            if (tid < NR) {
+                const int r = tid, gq = (r >> 2) * 16 + (r & 3);
+                F[F_LSUM + r] = F[F_LSUM + r] * drow[NR + r] + ((dredl[gq] + dredl[gq + 4]) + (dredl[gq + 8] + dredl[gq + 12]));
+            }
+            // ---- V side: tile grp / 2, channel 128 (grp / 2) + tl, tokens 64 (grp % 2) .. -> A (hi | lo) ----
+            if (worker) {
+                const int t = grp >> 1, half = grp & 1, d = 128 * t + tl;
+                const uint8_t * vbase = f16 ? stg : stg + 2 * SJKVARN_TQ6_BLOCK_BYTES;   // tq6_0: V row follows K row
+                uint32_t ch[32], cl[32];
+                if (f16) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const uint8_t * ra = vbase + (64 * half + 2 * c) * D_STG_F16;
+                        const uint32_t x0 = *reinterpret_cast<const uint16_t *>(ra + 2 * d);
+                        const uint32_t x1 = *reinterpret_cast<const uint16_t *>(ra + D_STG_F16 + 2 * d);
+                        ch[c] = x0 | (x1 << 16);
+                    }
+                } else {
+                    const uint8_t * col = vcodes + (64 * half) * 256 + d;
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const uint32_t e0 = centr[32 * col[(2 * c) * 256] + lane], e1 = centr[32 * col[(2 * c + 1) * 256] + lane];
+                        ch[c] = prmt(e0, e1, 0x5410u);
+                        cl[c] = prmt(e0, e1, 0x7632u);
+                    }
+                    tc::st_x16(tmem + lane_base + DCOL_A + 128 * t + 64 + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(cl));
+                    tc::st_x16(tmem + lane_base + DCOL_A + 128 * t + 64 + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(cl + 16));
+                }
+                tc::st_x16(tmem + lane_base + DCOL_A + 128 * t + 32 * half, *reinterpret_cast<uint32_t (*)[16]>(ch));
+                tc::st_x16(tmem + lane_base + DCOL_A + 128 * t + 32 * half + 16, *reinterpret_cast<uint32_t (*)[16]>(ch + 16));
+            }
+            dense_issue(dbv, DCOL_O, f16);
+            ok = dense_wait();
+            if (!ok) break;
+            // ---- epilogue (softmax warps): channel 128 half + tl, all rows ----
+            if (warp >= NW && warp < 2 * NW) {
+                const int half = (warp - NW) >> 2;
+                float o[16], ol[16];
+                tc::ld_x16(tmem + lane_base + DCOL_O + 32 * half, o);
+                tc::ld_x16(tmem + lane_base + DCOL_O + 32 * half + 16, ol);
+                tc::wait_ld();
+#pragma unroll
+                for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], drow[NR + r], o[r] + ol[r]);
+            }
+            tc::fence_before_sync();
+            __syncthreads();
+            tc::fence_after_sync();
+        }
+        if (d_pending) tc::mbar_wait(&bars[B_DENSE], dphase);      // a chunk that gave up: its MMAs first (bounded)
+        __syncthreads();                                          // B_K area and TMEM free for the records
+    }
 
     if (warp < NW) {
         // ================= unpack: A_K, B_K (+ zero-point partials), A_V of record g =================
@@ -277,9 +632,6 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             qlim[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
         }
         const int vcol = sjk_v_ch(l, 128 * half + tl);           // epilogue channel 128 half + tl
-        float acc[NR];
-#pragma unroll
-        for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
         float vc_n = 0.0f, vc_e = 0.0f;                          // Vch: newest record / record of the next epilogue
         for (uint32_t g = 0; g <= n; ++g) {                      // pass n only finishes record n - 1
             const uint32_t b = g & 1u, pb = b ^ 1u;
@@ -468,7 +820,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                 tc::mma_ts_i8(tmem + COL_S, a0 + 8 * k, bd + (uint64_t) ((2 * BCH * k) >> 4), idesc, k ? 1u : 0u);
             tc::mma_commit(&bars[B_SFULL]);
         };
-        uint32_t loaded = 0, k_issued = 0, v_issued = 0;
+        uint32_t loaded = pre_loaded, k_issued = 0, v_issued = 0;   // record 0 was issued before the staged rows
         for (; loaded < n && loaded < NS; ++loaded) load(loaded, blk_of(loaded));
         uint32_t next_blk = loaded < n ? blk_of(loaded) : 0u;    // block of the next record to load, read ahead
         if (n) {
@@ -538,23 +890,55 @@ int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp) {
            n_q * grp <= NR && l.bytes == REC_MAX;
 }
 
-// one persistent CTA per SM over the call's KV heads
-int sjk_tc_body_splits(uint32_t n_rec, int n_kv, int * recs_per_split) {
-    if (n_rec == 0) { *recs_per_split = 1; return 0; }
-    const int target = (148 + n_kv - 1) / n_kv;
-    int rps = (int) ((n_rec + (uint32_t) target - 1) / (uint32_t) target);
-    if (rps < 1) rps = 1;
-    *recs_per_split = rps;
-    return (int) ((n_rec + (uint32_t) rps - 1) / (uint32_t) rps);
+// Splits (persistent CTAs) per KV head: one CTA per SM over the call's KV heads, at most one per work item.
+int sjk_tc_body_max_splits(int n_kv) {
+    const int t = (148 + (n_kv > 0 ? n_kv : 1) - 1) / (n_kv > 0 ? n_kv : 1);
+    return t < MAX_SPLITS ? t : MAX_SPLITS;
 }
 
-int sjk_tc_body_launch(const sjk_view * v, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
-                       const float * q, float scale, float * part, int split0, int splits, int recs_per_split,
+// A staged-row chunk costs about DENSE_WEIGHT sealed records of CTA time; the record ranges are balanced so that
+// the CTAs that also take a chunk get fewer records.
+constexpr double DENSE_WEIGHT = 2.0;
+
+int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int with_dense, uint32_t qpos0, int n_q,
+                       int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                        sjk_stream st) {
     TcParams p;
     p.lay = v->lay; p.body = v->body; p.blocks = v->blocks; p.H = v->n_head_kv; p.kv0 = kv0; p.S = v->S;
     p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
-    p.q = q; p.scale = scale; p.part = part; p.split0 = split0; p.recs_per_split = recs_per_split;
+    p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
+    p.sink = v->sink; p.ring = v->ring; p.staging = v->staging; p.sink_type = v->sink_type; p.cap = v->cap;
+    p.stage_bytes = (uint32_t) v->stage_bytes; p.B = B; p.N = N;
+    p.n_sink_chunks = 0; p.n_dense = 0;
+    if (with_dense) {
+        const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
+        p.n_sink_chunks = (s_end + 127u) / 128u;
+        p.n_dense = p.n_sink_chunks + (N > t0 ? (N - t0 + 127u) / 128u : 0u);
+    }
+    const uint32_t items = n_rec + p.n_dense;
+    int splits = sjk_tc_body_max_splits(n_kv);
+    if ((uint32_t) splits > items) splits = (int) items;
+    *splits_out = splits;
+    if (splits == 0) return 0;
+    // record ranges: split s takes d(s) chunks (u = s, s + splits, ..) and about target - DENSE_WEIGHT d(s) records
+    double want[MAX_SPLITS], total = 0.0;
+    const double target = ((double) n_rec + DENSE_WEIGHT * p.n_dense) / splits;
+    for (int s = 0; s < splits; ++s) {
+        const uint32_t d = p.n_dense > (uint32_t) s ? (p.n_dense - 1u - (uint32_t) s) / (uint32_t) splits + 1u : 0u;
+        const double w = target - DENSE_WEIGHT * d;
+        want[s] = w > 0.0 ? w : 0.0;
+        total += want[s];
+    }
+    double run = 0.0;
+    p.rec_bounds[0] = 0;
+    for (int s = 0; s < splits; ++s) {
+        run += want[s];
+        uint32_t b = total > 0.0 ? (uint32_t) (run / total * n_rec + 0.5) : 0u;
+        if (b > n_rec) b = n_rec;
+        if (b < p.rec_bounds[s]) b = p.rec_bounds[s];
+        p.rec_bounds[s + 1] = b;
+    }
+    p.rec_bounds[splits] = n_rec;
     cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
     attend_body_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);

@@ -17,11 +17,13 @@ int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, f
 // decode row t of one record (is_v selects V) to out[D] (device)
 int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st);
 
-// tensor-core body attention (sjk_attend_tc.cu)
+// tensor-core attention over the sealed body of a 4-bit scalar layer (sjk_attend_tc.cu); with_dense: the same
+// CTAs also take the staged rows (sink and staging ring, formats of sjk_tc_dense_supported). *splits_out gets the
+// number of partial slots per query row the launch writes (from split0).
 int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp);
-int sjk_tc_body_splits(uint32_t n_rec, int n_kv, int * recs_per_split);
-int sjk_tc_body_launch(const sjk_view * v, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
-                       const float * q, float scale, float * part, int split0, int splits, int recs_per_split,
+int sjk_tc_body_max_splits(int n_kv);
+int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int with_dense, uint32_t qpos0, int n_q,
+                       int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                        sjk_stream st);
 
 // tensor-core attention over the staged rows: the sink [0, S) and the staging ring [B, N) (sjk_attend_dense.cu)

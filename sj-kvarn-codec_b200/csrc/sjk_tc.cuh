@@ -64,6 +64,12 @@ __device__ __forceinline__ void st_x16(uint32_t taddr, const uint32_t (&v)[16]) 
                  "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
                  : "memory");
 }
+__device__ __forceinline__ void ld_x4_u(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+}
 __device__ __forceinline__ void ld_x8_u(uint32_t taddr, uint32_t (&r)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -279,6 +285,23 @@ __device__ __forceinline__ float warp_rows16(const float (&v)[16], int lane) {
     const float d = MAX ? fmaxf(keep, r) : keep + r;
     r = __shfl_xor_sync(0xFFFFFFFFu, d, 1);
     return MAX ? fmaxf(d, r) : d + r;
+}
+
+// Reduce 4 per-thread values (rows 0..3) across the 32 lanes; afterwards lanes 8r..8r+7 hold row r.
+template <bool MAX>
+__device__ __forceinline__ float warp_rows4(const float (&v)[4], int lane) {
+    const bool u16 = lane & 16, u8 = lane & 8;
+    float r0 = __shfl_xor_sync(0xFFFFFFFFu, u16 ? v[0] : v[2], 16), r1 = __shfl_xor_sync(0xFFFFFFFFu, u16 ? v[1] : v[3], 16);
+    const float a0 = MAX ? fmaxf(u16 ? v[2] : v[0], r0) : (u16 ? v[2] : v[0]) + r0;
+    const float a1 = MAX ? fmaxf(u16 ? v[3] : v[1], r1) : (u16 ? v[3] : v[1]) + r1;
+    const float r = __shfl_xor_sync(0xFFFFFFFFu, u8 ? a0 : a1, 8);
+    float c = MAX ? fmaxf(u8 ? a1 : a0, r) : (u8 ? a1 : a0) + r;
+#pragma unroll
+    for (int o = 4; o; o >>= 1) {
+        const float x = __shfl_xor_sync(0xFFFFFFFFu, c, o);
+        c = MAX ? fmaxf(c, x) : c + x;
+    }
+    return c;
 }
 
 // Sum 4 per-thread values (rows 0..3) across the 32 lanes; afterwards lanes 8r..8r+7 hold row r.
