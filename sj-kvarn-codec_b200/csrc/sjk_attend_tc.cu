@@ -86,19 +86,20 @@ enum : uint32_t {                                             // offsets in floa
     F_QMAX = 96,       // [8][4]        per-unpack-warp row maxima of |q|
     F_UMAX2 = 128,     // [2][8]        max |Kscale| per unpack warp, per buffer
     F_M2 = 144,        // [2][16]       running max (log2 domain) after the record of each buffer
-    F_ALPHA = 176,     // [2][16]       rescale of the running sums when the record of each buffer arrived
-    F_VINV = 208,      // [2][16]       2^-ev of the P' rescale per buffer
-    F_RMAXV = 240,     // [2][8]        per-softmax-warp max |Vscale|
-    F_RMAX = 256,      // [2][2][4][8]  row maxima of the scores per (buffer, row half, lane quarter)
-    F_RL = 384,        // [2][2][4][8]  row sums of p
-    F_RZ = 512,        // [2][2][4][8]  row sums of p Vzero
-    F_LSUM = 640,      // [16]          running sums of p
-    F_END = 656
+    F_ALPHA = 176,     // [3][16]       rescale of the running sums when record g arrived (slot g % 3)
+    F_VINV = 224,      // [3][16]       2^-ev of the P' rescale (slot g % 3)
+    F_RMAXV = 272,     // [2][8]        per-softmax-warp max |Vscale|
+    F_RMAX = 288,      // [2][2][4][8]  row maxima of the scores per (buffer, row half, lane quarter)
+    F_RL = 416,        // [2][2][4][8]  row sums of p
+    F_RZ = 544,        // [3][2][4][8]  row sums of p Vzero (slot g % 3)
+    F_LSUM = 736,      // [16]          running sums of p
+    F_OK = 752,        // [4]           per role: all its waits completed (unpack, softmax, issuer)
+    F_END = 768
 };
 constexpr uint32_t OFF_BAR = OFF_F + F_END * 4;
 enum : uint32_t {                                             // mbarrier indices
     B_RFULL = 0, B_REMPTY = 3, B_AK = 6, B_AV = 8, B_SFULL = 10, B_SFREE = 11, B_BV = 12, B_VDONE = 14, B_OFREE = 16,
-    B_DENSE = 18, B_COUNT = 19
+    B_DENSE = 18, B_EPI = 19, B_COUNT = 22
 };
 constexpr uint32_t OFF_TMEM = OFF_BAR + B_COUNT * 8;
 // staged-row (dense) phase: rows staged in record stages 1..2, [q hi | q lo] in the B_K area, and its own
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
         }
         tc::mbar_init(&bars[B_SFULL], 1); tc::mbar_init(&bars[B_SFREE], NW);
         tc::mbar_init(&bars[B_DENSE], 1);
+        for (int i = 0; i < 3; ++i) tc::mbar_init(&bars[B_EPI + i], NW);
         tc::mbar_fence_init();
     }
     if (tid < 2 * NR) F[F_M2 + tid] = -INFINITY;
@@ -482,9 +484,9 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             dense_issue(dbv, DCOL_O, f16);
             ok = dense_wait();
             if (!ok) break;
-            // ---- epilogue (softmax warps): channel 128 half + tl, all rows ----
-            if (warp >= NW && warp < 2 * NW) {
-                const int half = (warp - NW) >> 2;
+            // ---- epilogue (unpack warps, which hold the outputs): channel 128 half + tl, all rows ----
+            if (warp < NW) {
+                const int half = warp >> 2;
                 float o[16], ol[16];
                 tc::ld_x16(tmem + lane_base + DCOL_O + 32 * half, o);
                 tc::ld_x16(tmem + lane_base + DCOL_O + 32 * half + 16, ol);
@@ -539,6 +541,40 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) kcol[j] = sjk_k_ch(l, kch[j]);
         const int shift = (tl & 8) ? 4 : 0;                      // the thread's row nibbles (token tl / channel tl)
+        const int vcol = sjk_v_ch(l, 128 * half + tl);           // output channel 128 half + tl (epilogue)
+        float vc_m1 = 0.0f, vc_m2 = 0.0f;                        // its Vch in records g - 1 and g - 2
+        // epilogue of record e (O buffer e % 2, softmax slot e % 3): channel 128 half + tl, all rows. The caller
+        // has waited for the record's V MMAs; the softmax warps publish alpha, 2^-ev and z through B_EPI.
+        auto epilogue = [&](uint32_t e, float vc) -> bool {
+            const uint32_t eb = e & 1u, e3 = e % 3u;
+            const bool ready = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_EPI + e3], (e / 3u) & 1u));
+            if (ready) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {                // rows 8 hh .. 8 hh + 7
+                    uint32_t o0[8], o1[8], o2[8];
+                    const uint32_t oc = tmem + lane_base + COL_O + 96 * eb + 48 * half + 8 * hh;
+                    tc::ld_x8_u(oc, o0);
+                    tc::ld_x8_u(oc + 16, o1);
+                    tc::ld_x8_u(oc + 32, o2);
+                    float al[8], vi[8], za[8], zc[8], zd[8], ze[8];
+                    ld8(F + F_ALPHA + 16 * e3 + 8 * hh, al);
+                    ld8(F + F_VINV + 16 * e3 + 8 * hh, vi);
+                    ld8(F + F_RZ + 64 * e3 + 32 * hh, za); ld8(F + F_RZ + 64 * e3 + 32 * hh + 8, zc);
+                    ld8(F + F_RZ + 64 * e3 + 32 * hh + 16, zd); ld8(F + F_RZ + 64 * e3 + 32 * hh + 24, ze);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        // |sum_t code P''| < 128 * 15 * 2^20 < 2^31: the digit sums recombine exactly in s32
+                        const float O = (float) (int) (o0[i] + (o1[i] << 8) + (o2[i] << 16));
+                        const float z = (za[i] + zc[i]) + (zd[i] + ze[i]);
+                        acc[8 * hh + i] = fmaf(acc[8 * hh + i], al[i], vc * fmaf(O, vi[i], z));
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            warp_arrive(&bars[B_OFREE + eb], lane);
+            return ready;
+        };
         for (uint32_t g = 0; g < n; ++g) {
             const uint32_t s = g % NS, b = g & 1u;
             const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
@@ -556,6 +592,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             ok = tc::nbar_and(1, NW * 32, ok && w_ok);
             if (!ok) break;
             tc::fence_after_sync();
+            const float vc_g = h2f_at(rec + l.v_ch + 2 * vcol);
             float maxk = 0.0f;
 #pragma unroll
             for (int w = 0; w < NW; ++w) maxk = fmaxf(maxk, F[F_UMAX2 + 8 * b + w]);
@@ -601,6 +638,9 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             // ---- A_V: channel 128 half + tl over the 8 token tiles; A_V[b] was last read by the V MMAs of g - 2 ----
             if (g >= 2) ok = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_VDONE + b], ((g - 2) >> 1) & 1u));
             tc::fence_after_sync();
+            if (ok && g >= 2) ok = epilogue(g - 2, vc_m2);           // record g - 2 out of O[b] before V(g) reuses it
+            vc_m2 = vc_m1;
+            vc_m1 = vc_g;
             if (ok) {
                 const uint8_t * vp = rec + l.v_payload;
                 const int d = 128 * half + tl;
@@ -617,12 +657,19 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             }
             warp_arrive(&bars[B_REMPTY + s], lane);
         }
+        // the last two records' epilogues (their V MMAs may still be running)
+        for (uint32_t e = n >= 2 ? n - 2 : 0u; ok && e < n; ++e) {
+            ok = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_VDONE + (e & 1u)], (e >> 1) & 1u));
+            tc::fence_after_sync();
+            if (ok) ok = epilogue(e, e + 2 == n ? vc_m2 : vc_m1);
+        }
+        ok = tc::nbar_and(1, NW * 32, ok);
+        if (lane == 0) F[F_OK] = ok ? 1.0f : 0.0f;             // (read after the CTA barrier below)
     } else if (warp < 2 * NW) {
-        // ===== softmax: scores and weights of record g, B_V digits, then the epilogue of record g - 1 =====
-        // Thread (quarter, half, lane): token tl of the record for rows 8 half .. 8 half + 7, and channel
-        // 128 half + tl of the output for all rows. Lane 0 of the quarter-0 warps keeps the running sums l.
+        // ===== softmax: scores and weights of record g, B_V digits, row sums; the unpack warps run the epilogue =====
+        // Thread (quarter, half, lane): token tl of the record for rows 8 half .. 8 half + 7. Lanes 0..7 of the
+        // quarter-0 warps keep the running max / sums of their half's rows.
         const int sw = warp - NW, quarter = sw & 3, half = sw >> 2, tl = quarter * 32 + lane;
-        const bool keeper = quarter == 0 && lane == 0;
         const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
         const float sl2 = p.scale * LOG2E;
         uint32_t qlim[8];                                        // rows 8 half + i: positions < qlim are visible
@@ -631,10 +678,8 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             const int r = 8 * half + i;
             qlim[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
         }
-        const int vcol = sjk_v_ch(l, 128 * half + tl);           // epilogue channel 128 half + tl
-        float vc_n = 0.0f, vc_e = 0.0f;                          // Vch: newest record / record of the next epilogue
         for (uint32_t g = 0; g <= n; ++g) {                      // pass n only finishes record n - 1
-            const uint32_t b = g & 1u, pb = b ^ 1u;
+            const uint32_t b = g & 1u, pb = b ^ 1u, s3 = g % 3u, ps3 = (g + 2u) % 3u;   // ps3: slot of record g - 1
             if (g < n) {
                 const uint32_t s = g % NS;
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
@@ -656,8 +701,6 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                 warp_arrive(&bars[B_SFREE], lane);
                 const float kt = h2f_at(rec + l.k_tok + 2 * tl);
                 const float vsc = h2f_at(rec + l.v_scale + 2 * tl), vz = h2f_at(rec + l.v_zero + 2 * tl);
-                vc_e = vc_n;
-                vc_n = h2f_at(rec + l.v_ch + 2 * vcol);
                 warp_arrive(&bars[B_REMPTY + s], lane);
                 // ---- scores of token tl for rows 8 half .. 8 half + 7 (log2 domain), row maxima, max |Vscale| ----
                 float s2[8];
@@ -697,11 +740,11 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                     if (quarter == 0 && lane < 8) {                    // the keeper warp of this half records the row
                         if (g >= 1) {                                  // record g - 1 joins the running sum
                             const float * rl = F + F_RL + 64 * pb + 32 * half + i;
-                            F[F_LSUM + r] = F[F_LSUM + r] * F[F_ALPHA + 16 * pb + r] + ((rl[0] + rl[8]) + (rl[16] + rl[24]));
+                            F[F_LSUM + r] = F[F_LSUM + r] * F[F_ALPHA + 16 * ps3 + r] + ((rl[0] + rl[8]) + (rl[16] + rl[24]));
                         }
                         F[F_M2 + 16 * b + r] = mn;
-                        F[F_ALPHA + 16 * b + r] = mn == -INFINITY ? 1.0f : ex2(mold - mn);
-                        F[F_VINV + 16 * b + r] = pow2f(-ev);
+                        F[F_ALPHA + 16 * s3 + r] = mn == -INFINITY ? 1.0f : ex2(mold - mn);
+                        F[F_VINV + 16 * s3 + r] = pow2f(-ev);
                     }
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
@@ -724,81 +767,26 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                         bv[16 * i + 512] = (uint8_t) (z >> 16);
                     }
                     tc::fence_proxy_async();
-                    warp_arrive(&bars[B_BV + b], lane);
                     const float lw = warp_rows8<false>(ls, lane);
                     const float zw = warp_rows8<false>(zs, lane);
                     if ((lane & 3) == 0) {
                         F[F_RL + 64 * b + 32 * half + 8 * quarter + (lane >> 2)] = lw;
-                        F[F_RZ + 64 * b + 32 * half + 8 * quarter + (lane >> 2)] = zw;
+                        F[F_RZ + 64 * s3 + 32 * half + 8 * quarter + (lane >> 2)] = zw;
                     }
+                    warp_arrive(&bars[B_BV + b], lane);
+                    warp_arrive(&bars[B_EPI + s3], lane);            // alpha, 2^-ev and z of record g for the epilogue
                 }
             } else {
-                vc_e = vc_n;
                 tc::nbar_sync(2, NW * 32);                         // the last record's row sums are visible
                 if (quarter == 0 && lane < 8 && n >= 1) {
                     const int r = 8 * half + lane;
                     const float * rl = F + F_RL + 64 * pb + 32 * half + lane;
-                    F[F_LSUM + r] = F[F_LSUM + r] * F[F_ALPHA + 16 * pb + r] + ((rl[0] + rl[8]) + (rl[16] + rl[24]));
+                    F[F_LSUM + r] = F[F_LSUM + r] * F[F_ALPHA + 16 * ps3 + r] + ((rl[0] + rl[8]) + (rl[16] + rl[24]));
                 }
-            }
-            // ---- epilogue of record g - 1 (buffer pb): channel 128 half + tl, all rows ----
-            if (g >= 1) {
-                const uint32_t pg = g - 1;
-                // warp-uniform: the TMEM loads below are .sync.aligned
-                const bool e_ok = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_VDONE + pb], (pg >> 1) & 1u));
-                tc::fence_after_sync();
-                if (e_ok) {
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {                // rows 8 hh .. 8 hh + 7
-                        uint32_t o0[8], o1[8], o2[8];
-                        const uint32_t oc = tmem + lane_base + COL_O + 96 * pb + 48 * half + 8 * hh;
-                        tc::ld_x8_u(oc, o0);
-                        tc::ld_x8_u(oc + 16, o1);
-                        tc::ld_x8_u(oc + 32, o2);
-                        float al[8], vi[8], za[8], zc[8], zd[8], ze[8];
-                        ld8(F + F_ALPHA + 16 * pb + 8 * hh, al);
-                        ld8(F + F_VINV + 16 * pb + 8 * hh, vi);
-                        ld8(F + F_RZ + 64 * pb + 32 * hh, za); ld8(F + F_RZ + 64 * pb + 32 * hh + 8, zc);
-                        ld8(F + F_RZ + 64 * pb + 32 * hh + 16, zd); ld8(F + F_RZ + 64 * pb + 32 * hh + 24, ze);
-                        tc::wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            // |sum_t code P''| < 128 * 15 * 2^20 < 2^31: the digit sums recombine exactly in s32
-                            const float O = (float) (int) (o0[i] + (o1[i] << 8) + (o2[i] << 16));
-                            const float z = (za[i] + zc[i]) + (zd[i] + ze[i]);
-                            acc[8 * hh + i] = fmaf(acc[8 * hh + i], al[i], vc_e * fmaf(O, vi[i], z));
-                        }
-                    }
-                }
-                tc::fence_before_sync();
-                warp_arrive(&bars[B_OFREE + pb], lane);
-                ok = ok && e_ok;
             }
         }
         ok = tc::nbar_and(2, NW * 32, ok);
-        // ---- partials (m in the natural-log domain, l, o[D]) per real query row ----
-        const uint32_t mb = n >= 1 ? (n - 1) & 1u : 1u;
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            if (r < p.rows) {
-                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
-                dst[2 + 128 * half + tl] = ok ? acc[r] : 0.0f;
-            }
-        }
-        if (keeper) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = 8 * half + i;
-                if (r < p.rows) {
-                    const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                    float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
-                    const float m2 = F[F_M2 + 16 * mb + r];
-                    dst[0] = ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
-                    dst[1] = ok ? F[F_LSUM + r] : 0.0f;
-                }
-            }
-        }
+        if (lane == 0) F[F_OK + 1] = ok ? 1.0f : 0.0f;        // (read after the CTA barrier below)
     } else if (lane == 0) {
         // ========================== issuer: record copies, MMAs, commits ==========================
         const uint32_t idesc = tc::idesc_s8(128, NB);
@@ -863,6 +851,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                 if (loaded < n) next_blk = blk_of(loaded);
             }
         }
+        F[F_OK + 2] = ok ? 1.0f : 0.0f;
         if (!ok) {
             // drain (bounded): the last commits cover every MMA issued; the last NS copies may still be in flight
             if (k_issued) tc::mbar_wait(&bars[B_SFULL], (k_issued - 1) & 1u);
@@ -875,6 +864,31 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // ---- partials (m in the natural-log domain, l, o[D]) per real query row, valid only if every role finished ----
+    {
+        const bool all_ok = F[F_OK] != 0.0f && F[F_OK + 1] != 0.0f && F[F_OK + 2] != 0.0f && ok;
+        if (warp < NW) {                                       // unpack warps hold the outputs: channel 128 half + tl
+            const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                if (r < p.rows) {
+                    const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
+                    float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
+                    dst[2 + 128 * half + tl] = all_ok ? acc[r] : 0.0f;
+                }
+            }
+        } else if (warp < 2 * NW && tid - NW * 32 < NR) {      // one thread per row: m and l
+            const int r = tid - NW * 32;
+            if (r < p.rows) {
+                const uint32_t mb = n >= 1 ? (n - 1) & 1u : 1u;
+                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
+                float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
+                const float m2 = F[F_M2 + 16 * mb + r];
+                dst[0] = all_ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
+                dst[1] = all_ok ? F[F_LSUM + r] : 0.0f;
+            }
+        }
+    }
     if (warp == 2 * NW) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
