@@ -826,6 +826,15 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                 issue_k(g + 1);
                 ++k_issued;
             }
+            // the stage of record g takes record g + NS once both consumer groups released it (the softmax warps do
+            // right after reading S of record g, long before its B_V is ready: load early, ahead of V(g))
+            if (loaded < n) {
+                ok = tc::mbar_wait(&bars[B_REMPTY + g % NS], (g / NS) & 1u);
+                if (!ok) break;
+                load(loaded, next_blk);
+                ++loaded;
+                if (loaded < n) next_blk = blk_of(loaded);
+            }
             ok = tc::mbar_wait(&bars[B_AV + b], (g >> 1) & 1u);
             if (ok) ok = tc::mbar_wait(&bars[B_BV + b], (g >> 1) & 1u);
             if (ok && g >= 2) ok = tc::mbar_wait(&bars[B_OFREE + b], ((g - 2) >> 1) & 1u);
@@ -841,14 +850,6 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                         tc::mma_ts_i8(d0 + 48 * tile, a0 + 32 * tile + 8 * k, bd + (uint64_t) ((2 * BCH * k) >> 4), idesc, k ? 1u : 0u);
                 tc::mma_commit(&bars[B_VDONE + b]);
                 ++v_issued;
-            }
-            // the stage of record g takes record g + NS once both consumer groups released it
-            if (loaded < n) {
-                ok = tc::mbar_wait(&bars[B_REMPTY + g % NS], (g / NS) & 1u);
-                if (!ok) break;
-                load(loaded, next_blk);
-                ++loaded;
-                if (loaded < n) next_blk = blk_of(loaded);
             }
         }
         F[F_OK + 2] = ok ? 1.0f : 0.0f;
