@@ -84,7 +84,7 @@ enum : uint32_t {                                             // offsets in floa
     F_KINV = 0,        // [2][16]       2^-e of the Q' rescale per buffer
     F_CPART = 32,      // [2][8][4]     zero-point partials per unpack warp (warps 2i, 2i+1: rows 4i..4i+3)
     F_QMAX = 96,       // [8][4]        per-unpack-warp row maxima of |q|
-    F_UMAX2 = 128,     // [2][8]        max |Kscale| per unpack warp, per buffer
+    F_FREE = 128,      // [16]          (unused)
     F_M2 = 144,        // [2][16]       running max (log2 domain) after the record of each buffer
     F_ALPHA = 176,     // [3][16]       rescale of the running sums when record g arrived (slot g % 3)
     F_VINV = 224,      // [3][16]       2^-ev of the P' rescale (slot g % 3)
@@ -544,11 +544,13 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
         const int vcol = sjk_v_ch(l, 128 * half + tl);           // output channel 128 half + tl (epilogue)
         float vc_m1 = 0.0f, vc_m2 = 0.0f;                        // its Vch in records g - 1 and g - 2
         // epilogue of record e (O buffer e % 2, softmax slot e % 3): channel 128 half + tl, all rows. The caller
-        // has waited for the record's V MMAs; the softmax warps publish alpha, 2^-ev and z through B_EPI.
-        auto epilogue = [&](uint32_t e, float vc) -> bool {
+        // has waited for the record's V MMAs (B_VDONE) and for alpha, 2^-ev and z from the softmax warps (B_EPI).
+        auto wait_epi = [&](uint32_t e) -> bool {
+            return __all_sync(0xFFFFFFFFu, tc::mbar_wait2(&bars[B_VDONE + (e & 1u)], (e >> 1) & 1u, &bars[B_EPI + e % 3u], (e / 3u) & 1u));
+        };
+        auto epilogue = [&](uint32_t e, float vc) {
             const uint32_t eb = e & 1u, e3 = e % 3u;
-            const bool ready = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_EPI + e3], (e / 3u) & 1u));
-            if (ready) {
+            {
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {                // rows 8 hh .. 8 hh + 7
                     uint32_t o0[8], o1[8], o2[8];
@@ -563,39 +565,36 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                     ld8(F + F_RZ + 64 * e3 + 32 * hh + 16, zd); ld8(F + F_RZ + 64 * e3 + 32 * hh + 24, ze);
                     tc::wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
+                    for (int i = 0; i < 8; i += 2) {           // rows in pairs: packed fp32 arithmetic
                         // |sum_t code P''| < 128 * 15 * 2^20 < 2^31: the digit sums recombine exactly in s32
-                        const float O = (float) (int) (o0[i] + (o1[i] << 8) + (o2[i] << 16));
-                        const float z = (za[i] + zc[i]) + (zd[i] + ze[i]);
-                        acc[8 * hh + i] = fmaf(acc[8 * hh + i], al[i], vc * fmaf(O, vi[i], z));
+                        const float2 O = make_float2((float) (int) (o0[i] + (o1[i] << 8) + (o2[i] << 16)),
+                                                     (float) (int) (o0[i + 1] + (o1[i + 1] << 8) + (o2[i + 1] << 16)));
+                        const float2 z = add2(add2(make_float2(za[i], za[i + 1]), make_float2(zc[i], zc[i + 1])),
+                                              add2(make_float2(zd[i], zd[i + 1]), make_float2(ze[i], ze[i + 1])));
+                        const float2 t = mul2(make_float2(vc, vc), fma2(O, make_float2(vi[i], vi[i + 1]), z));
+                        const float2 r = fma2(make_float2(acc[8 * hh + i], acc[8 * hh + i + 1]), make_float2(al[i], al[i + 1]), t);
+                        acc[8 * hh + i] = r.x;
+                        acc[8 * hh + i + 1] = r.y;
                     }
                 }
             }
             tc::fence_before_sync();
             warp_arrive(&bars[B_OFREE + eb], lane);
-            return ready;
         };
         for (uint32_t g = 0; g < n; ++g) {
             const uint32_t s = g % NS, b = g & 1u;
             const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
             // A_K[b] and B_K[b] were last read by the K MMAs of record g - 2: done once those of g - 1 are
-            bool w_ok = tc::mbar_wait(&bars[B_RFULL + s], (g / NS) & 1u);
-            if (g >= 1) w_ok = w_ok && tc::mbar_wait(&bars[B_SFULL], (g - 1) & 1u);
+            const bool w_ok = g >= 1 ? tc::mbar_wait2(&bars[B_RFULL + s], (g / NS) & 1u, &bars[B_SFULL], (g - 1) & 1u)
+                                     : tc::mbar_wait(&bars[B_RFULL + s], (g / NS) & 1u);
+            ok = __all_sync(0xFFFFFFFFu, ok && w_ok);
+            if (!ok) break;
+            tc::fence_after_sync();
             float ks[4], kz[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) { ks[j] = h2f_at(rec + l.k_scale + 2 * kcol[j]); kz[j] = h2f_at(rec + l.k_zero + 2 * kcol[j]); }
-            {
-                float mk = fmaxf(fmaxf(fabsf(ks[0]), fabsf(ks[1])), fmaxf(fabsf(ks[2]), fabsf(ks[3])));
-                for (int o = 16; o; o >>= 1) mk = fmaxf(mk, __shfl_xor_sync(0xFFFFFFFFu, mk, o));
-                if (lane == 0) F[F_UMAX2 + 8 * b + warp] = mk;
-            }
-            ok = tc::nbar_and(1, NW * 32, ok && w_ok);
-            if (!ok) break;
-            tc::fence_after_sync();
             const float vc_g = h2f_at(rec + l.v_ch + 2 * vcol);
-            float maxk = 0.0f;
-#pragma unroll
-            for (int w = 0; w < NW; ++w) maxk = fmaxf(maxk, F[F_UMAX2 + 8 * b + w]);
+            const float maxk = absmax256_h(rec + l.k_scale, lane);  // max |Kscale| of the record (every warp on its own)
             // ---- A_K: token tl, channel tiles 8 half .. 8 half + 7 ----
             {
                 const uint8_t * kp = rec + l.k_payload;
@@ -619,14 +618,17 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                     const int e = (bound > 0.0f && bound < INFINITY) ? 21 - pow2_exp(bound) : 0;
                     const float sc = pow2f(e);
                     if (bg == 0) F[F_KINV + 16 * b + r] = pow2f(-e);
-                    const uint32_t z0 = digits3(qv[i][0] * ks[0], sc), z1 = digits3(qv[i][1] * ks[1], sc);
-                    const uint32_t z2 = digits3(qv[i][2] * ks[2], sc), z3 = digits3(qv[i][3] * ks[3], sc);
+                    const uint2 z01 = digits3x2(mul2(make_float2(qv[i][0], qv[i][1]), make_float2(ks[0], ks[1])), make_float2(sc, sc));
+                    const uint2 z23 = digits3x2(mul2(make_float2(qv[i][2], qv[i][3]), make_float2(ks[2], ks[3])), make_float2(sc, sc));
+                    const uint32_t z0 = z01.x, z1 = z01.y, z2 = z23.x, z3 = z23.y;
                     const uint32_t a = prmt(z0, z1, 0x5140u), c = prmt(z2, z3, 0x5140u);   // [z0.0 z1.0 z0.1 z1.1]
                     const uint32_t off = b_off(r, 4 * bg);
                     *reinterpret_cast<uint32_t *>(bk + off) = prmt(a, c, 0x5410u);
                     *reinterpret_cast<uint32_t *>(bk + off + 256) = prmt(a, c, 0x7632u);
                     *reinterpret_cast<uint32_t *>(bk + off + 512) = prmt(prmt(z0, z1, 0x0062u), prmt(z2, z3, 0x0062u), 0x5410u);
-                    cz[i] = (qv[i][0] * kz[0] + qv[i][1] * kz[1]) + (qv[i][2] * kz[2] + qv[i][3] * kz[3]);
+                    const float2 c2 = fma2(make_float2(qv[i][0], qv[i][2]), make_float2(kz[0], kz[2]),
+                                           mul2(make_float2(qv[i][1], qv[i][3]), make_float2(kz[1], kz[3])));
+                    cz[i] = c2.x + c2.y;
                 }
                 const float cw = warp_sum_rows4(cz[0], cz[1], cz[2], cz[3], lane);
                 if ((lane & 7) == 0) F[F_CPART + 32 * b + warp * 4 + (lane >> 3)] = cw;
@@ -636,9 +638,9 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             tc::fence_before_sync();
             warp_arrive(&bars[B_AK + b], lane);
             // ---- A_V: channel 128 half + tl over the 8 token tiles; A_V[b] was last read by the V MMAs of g - 2 ----
-            if (g >= 2) ok = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_VDONE + b], ((g - 2) >> 1) & 1u));
+            if (g >= 2) ok = wait_epi(g - 2);
             tc::fence_after_sync();
-            if (ok && g >= 2) ok = epilogue(g - 2, vc_m2);           // record g - 2 out of O[b] before V(g) reuses it
+            if (ok && g >= 2) epilogue(g - 2, vc_m2);                // record g - 2 out of O[b] before V(g) reuses it
             vc_m2 = vc_m1;
             vc_m1 = vc_g;
             if (ok) {
@@ -659,9 +661,9 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
         }
         // the last two records' epilogues (their V MMAs may still be running)
         for (uint32_t e = n >= 2 ? n - 2 : 0u; ok && e < n; ++e) {
-            ok = __all_sync(0xFFFFFFFFu, tc::mbar_wait(&bars[B_VDONE + (e & 1u)], (e >> 1) & 1u));
+            ok = wait_epi(e);
             tc::fence_after_sync();
-            if (ok) ok = epilogue(e, e + 2 == n ? vc_m2 : vc_m1);
+            if (ok) epilogue(e, e + 2 == n ? vc_m2 : vc_m1);
         }
         ok = tc::nbar_and(1, NW * 32, ok);
         if (lane == 0) F[F_OK] = ok ? 1.0f : 0.0f;             // (read after the CTA barrier below)
@@ -683,9 +685,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             if (g < n) {
                 const uint32_t s = g % NS;
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
-                bool w_ok = tc::mbar_wait(&bars[B_RFULL + s], (g / NS) & 1u);
-                w_ok = w_ok && tc::mbar_wait(&bars[B_SFULL], g & 1u);
-                w_ok = w_ok && tc::mbar_wait(&bars[B_AK + b], (g >> 1) & 1u);
+                const bool w_ok = tc::mbar_wait3(&bars[B_RFULL + s], (g / NS) & 1u, &bars[B_SFULL], g & 1u, &bars[B_AK + b], (g >> 1) & 1u);
                 tc::fence_after_sync();
                 uint32_t a0[8], a1[8], a2[8];
                 tc::ld_x8_u(tmem + lane_base + COL_S + 8 * half, a0);
@@ -708,11 +708,17 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                     const uint32_t pos = p.S + (r_begin + g) * (uint32_t) G + (uint32_t) tl;
                     const float kts = kt * sl2;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float C = i < 4 ? cp0[i] + cp0[i + 4] : cp1[i - 4] + cp1[i];
-                        // digit sums: |a0|, |a1| < 2^19, so a0 + 256 a1 is exact in s32
-                        const float S = fmaf(65536.0f, i2f(a2[i]), (float) ((int) a0[i] + ((int) a1[i] << 8)));
-                        s2[i] = pos < qlim[i] ? kts * fmaf(S, kinv[i], C) : -INFINITY;
+                    for (int i = 0; i < 8; i += 2) {                   // rows in pairs: packed fp32 arithmetic
+                        const float2 C = i < 4 ? add2(make_float2(cp0[i], cp0[i + 1]), make_float2(cp0[i + 4], cp0[i + 5]))
+                                               : add2(make_float2(cp1[i - 4], cp1[i - 3]), make_float2(cp1[i], cp1[i + 1]));
+                        // digit sums: |a0|, |a1| < 2^19, so a0 + 256 a1 is exact in s32; a2 through the magic constant
+                        const float2 hi = add2(make_float2(__uint_as_float(a2[i] + MAGIC_BITS), __uint_as_float(a2[i + 1] + MAGIC_BITS)),
+                                               make_float2(-MAGIC, -MAGIC));
+                        const float2 lo = make_float2((float) ((int) a0[i] + ((int) a1[i] << 8)), (float) ((int) a0[i + 1] + ((int) a1[i + 1] << 8)));
+                        const float2 S = fma2(make_float2(65536.0f, 65536.0f), hi, lo);
+                        const float2 v = mul2(make_float2(kts, kts), fma2(S, make_float2(kinv[i], kinv[i + 1]), C));
+                        s2[i] = pos < qlim[i] ? v.x : -INFINITY;
+                        s2[i + 1] = pos < qlim[i + 1] ? v.y : -INFINITY;
                     }
                     const float mw = warp_rows8<true>(s2, lane);
                     if ((lane & 3) == 0) F[F_RMAX + 64 * b + 32 * half + 8 * quarter + (lane >> 2)] = mw;
@@ -757,14 +763,21 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                     uint8_t * bv = sm + OFF_BV + b * 8 * BCH + b_off(8 * half, (tl & ~15) + pi_pos(tl & 15));
                     float ls[8], zs[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float pw = mnew[i] == -INFINITY ? 0.0f : ex2(s2[i] - mnew[i]);
-                        ls[i] = pw;
-                        zs[i] = pw * vz;
-                        const uint32_t z = digits3(pw * vsc, vscl[i]);
-                        bv[16 * i] = (uint8_t) z;
-                        bv[16 * i + 256] = (uint8_t) (z >> 8);
-                        bv[16 * i + 512] = (uint8_t) (z >> 16);
+                    for (int i = 0; i < 8; i += 2) {                   // rows in pairs: packed fp32 arithmetic
+                        const float2 d = add2(make_float2(s2[i], s2[i + 1]), make_float2(-mnew[i], -mnew[i + 1]));
+                        const float2 pw = make_float2(mnew[i] == -INFINITY ? 0.0f : ex2(d.x), mnew[i + 1] == -INFINITY ? 0.0f : ex2(d.y));
+                        ls[i] = pw.x;
+                        ls[i + 1] = pw.y;
+                        const float2 zz = mul2(pw, make_float2(vz, vz));
+                        zs[i] = zz.x;
+                        zs[i + 1] = zz.y;
+                        const uint2 z = digits3x2(mul2(pw, make_float2(vsc, vsc)), make_float2(vscl[i], vscl[i + 1]));
+                        bv[16 * i] = (uint8_t) z.x;
+                        bv[16 * i + 256] = (uint8_t) (z.x >> 8);
+                        bv[16 * i + 512] = (uint8_t) (z.x >> 16);
+                        bv[16 * i + 16] = (uint8_t) z.y;
+                        bv[16 * i + 16 + 256] = (uint8_t) (z.y >> 8);
+                        bv[16 * i + 16 + 512] = (uint8_t) (z.y >> 16);
                     }
                     tc::fence_proxy_async();
                     const float lw = warp_rows8<false>(ls, lane);
@@ -819,8 +832,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             const uint32_t b = g & 1u;
             // K MMAs of record g + 1, ahead of the V MMAs of record g
             if (g + 1 < n) {
-                ok = tc::mbar_wait(&bars[B_AK + (b ^ 1u)], ((g + 1) >> 1) & 1u);
-                if (ok) ok = tc::mbar_wait(&bars[B_SFREE], g & 1u);
+                ok = tc::mbar_wait2(&bars[B_AK + (b ^ 1u)], ((g + 1) >> 1) & 1u, &bars[B_SFREE], g & 1u);
                 if (!ok) break;
                 tc::fence_after_sync();
                 issue_k(g + 1);
@@ -835,9 +847,8 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
                 ++loaded;
                 if (loaded < n) next_blk = blk_of(loaded);
             }
-            ok = tc::mbar_wait(&bars[B_AV + b], (g >> 1) & 1u);
-            if (ok) ok = tc::mbar_wait(&bars[B_BV + b], (g >> 1) & 1u);
-            if (ok && g >= 2) ok = tc::mbar_wait(&bars[B_OFREE + b], ((g - 2) >> 1) & 1u);
+            ok = g >= 2 ? tc::mbar_wait3(&bars[B_AV + b], (g >> 1) & 1u, &bars[B_BV + b], (g >> 1) & 1u, &bars[B_OFREE + b], ((g - 2) >> 1) & 1u)
+                        : tc::mbar_wait2(&bars[B_AV + b], (g >> 1) & 1u, &bars[B_BV + b], (g >> 1) & 1u);
             if (!ok) break;
             tc::fence_after_sync();
             {
@@ -902,7 +913,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp) {
     const sj_kvarn_layout & l = v->lay;
     return l.D == 256 && l.G == 128 && l.body == SJKVARN_BODY_SCALAR && l.bits_k == 4 && l.bits_v == 4 &&
-           n_q * grp <= NR && l.bytes == REC_MAX;
+           n_q * grp <= NR && l.bytes == REC_MAX && l.k_scale % 16 == 0;
 }
 
 // Splits (persistent CTAs) per KV head: one CTA per SM over the call's KV heads, at most one per work item.

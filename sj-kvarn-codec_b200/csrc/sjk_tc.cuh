@@ -153,6 +153,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
     atomicExch(&sjk_dev_status, SJK_DEV_TIMEOUT);
     return false;
 }
+// non-blocking test of a phase (acquire at CTA scope when it reports completion)
+__device__ __forceinline__ bool mbar_test(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+                 : "=r"(ok)
+                 : "r"(smem_addr(bar)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+// wait for two / three phases: all are tested back to back, and only those not complete yet take the bounded
+// wait, so phases that completed earlier cost one round trip together instead of one each
+__device__ __forceinline__ bool mbar_wait2(uint64_t * b0, uint32_t p0, uint64_t * b1, uint32_t p1) {
+    const bool r0 = mbar_test(b0, p0), r1 = mbar_test(b1, p1);
+    return (r0 || mbar_wait(b0, p0)) && (r1 || mbar_wait(b1, p1));
+}
+__device__ __forceinline__ bool mbar_wait3(uint64_t * b0, uint32_t p0, uint64_t * b1, uint32_t p1, uint64_t * b2, uint32_t p2) {
+    const bool r0 = mbar_test(b0, p0), r1 = mbar_test(b1, p1), r2 = mbar_test(b2, p2);
+    return (r0 || mbar_wait(b0, p0)) && (r1 || mbar_wait(b1, p1)) && (r2 || mbar_wait(b2, p2));
+}
 // plain arrival (count 1) on an mbarrier, release semantics at CTA scope
 __device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
@@ -216,6 +235,51 @@ __device__ __forceinline__ float ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
+// Packed fp32 pairs (sm_100 f32x2 instructions): each lane computes both halves with the rounding of the
+// scalar instruction, so results are identical to two scalar operations at half the issue slots.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+// lane-wise max of two pairs of unsigned 16-bit values
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// Largest |x| over 256 consecutive fp16 values (16-byte aligned), for every lane of the warp: lane L reads
+// values 8L .. 8L + 7. The magnitude bits of finite values and infinities order like unsigned integers; a NaN
+// counts as infinity.
+__device__ __forceinline__ float absmax256_h(const uint8_t * p, int lane) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p + 16 * lane);
+    uint32_t m = max_u16x2(max_u16x2(w.x & 0x7FFF7FFFu, w.y & 0x7FFF7FFFu), max_u16x2(w.z & 0x7FFF7FFFu, w.w & 0x7FFF7FFFu));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = max_u16x2(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    uint32_t h = (m & 0xFFFFu) > (m >> 16) ? (m & 0xFFFFu) : (m >> 16);
+    h = h < 0x7C00u ? h : 0x7C00u;
+    return __half2float(__ushort_as_half((unsigned short) h));
+}
+
 // 8 consecutive floats of shared memory (16-byte aligned) into / from registers
 __device__ __forceinline__ void ld8(const float * p, float (&v)[8]) {
     const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
@@ -321,6 +385,12 @@ __device__ __forceinline__ float warp_sum_rows4(float v0, float v1, float v2, fl
 // to the bytes of x + 0x808080 (each in [0, 255]), and flipping bit 7 of each byte maps them back to signed.
 __device__ __forceinline__ uint32_t digits3(float v, float sc) {
     return (__float_as_uint(fmaf(v, sc, MAGIC)) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u;
+}
+// digits3 of two values (packed fp32 arithmetic, same results)
+__device__ __forceinline__ uint2 digits3x2(float2 v, float2 sc) {
+    const float2 f = fma2(v, sc, make_float2(MAGIC, MAGIC));
+    return make_uint2((__float_as_uint(f.x) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u,
+                      (__float_as_uint(f.y) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u);
 }
 
 }  // namespace num
