@@ -84,7 +84,7 @@ enum : uint32_t {                                             // offsets in floa
     F_KINV = 0,        // [2][16]       2^-e of the Q' rescale per buffer
     F_CPART = 32,      // [2][8][4]     zero-point partials per unpack warp (warps 2i, 2i+1: rows 4i..4i+3)
     F_QMAX = 96,       // [8][4]        per-unpack-warp row maxima of |q|
-    F_FREE = 128,      // [16]          (unused)
+    F_ROWOFF = 128,    // [16] (u32)    offset of each query row's partial in p.part
     F_M2 = 144,        // [2][16]       running max (log2 domain) after the record of each buffer
     F_ALPHA = 176,     // [3][16]       rescale of the running sums when record g arrived (slot g % 3)
     F_VINV = 224,      // [3][16]       2^-ev of the P' rescale (slot g % 3)
@@ -115,6 +115,7 @@ enum : uint32_t { DM_ROWP = 256, DM_NRM = 1280, DM_RED = 3328, DM_RED_L = 3584, 
 constexpr uint32_t OFF_DCODE = OFF_DM + DM_END;               // V codes of a chunk, [token][channel] bytes
 constexpr uint32_t OFF_DCENT = OFF_DCODE + 128 * 256;        // centroid (fp16 hi | lo) table, one copy per bank
 constexpr uint32_t SMEM_TOTAL = OFF_DCENT + 64 * 32 * 4;
+constexpr uint32_t OFF_XF = OFF_DCODE;                        // [16][256] outputs on their way out (after the staged rows)
 constexpr uint32_t DCOL_A = 0, DCOL_S = 256, DCOL_O = 320;   // dense TMEM: A (2 blocks x hi|lo), S (2 x 32), O (2 x 32)
 static_assert(128 * D_STG_F16 <= 2 * REC_MAX && 128 * D_STG_TQ6 <= 2 * REC_MAX, "staged rows fit in stages 1..2");
 static_assert(2 * TILE_H <= 2 * 16 * BCH, "[q hi | q lo] fits in the B_K area");
@@ -175,7 +176,12 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
         tc::mbar_fence_init();
     }
     if (tid < 2 * NR) F[F_M2 + tid] = -INFINITY;
-    if (tid < NR) F[F_LSUM + tid] = 0.0f;
+    if (tid < NR) {
+        F[F_LSUM + tid] = 0.0f;
+        const int iq = tid / p.grp, hq = hl * p.grp + tid % p.grp;
+        reinterpret_cast<uint32_t *>(F + F_ROWOFF)[tid] =
+            (uint32_t) (((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2));
+    }
     // staged-row chunk u of this head: first position, length, row format and the global K row of each token
     struct Chunk { uint32_t p0, len, side_off; bool f16, in_sink; };
     auto chunk_of = [&](uint32_t u) -> Chunk {
@@ -666,6 +672,11 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             if (ok) epilogue(e, e + 2 == n ? vc_m2 : vc_m1);
         }
         ok = tc::nbar_and(1, NW * 32, ok);
+        {                                                      // the outputs go out through shared memory
+            float * xf = reinterpret_cast<float *>(sm + OFF_XF);
+#pragma unroll
+            for (int r = 0; r < NR; ++r) xf[r * D + 128 * half + tl] = acc[r];
+        }
         if (lane == 0) F[F_OK] = ok ? 1.0f : 0.0f;             // (read after the CTA barrier below)
     } else if (warp < 2 * NW) {
         // ===== softmax: scores and weights of record g, B_V digits, row sums; the unpack warps run the epilogue =====
@@ -879,26 +890,20 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     // ---- partials (m in the natural-log domain, l, o[D]) per real query row, valid only if every role finished ----
     {
         const bool all_ok = F[F_OK] != 0.0f && F[F_OK + 1] != 0.0f && F[F_OK + 2] != 0.0f && ok;
-        if (warp < NW) {                                       // unpack warps hold the outputs: channel 128 half + tl
-            const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;
-#pragma unroll
-            for (int r = 0; r < NR; ++r) {
-                if (r < p.rows) {
-                    const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                    float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
-                    dst[2 + 128 * half + tl] = all_ok ? acc[r] : 0.0f;
-                }
-            }
-        } else if (warp < 2 * NW && tid - NW * 32 < NR) {      // one thread per row: m and l
-            const int r = tid - NW * 32;
-            if (r < p.rows) {
-                const uint32_t mb = n >= 1 ? (n - 1) & 1u : 1u;
-                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
-                const float m2 = F[F_M2 + 16 * mb + r];
-                dst[0] = all_ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
-                dst[1] = all_ok ? F[F_LSUM + r] : 0.0f;
-            }
+        const uint32_t * rowoff = reinterpret_cast<const uint32_t *>(F + F_ROWOFF);
+        const float * xf = reinterpret_cast<const float *>(sm + OFF_XF);
+        for (int i = tid; i < p.rows * (D / 2); i += NT) {     // outputs: pairs of channels, coalesced
+            const int r = i / (D / 2), c = 2 * (i % (D / 2));
+            const float2 v = all_ok ? make_float2(xf[r * D + c], xf[r * D + c + 1]) : make_float2(0.0f, 0.0f);
+            *reinterpret_cast<float2 *>(p.part + rowoff[r] + 2 + c) = v;
+        }
+        if (tid < p.rows) {                                    // m and l
+            const int r = tid;
+            const uint32_t mb = n >= 1 ? (n - 1) & 1u : 1u;
+            const float m2 = F[F_M2 + 16 * mb + r];
+            float * dst = p.part + rowoff[r];
+            dst[0] = all_ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
+            dst[1] = all_ok ? F[F_LSUM + r] : 0.0f;
         }
     }
     if (warp == 2 * NW) tc::tmem_dealloc(tmem, TM_COLS);
