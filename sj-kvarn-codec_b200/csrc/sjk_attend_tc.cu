@@ -54,6 +54,10 @@ struct TcParams {
     uint32_t n_rec;             // sealed records per head in [S, B)
     uint32_t qpos0;
     int n_q, n_head, grp, rows;
+    // query row r (r < rows) of the KV head's group: position iq = r / grp, query head hl grp + r % grp; the
+    // divisions are done once on the host
+    uint32_t row_iq[NR];        // r / grp
+    int row_q[NR];              // iq n_head + r % grp: q row (and partial row) of r, less hl grp
     const float * q;
     float scale;
     float * part;               // [splits][n_q*n_head][D + 2]
@@ -178,9 +182,8 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     if (tid < 2 * NR) F[F_M2 + tid] = -INFINITY;
     if (tid < NR) {
         F[F_LSUM + tid] = 0.0f;
-        const int iq = tid / p.grp, hq = hl * p.grp + tid % p.grp;
         reinterpret_cast<uint32_t *>(F + F_ROWOFF)[tid] =
-            (uint32_t) (((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2));
+            (uint32_t) (((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) (p.row_q[tid] + hl * p.grp)) * (D + 2));
     }
     // staged-row chunk u of this head: first position, length, row format and the global K row of each token
     struct Chunk { uint32_t p0, len, side_off; bool f16, in_sink; };
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = r0 + i, rr = r < p.rows ? r : 0;
-            qx[i] = tid < 512 ? __ldg(qg + ((size_t) (rr / p.grp) * p.n_head + hl * p.grp + rr % p.grp) * D + d) : 0.0f;
+            qx[i] = tid < 512 ? __ldg(qg + (size_t) (p.row_q[rr] + hl * p.grp) * D + d) : 0.0f;
         }
     }
     tc::fence_before_sync();
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int r = 4 * grp + i;
-            qlim4[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
+            qlim4[i] = r < p.rows ? p.qpos0 + p.row_iq[r] + 1u : 0u;
         }
         uint32_t dphase = 0;
         bool d_pending = false;
@@ -523,8 +526,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) qv[i][j] = 0.0f;
             if (r < p.rows) {
-                const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-                const float * qr = p.q + ((size_t) iq * p.n_head + hq) * D;
+                const float * qr = p.q + (size_t) (p.row_q[r] + hl * p.grp) * D;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) qv[i][j] = qr[kch[j]];
             }
@@ -689,7 +691,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = 8 * half + i;
-            qlim[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
+            qlim[i] = r < p.rows ? p.qpos0 + p.row_iq[r] + 1u : 0u;
         }
         for (uint32_t g = 0; g <= n; ++g) {                      // pass n only finishes record n - 1
             const uint32_t b = g & 1u, pb = b ^ 1u, s3 = g % 3u, ps3 = (g + 2u) % 3u;   // ps3: slot of record g - 1
@@ -937,6 +939,11 @@ int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_re
     TcParams p;
     p.lay = v->lay; p.body = v->body; p.blocks = v->blocks; p.H = v->n_head_kv; p.kv0 = kv0; p.S = v->S;
     p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
+    for (int r = 0; r < NR; ++r) {
+        const int iq = r < p.rows ? r / p.grp : 0, g = r < p.rows ? r % p.grp : 0;
+        p.row_iq[r] = (uint32_t) iq;
+        p.row_q[r] = iq * n_head + g;
+    }
     p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
     p.sink = v->sink; p.ring = v->ring; p.staging = v->staging; p.sink_type = v->sink_type; p.cap = v->cap;
     p.stage_bytes = (uint32_t) v->stage_bytes; p.B = B; p.N = N;
