@@ -237,6 +237,8 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // launched as a programmatic dependent of the kernels that write the partials: wait until they completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the outputs of the first MERGE_PRE splits of this thread's group go in flight with the (m, l) loads
     const int dl = tid & 63, grp4 = tid >> 6;
     const bool live = d0 + dl < D;
@@ -416,8 +418,20 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
         if (sjk_check(e)) return SJK_ERR_DEVICE;
         if (sjk_check_launch()) return SJK_ERR_DEVICE;
     }
-    attend_merge_kernel<<<dim3((unsigned) (n_q * n_head), (unsigned) ((v->lay.D + 63) / 64)), 256,
-                          (size_t) (splits + 256) * sizeof(float), st>>>(p.part, splits, n_q * n_head, v->lay.D, out);
+    // programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them
+    // on the device (griddepcontrol.wait), so the launch gap between the two kernels disappears
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) (n_q * n_head), (unsigned) ((v->lay.D + 63) / 64));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t) (splits + 256) * sizeof(float);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, (const float *) p.part, splits, n_q * n_head, v->lay.D, out)))
+        return SJK_ERR_DEVICE;
     return sjk_check_launch();
 }
 

@@ -222,6 +222,8 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // the merge kernel that follows may be launched now; it waits for this grid on the device
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
     float acc[NR];                                      // softmax warps: running output of their channel, all rows
