@@ -933,7 +933,7 @@ int sjk_tc_body_max_splits(int n_kv) {
 
 // A staged-row chunk costs about DENSE_WEIGHT sealed records of CTA time; the record ranges are balanced so that
 // the CTAs that also take a chunk get fewer records.
-constexpr double DENSE_WEIGHT = 2.0;
+constexpr double DENSE_WEIGHT = 4.5;
 
 int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int with_dense, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
