@@ -296,6 +296,58 @@ def run_seal(args, torch, L, stream_obj):
     return dict(ms=ms, ms_store=ms_store, records=(B1 - B0) // 128 * 4)
 
 
+CFG2 = dict(LAYERS=4, N=32768, TAIL=4096, TAIL_MAX=8192, N_UB=512)
+
+
+def run_config2(args, torch, L, stream_obj):
+    """BASELINE config 2 (3/2 trellis): the per-layer seal of one 4096-token commit, and decode attention at 32K
+    context (B = 28,672 after idling at 32,768, tail 4,096). K is Student-t(4) before the channel scales. The
+    attention metric is per layer call, so 4 layers stand in for the model's 16."""
+    import sjk
+    import synth
+    st = C.c_void_p(stream_obj.cuda_stream)
+    c, c2 = CFG1, CFG2
+    t0 = time.time()
+    m = GpuModel(torch, L, seed=2, stream=st, layers=c2["LAYERS"], n_ctx=c2["N"] + 1024, bits=(3, 2), body=2, heavy=True)
+    m.grow(c2["N"])
+    m.idle(0)
+    torch.cuda.synchronize()
+    B, N = m.pol.B, c2["N"]
+    assert B == 28672, B
+    build_s = time.time() - t0
+    n_q, n_head, D = c["NQ"], c["HQ"], c["D"]
+    q = torch.from_numpy(synth.queries(2, c2["LAYERS"], n_q, n_head, D)).cuda()
+    out = torch.empty_like(q)
+    per = n_q * n_head * D
+
+    def step():
+        for il, lay in enumerate(m.layers):
+            rc = L.sjk_layer_attend(C.byref(lay), B, N, N - n_q, n_q, n_head, C.c_void_p(q.data_ptr() + il * per * 4),
+                                    SCALE, C.c_void_p(out.data_ptr() + il * per * 4), st)
+            if rc:
+                raise sjk.SjkError(rc, "attend")
+
+    ms = time_events(torch, stream_obj, step, max(3, args.steps), args.warmup)
+    m.free()
+    # the seal of one 4096-token commit (32 groups x 4 heads, 3/2 trellis) out of an 8,320-position ring
+    ms_seal = None
+    s = GpuModel(torch, L, seed=2, stream=st, layers=1, n_ctx=16384, bits=(3, 2), body=2, heavy=True)
+    s.grow(8320)
+    s.L.sj_kvarn_policy_begin_ubatch(C.byref(s.pol), 8320, 512)
+    B0, B1 = s.pol.B, s.pol.B_pending
+    lay = s.layers[0]
+
+    def seal():
+        rc = L.sjk_layer_seal(C.byref(lay), B0, B1, st)
+        if rc:
+            raise sjk.SjkError(rc, "seal")
+
+    ms_seal = time_events(torch, stream_obj, seal, 3, 1)
+    s.free()
+    abytes = attn_bytes_per_call(B, N, rec_bytes=22784)
+    return dict(ms=ms / c2["LAYERS"], B=B, N=N, bytes=abytes, ms_seal=ms_seal, records=(B1 - B0) // 128 * 4, build_s=build_s)
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # reference CPU path (oracle/_ref: the reference sj_kvarn.h compiled from its own source)
 # ---------------------------------------------------------------------------------------------------------------
@@ -463,6 +515,7 @@ def main():
     ap.add_argument("--cpu-threads", type=int, default=0, help="host threads for the CPU reference (0 = all)")
     ap.add_argument("--ref-pairs", type=int, default=16, help="(row, head) pairs per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config2", action="store_true", help="skip the config-2 (3/2 trellis) side measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -489,6 +542,7 @@ def main():
         dist = td
     res = run_gpu_arm(args, torch, dist, rank, world, local_rank)
     seal = run_seal(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 else None
+    cfg2 = run_config2(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 and not args.no_config2 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -539,6 +593,15 @@ def main():
                  "hbm_gbs": seal_bytes / (seal["ms"] * 1e-3) / 1e9, "hbm_frac": seal_bytes / (seal["ms"] * 1e-3) / 1e9 / peak,
                  "ring_write_ms": seal["ms_store"],
                  "ring_write_gbs": store_bytes / (seal["ms_store"] * 1e-3) / 1e9},
+        "config2": None if cfg2 is None else {
+            "workload": "config 2: 3/2 trellis body, decode attention at 32K ctx (B = 28,672, tail 4,096), per layer call; "
+                        "seal of one 4096-token commit (128 records, 1 layer)",
+            "attn_us_per_call": cfg2["ms"] * 1e3, "attn_bytes_per_call": cfg2["bytes"],
+            "attn_gbs": cfg2["bytes"] / (cfg2["ms"] * 1e-3) / 1e9, "attn_frac": cfg2["bytes"] / (cfg2["ms"] * 1e-3) / 1e9 / peak,
+            "seal_mtoks": 4096 / (cfg2["ms_seal"] * 1e-3) / 1e6, "seal_ms": cfg2["ms_seal"],
+            "seal_hbm_frac": cfg2["records"] * (128 * 392 + 22784) / (cfg2["ms_seal"] * 1e-3) / 1e9 / peak,
+            "kernel": "attend_trellis_tc_kernel (sealed records) + attend_dense_tc_kernel (sink + staging ring) + attend_merge_kernel",
+            "build_s": cfg2["build_s"]},
         "cpu_baseline": cpu,
         "build_s": res["build_s"],
     }

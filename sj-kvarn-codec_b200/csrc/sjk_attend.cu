@@ -361,9 +361,10 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     // the staged-row formats, the same kernel takes the sink and the staging ring, else the dense kernel does
     const uint32_t b_end = B < N ? B : N;
     const bool tc_body = sjk_tc_body_supported(v, n_q, grp) != 0;
+    const bool tc_trellis = !tc_body && sjk_tc_trellis_supported(v, n_q, grp) != 0;
     const bool dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
     const bool fused = tc_body && dense;
-    const uint32_t n_tc = (tc_body && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
+    const uint32_t n_tc = ((tc_body || tc_trellis) && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
     uint32_t n_sink_d = 0, n_dense = 0;
     if (dense && !fused) {
         const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
@@ -375,14 +376,18 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense);
     const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
     // the tensor-core kernel's split count is known after its launch plan; bound it for the scratch check
-    const int splits_tc_max = (tc_body && (n_tc > 0 || fused)) ? sjk_tc_body_max_splits(n_kv) : 0;
+    const int splits_tc_max = (tc_body && (n_tc > 0 || fused)) ? sjk_tc_body_max_splits(n_kv)
+                              : (tc_trellis && n_tc > 0)      ? sjk_tc_trellis_max_splits(n_kv)
+                                                              : 0;
     const size_t need = (size_t) (splits_tc_max + splits_d + splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
     if (splits_tc_max + splits_d + splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
     int splits_tc = 0;
     if (splits_tc_max) {
-        const int rc = sjk_tc_body_launch(v, B, N, n_tc, fused ? 1 : 0, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
-                                          (float *) scratch, 0, &splits_tc, st);
+        const int rc = tc_body ? sjk_tc_body_launch(v, B, N, n_tc, fused ? 1 : 0, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
+                                                    (float *) scratch, 0, &splits_tc, st)
+                               : sjk_tc_trellis_launch(v, B, N, n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
+                                                       (float *) scratch, 0, &splits_tc, st);
         if (rc) return rc;
     }
     const int splits = splits_tc + splits_d + splits_v1;
@@ -438,9 +443,9 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
 // status words of every kernel with bounded waits: 1 if any wait ran out since the last call
 extern "C" int sjk_device_status(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
-    const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take();
-    if (a < 0 || b < 0) return -1;
-    return a | b;
+    const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take(), c = sjk_tc_trellis_status_take();
+    if (a < 0 || b < 0 || c < 0) return -1;
+    return a | b | c;
 }
 
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
