@@ -348,6 +348,68 @@ def run_config2(args, torch, L, stream_obj):
     return dict(ms=ms / c2["LAYERS"], B=B, N=N, bytes=abytes, ms_seal=ms_seal, records=(B1 - B0) // 128 * 4, build_s=build_s)
 
 
+CFG4 = dict(LAYERS=2, GROUPS=8192, TAIL=4096)
+
+
+def run_config4(args, torch, L, stream_obj, dist, rank, world):
+    """one sequence of 1,048,576 sealed tokens (8,192 groups per KV head and layer) plus the
+    128-token sink and a 4,096-token tail, split by context slice across the ranks. Rank r holds groups
+    [8192 r / W, 8192 (r + 1) / W) of every layer; rank 0 also holds the sink, the last rank the tail. Per layer
+    call every rank attends over its own regions (sjk_attend_partial), the (m, l, o) triples are all-gathered
+    over NCCL and merged in rank order (sjk_attend_merge); every rank ends with the whole output. The metric is
+    per layer call, so 2 layers stand in for 16. Each rank's slice holds its own seeded synthetic K/V."""
+    import sjk
+    import slices
+    import synth
+    st = C.c_void_p(stream_obj.cuda_stream)
+    c, c4 = CFG1, CFG4
+    g0, g1 = slices.group_range(rank, world, c4["GROUPS"])
+    n_local = c["SINK"] + (g1 - g0) * 128 + c4["TAIL"]
+    t0 = time.time()
+    m = GpuModel(torch, L, seed=4000 + rank, stream=st, layers=c4["LAYERS"], n_ctx=n_local + 1024)
+    m.grow(n_local)
+    m.idle(c4["TAIL"])
+    torch.cuda.synchronize()
+    B = m.pol.B
+    assert B == c["SINK"] + (g1 - g0) * 128, B
+    build_s = time.time() - t0
+    n_q, n_head, D = c["NQ"], c["HQ"], c["D"]
+    n_global = c["SINK"] + c4["GROUPS"] * 128 + c4["TAIL"]
+    qpos0 = n_global - n_q
+    rows, per = n_q * n_head, n_q * n_head * D
+    q = torch.from_numpy(synth.queries(4, c4["LAYERS"], n_q, n_head, D)).cuda()
+    out = torch.empty_like(q)
+    views = [sjk.view_of(lay) for lay in m.layers]
+    need = L.sjk_attend_scratch_bytes(C.byref(views[0]), n_local, n_q, n_head)
+    scratch = torch.empty(int(need), dtype=torch.uint8, device="cuda")
+    part = torch.empty((rows, D + 2), dtype=torch.float32, device="cuda")
+    reg = slices.regions(rank, world)
+
+    def step():
+        with torch.cuda.stream(stream_obj):
+            for il in range(c4["LAYERS"]):
+                rc = L.sjk_attend_partial(C.byref(views[il]), B, n_local, qpos0, n_q, n_head, reg,
+                                          C.c_void_p(q.data_ptr() + il * per * 4), SCALE, C.c_void_p(part.data_ptr()),
+                                          C.c_void_p(scratch.data_ptr()), need, st)
+                if rc:
+                    raise sjk.SjkError(rc, "attend_partial")
+                allp = slices.gather(dist, part) if dist else part[None]
+                rc = L.sjk_attend_merge(C.c_void_p(allp.data_ptr()), world, rows, D, C.c_void_p(out.data_ptr() + il * per * 4), st)
+                if rc:
+                    raise sjk.SjkError(rc, "attend_merge")
+
+    barrier = (lambda: dist.barrier()) if dist else None
+    ms = time_events(torch, stream_obj, step, max(3, args.steps), args.warmup, barrier)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    m.free()
+    B_global = c["SINK"] + c4["GROUPS"] * 128
+    return dict(ms=ms / c4["LAYERS"], bytes=attn_bytes_per_call(B_global, n_global), n_ctx=n_global, build_s=build_s,
+                exchange=rows * (D + 2) * 4, groups_per_rank=g1 - g0)
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # reference CPU path (oracle/_ref: the reference sj_kvarn.h compiled from its own source)
 # ---------------------------------------------------------------------------------------------------------------
@@ -516,6 +578,7 @@ def main():
     ap.add_argument("--ref-pairs", type=int, default=16, help="(row, head) pairs per reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config2", action="store_true", help="skip the config-2 (3/2 trellis) side measurement")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 (1M context sliced over the ranks) measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -541,6 +604,7 @@ def main():
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
         dist = td
     res = run_gpu_arm(args, torch, dist, rank, world, local_rank)
+    cfg4 = None if args.no_config4 else run_config4(args, torch, sjk.lib(), torch.cuda.Stream(), dist, rank, world)
     seal = run_seal(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 else None
     cfg2 = run_config2(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 and not args.no_config2 else None
 
@@ -602,6 +666,14 @@ def main():
             "seal_hbm_frac": cfg2["records"] * (128 * 392 + 22784) / (cfg2["ms_seal"] * 1e-3) / 1e9 / peak,
             "kernel": "attend_trellis_tc_kernel (sealed records) + attend_dense_tc_kernel (sink + staging ring) + attend_merge_kernel",
             "build_s": cfg2["build_s"]},
+        "config4": None if cfg4 is None else {
+            "workload": "config 4: one 1,048,576-token sequence (+ 128 sink, 4,096 tail), 4/4, split by context slice over "
+                        f"{world} rank(s); per layer call: partial attention per rank + NCCL all-gather of (m, l, o) + merge",
+            "attn_us_per_call": cfg4["ms"] * 1e3, "attn_bytes_per_call": cfg4["bytes"], "n_ctx": cfg4["n_ctx"],
+            "attn_gbs": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9,
+            "attn_frac_of_all_ranks": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9 / (peak * world),
+            "groups_per_rank": cfg4["groups_per_rank"], "exchange_bytes_per_rank": cfg4["exchange"],
+            "scaling": "strong (fixed sequence)", "build_s": cfg4["build_s"]},
         "cpu_baseline": cpu,
         "build_s": res["build_s"],
     }

@@ -340,6 +340,18 @@ size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_h
 int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
                float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st);
 
+/* Attention split by context (a single long sequence sliced across GPUs, sj_kvarn.h:1535-1564 computed piecewise):
+ * sjk_attend_partial attends over the regions selected by `regions` and returns one partial per
+ * (query row, query head): part_out[n_q * n_head][D + 2] = (m, l, o[D]), with m the running max of the scaled
+ * scores (natural log), l the sum of exp(score - m) and o the V rows weighted by exp(score - m), not normalized.
+ * sjk_attend_merge combines n_parts such partial sets, parts[n_parts][n_rows][D + 2], in index order into
+ * out[n_rows][D]; partials of disjoint position sets combine to the attention over their union. No
+ * counterpart in the reference, whose attention runs over one cache on one device. */
+enum { SJK_REGION_SINK = 1, SJK_REGION_BODY = 2, SJK_REGION_RING = 4, SJK_REGION_ALL = 7 };
+int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, unsigned regions,
+                       const float * q, float scale, float * part_out, void * scratch, size_t scratch_bytes, sjk_stream st);
+int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st);
+
 /* sjk_attend for callers that cannot allocate device memory - code that runs where cudaMalloc is off
  * limits, such as inside a stream capture, a custom allocator's own callbacks or an engine whose memory
  * is planned ahead. No counterpart in the reference. The scratch for the split partials is a fixed 16 MiB

@@ -232,7 +232,10 @@ __global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
 constexpr int MERGE_SPLITS = 768;                     // >= the most splits a call can make (148 + 296 + 296)
 constexpr int MERGE_PRE = 24;                         // outputs per thread loaded ahead of the weights
 
-__global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out) {
+// part_out (optional): instead of out, write the combined partial (m, l, o[D]) of each row (o not normalized), the
+// form sjk_attend_partial returns
+__global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out,
+                                                           float * part_out) {
     extern __shared__ float wts[];                     // [splits] weights, then [4][64] partial sums
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
@@ -297,8 +300,12 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     float * acc = wts + splits;
     acc[grp4 * 64 + dl] = o;
     __syncthreads();
-    if (tid < 64 && d0 + tid < D)
+    if (part_out) {
+        if (tid < 64 && d0 + tid < D) part_out[(size_t) row * (D + 2) + 2 + d0 + tid] = (acc[tid] + acc[64 + tid]) + (acc[128 + tid] + acc[192 + tid]);
+        if (blockIdx.y == 0 && tid == 0) { part_out[(size_t) row * (D + 2)] = m; part_out[(size_t) row * (D + 2) + 1] = t; }
+    } else if (tid < 64 && d0 + tid < D) {
         out[(size_t) row * D + d0 + tid] = ((acc[tid] + acc[64 + tid]) + (acc[128 + tid] + acc[192 + tid])) * s_inv;
+    }
 }
 
 struct Plan { int splits, chunks_per_split, n_chunks; uint32_t n_sink, n_body; };
@@ -312,16 +319,16 @@ int split_target(int n_kv) {
 
 // chunks left to the CUDA-core kernel: the body after the first body_skip records, plus the sink and the
 // staging ring unless the dense tensor-core kernel takes them (no_staged)
-Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip, bool no_staged) {
+Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip, bool no_staged, unsigned regions) {
     Plan pl;
     const uint32_t S = v->S;
     const uint32_t s_end = S < N ? S : N;
-    pl.n_sink = no_staged ? 0u : (s_end + 127u) / 128u;
+    pl.n_sink = (no_staged || !(regions & SJK_REGION_SINK)) ? 0u : (s_end + 127u) / 128u;
     const uint32_t b_end = B < N ? B : N;
-    pl.n_body = b_end > S ? (b_end - S + 127u) / 128u : 0u;
+    pl.n_body = (b_end > S && (regions & SJK_REGION_BODY)) ? (b_end - S + 127u) / 128u : 0u;
     pl.n_body = pl.n_body > body_skip ? pl.n_body - body_skip : 0u;
     const uint32_t t0 = B > S ? B : S;
-    const uint32_t n_tail = (N > t0 && !no_staged) ? (N - t0 + 127u) / 128u : 0u;
+    const uint32_t n_tail = (N > t0 && !no_staged && (regions & SJK_REGION_RING)) ? (N - t0 + 127u) / 128u : 0u;
     pl.n_chunks = (int) (pl.n_sink + pl.n_body + n_tail);
     const int target = split_target(n_kv);
     pl.chunks_per_split = (pl.n_chunks + target - 1) / target;
@@ -350,8 +357,9 @@ extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n
 }
 
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
-                     const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
-    if (!v || !q || !out || n_q <= 0 || n_head <= 0 || n_kv <= 0 || kv_head0 < 0 || kv_head0 + n_kv > v->n_head_kv ||
+                     const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
+                     unsigned regions, float * part_out) {
+    if (!v || !q || !(out || part_out) || n_q <= 0 || n_head <= 0 || n_kv <= 0 || kv_head0 < 0 || kv_head0 + n_kv > v->n_head_kv ||
         n_head % n_kv)
         return SJKVARN_ERR_ARG;
     if (B < v->S) return SJKVARN_ERR_ARG;
@@ -364,19 +372,21 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     const bool tc_trellis = !tc_body && sjk_tc_trellis_supported(v, n_q, grp) != 0;
     const bool dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
     const bool fused = tc_body && dense;
-    const uint32_t n_tc = ((tc_body || tc_trellis) && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
+    const bool body_on = (regions & SJK_REGION_BODY) != 0;
+    const uint32_t n_tc = ((tc_body || tc_trellis) && body_on && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
+    const unsigned staged = regions & (SJK_REGION_SINK | SJK_REGION_RING);
     uint32_t n_sink_d = 0, n_dense = 0;
     if (dense && !fused) {
         const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
-        n_sink_d = (s_end + 127u) / 128u;
-        n_dense = n_sink_d + (N > t0 ? (N - t0 + 127u) / 128u : 0u);
+        n_sink_d = (regions & SJK_REGION_SINK) ? (s_end + 127u) / 128u : 0u;
+        n_dense = n_sink_d + ((regions & SJK_REGION_RING) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
     }
     int cps_d = 1;
     const int splits_d = (dense && !fused) ? sjk_tc_dense_splits(n_dense, n_kv, &cps_d) : 0;
-    const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense);
+    const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense, regions);
     const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
     // the tensor-core kernel's split count is known after its launch plan; bound it for the scratch check
-    const int splits_tc_max = (tc_body && (n_tc > 0 || fused)) ? sjk_tc_body_max_splits(n_kv)
+    const int splits_tc_max = (tc_body && (n_tc > 0 || (fused && staged))) ? sjk_tc_body_max_splits(n_kv)
                               : (tc_trellis && n_tc > 0)      ? sjk_tc_trellis_max_splits(n_kv)
                                                               : 0;
     const size_t need = (size_t) (splits_tc_max + splits_d + splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
@@ -384,14 +394,16 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (splits_tc_max + splits_d + splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
     int splits_tc = 0;
     if (splits_tc_max) {
-        const int rc = tc_body ? sjk_tc_body_launch(v, B, N, n_tc, fused ? 1 : 0, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
+        const unsigned dense_regions = fused ? ((regions & SJK_REGION_SINK) ? 1u : 0u) | ((regions & SJK_REGION_RING) ? 2u : 0u) : 0u;
+        const int rc = tc_body ? sjk_tc_body_launch(v, B, N, n_tc, (int) dense_regions, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
                                                     (float *) scratch, 0, &splits_tc, st)
                                : sjk_tc_trellis_launch(v, B, N, n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
                                                        (float *) scratch, 0, &splits_tc, st);
         if (rc) return rc;
     }
     const int splits = splits_tc + splits_d + splits_v1;
-    if (splits == 0) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
+    // nothing to attend to: a zero output; an empty partial (m = -inf, l = 0, o = 0) comes from the merge kernel
+    if (splits == 0 && !part_out) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
     if (splits_d) {
         const int rc = sjk_tc_dense_launch(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch,
                                            splits_tc, splits_d, n_sink_d, n_dense, cps_d, st);
@@ -435,8 +447,26 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, (const float *) p.part, splits, n_q * n_head, v->lay.D, out)))
+    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, (const float *) p.part, splits, n_q * n_head, v->lay.D, out, part_out)))
         return SJK_ERR_DEVICE;
+    return sjk_check_launch();
+}
+
+// Attention over a subset of the regions, as one partial (m, l, o[D]) per (query row, query head). The
+// partials of disjoint region sets, or of context slices held by different GPUs, combine with sjk_attend_merge.
+extern "C" int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                                  unsigned regions, const float * q, float scale, float * part_out, void * scratch,
+                                  size_t scratch_bytes, sjk_stream st) {
+    if (!v || !part_out || (regions & ~(unsigned) SJK_REGION_ALL)) return SJKVARN_ERR_ARG;
+    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, nullptr, scratch, scratch_bytes, st,
+                            regions, part_out);
+}
+
+// out[n_rows][D] from n_parts partial sets parts[n_parts][n_rows][D + 2], combined in index order
+extern "C" int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st) {
+    if (!parts || !out || n_parts <= 0 || n_rows <= 0 || D <= 0 || n_parts > MERGE_SPLITS) return SJKVARN_ERR_ARG;
+    attend_merge_kernel<<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
+        parts, n_parts, n_rows, D, out, nullptr);
     return sjk_check_launch();
 }
 
@@ -451,7 +481,8 @@ extern "C" int sjk_device_status(void) {
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
                           float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
     if (!v) return SJKVARN_ERR_ARG;
-    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st);
+    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st,
+                            SJK_REGION_ALL, nullptr);
 }
 
 // ---- attention for callers that cannot allocate ------------------------------------------------------------
@@ -488,5 +519,6 @@ extern "C" int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uin
             g_static_ptr[dev] = ptr;
         }
     }
-    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, ptr, SJK_STATIC_SCRATCH_BYTES, st);
+    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, ptr, SJK_STATIC_SCRATCH_BYTES, st,
+                            SJK_REGION_ALL, nullptr);
 }

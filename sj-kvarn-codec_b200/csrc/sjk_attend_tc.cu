@@ -935,7 +935,7 @@ int sjk_tc_body_max_splits(int n_kv) {
 // the CTAs that also take a chunk get fewer records.
 constexpr double DENSE_WEIGHT = 4.5;
 
-int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int with_dense, uint32_t qpos0, int n_q,
+int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                        sjk_stream st) {
     TcParams p;
@@ -950,10 +950,10 @@ int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_re
     p.sink = v->sink; p.ring = v->ring; p.staging = v->staging; p.sink_type = v->sink_type; p.cap = v->cap;
     p.stage_bytes = (uint32_t) v->stage_bytes; p.B = B; p.N = N;
     p.n_sink_chunks = 0; p.n_dense = 0;
-    if (with_dense) {
+    if (dense_regions) {
         const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
-        p.n_sink_chunks = (s_end + 127u) / 128u;
-        p.n_dense = p.n_sink_chunks + (N > t0 ? (N - t0 + 127u) / 128u : 0u);
+        p.n_sink_chunks = (dense_regions & 1) ? (s_end + 127u) / 128u : 0u;
+        p.n_dense = p.n_sink_chunks + ((dense_regions & 2) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
     }
     const uint32_t items = n_rec + p.n_dense;
     int splits = sjk_tc_body_max_splits(n_kv);

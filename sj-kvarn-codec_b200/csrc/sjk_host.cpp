@@ -417,7 +417,8 @@ extern "C" void sj_kvarn_layer_attend_row(const sj_kvarn_layer * L, uint32_t B, 
                                           uint32_t qpos, float scale, float * out_rot) {
     sjk_view vw;
     sjk_layer_view(L, &vw);
-    sticky(sjk_attend_heads(&vw, B, N, qpos, 1, 1, h, 1, q_rot, scale, out_rot, L->work, L->work_bytes, L->stream));
+    sticky(sjk_attend_heads(&vw, B, N, qpos, 1, 1, h, 1, q_rot, scale, out_rot, L->work, L->work_bytes, L->stream,
+                            SJK_REGION_ALL, nullptr));
 }
 
 extern "C" uint8_t * sj_kvarn_layer_record(const sj_kvarn_layer * L, uint32_t g, int h) {

@@ -8,21 +8,23 @@ void sjk_set_cuda_error(cudaError_t e);
 void sjk_set_sticky(int status);
 
 // attention over KV heads [kv_head0, kv_head0 + n_kv) only (query heads kv*grp.. of those)
+// regions: SJK_REGION_* mask of the positions attended to; part_out: when not null, the combined partial
+// (m, l, o[D]) per (query row, query head) instead of the normalized output
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0,
                      int n_kv, const float * q, float scale, float * out, void * scratch, size_t scratch_bytes,
-                     sjk_stream st);
+                     sjk_stream st, unsigned regions, float * part_out);
 size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv);
 // decode the K and V rows of position pos, KV head h, to k[D], v[D] (device)
 int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, float * vo, sjk_stream st);
 // decode row t of one record (is_v selects V) to out[D] (device)
 int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st);
 
-// tensor-core attention over the sealed body of a 4-bit scalar layer (sjk_attend_tc.cu); with_dense: the same
-// CTAs also take the staged rows (sink and staging ring, formats of sjk_tc_dense_supported). *splits_out gets the
+// tensor-core attention over the sealed body of a 4-bit scalar layer (sjk_attend_tc.cu); dense_regions: the same
+// CTAs also take the staged rows (bit 0 the sink, bit 1 the staging ring; formats of sjk_tc_dense_supported). *splits_out gets the
 // number of partial slots per query row the launch writes (from split0).
 int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp);
 int sjk_tc_body_max_splits(int n_kv);
-int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int with_dense, uint32_t qpos0, int n_q,
+int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                        sjk_stream st);
 

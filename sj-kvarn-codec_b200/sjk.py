@@ -136,6 +136,8 @@ SIGNATURES = {
     "sjk_attend_scratch_bytes": (C.c_size_t, [P(View), u32, C.c_int, C.c_int]),
     "sjk_attend": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp, C.c_size_t, vp]),
     "sjk_attend_static": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
+    "sjk_attend_partial": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, C.c_uint, vp, C.c_float, vp, vp, C.c_size_t, vp]),
+    "sjk_attend_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, vp]),
     "sjk_layer_store": (C.c_int, [P(Layer), u32, u32, vp, vp, C.c_int, vp]),
     "sjk_layer_seal": (C.c_int, [P(Layer), u32, u32, vp]),
     "sjk_layer_attend": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
@@ -193,6 +195,10 @@ def config(head_dim=256, n_head_kv=4, n_ctx=16384, n_ubatch=512, **kw):
     for k, v in kw.items():
         setattr(c, k, v)
     return c
+
+
+# region mask of sjk_attend_partial (include/sjk.h)
+REGION_SINK, REGION_BODY, REGION_RING, REGION_ALL = 1, 2, 4, 7
 
 
 def view_of(layer):

@@ -1,0 +1,64 @@
+"""Context slicing of one long sequence across GPUs.
+
+Every rank holds a contiguous range of the sealed groups of each layer. Rank 0 also holds the sink, and the last
+rank holds the staging ring (the newest positions). Each rank attends over its own regions with
+sjk_attend_partial, getting one (m, l, o[D]) triple per (query row, query head). The triples are all-gathered over
+the process group (NCCL over NVLink on the GPU box) and merged in rank order with sjk_attend_merge. Every rank
+therefore ends with the same output, equal to attention over the whole context (sj_kvarn.h:1535-1564) up to fp32
+rounding. The only exchange per layer call is the all-gather of n_q * n_head * (D + 2) floats per rank.
+"""
+import numpy as np
+
+SJK_REGION_SINK, SJK_REGION_BODY, SJK_REGION_RING = 1, 2, 4
+
+
+def group_range(rank, world, n_groups):
+    """Contiguous, balanced range [g0, g1) of the sealed groups owned by `rank`."""
+    return n_groups * rank // world, n_groups * (rank + 1) // world
+
+
+def regions(rank, world):
+    """The cache regions `rank` attends over: its body slice, plus the sink on rank 0 and the ring on the last rank."""
+    r = SJK_REGION_BODY
+    if rank == 0:
+        r |= SJK_REGION_SINK
+    if rank == world - 1:
+        r |= SJK_REGION_RING
+    return r
+
+
+def gather(dist, part):
+    """All-gather the partial triples of every rank, in rank order: [world, rows, D + 2] (one NCCL all-gather into
+    a single buffer on the GPU box; a list all-gather on backends without it)."""
+    import torch
+    world = dist.get_world_size()
+    out = torch.empty((world,) + tuple(part.shape), dtype=part.dtype, device=part.device)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, part.contiguous())
+    else:
+        dist.all_gather(list(out.unbind(0)), part.contiguous())
+    return out
+
+
+def merge_partials_np(parts):
+    """Combine partial triples [P, rows, D + 2] in index order into [rows, D] (the merge kernel's arithmetic in
+    numpy, for host-side checks): out = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m), m = max_i m_i."""
+    parts = np.asarray(parts, np.float64)
+    m, l, o = parts[:, :, 0], parts[:, :, 1], parts[:, :, 2:]
+    mx = m.max(axis=0)
+    w = np.where(np.isneginf(m), 0.0, np.exp(m - np.where(np.isneginf(mx), 0.0, mx)))
+    den = (l * w).sum(axis=0)
+    num = (o * w[:, :, None]).sum(axis=0)
+    return np.where(den[:, None] > 0, num / np.where(den == 0, 1.0, den)[:, None], 0.0)
+
+
+def partial_np(q, k, v, scale):
+    """Reference partial triple over one slice of positions: q [rows, D], k, v [n, D] -> [rows, D + 2]."""
+    s = (q.astype(np.float64) @ k.astype(np.float64).T) * scale
+    if s.shape[1] == 0:
+        out = np.zeros((q.shape[0], q.shape[1] + 2))
+        out[:, 0] = -np.inf
+        return out
+    m = s.max(axis=1)
+    p = np.exp(s - m[:, None])
+    return np.concatenate([m[:, None], p.sum(axis=1)[:, None], p @ v.astype(np.float64)], axis=1)

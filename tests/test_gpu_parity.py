@@ -207,6 +207,47 @@ def test_attend_regions_and_shapes(L, oracle_lib, D, staging, sink_f16, bk, bv, 
     oc.close()
 
 
+@pytest.mark.parametrize("bk,bv,body", [(4, 4, 0), (3, 2, 1)])
+def test_attend_partial_merge(L, oracle_lib, bk, bv, body):
+    """Attention split by context on one GPU: partials over disjoint region sets (sink + body, staging ring),
+    merged in order, equal the attention over the whole layer; all regions through the partial path equal
+    sjk_attend; the empty region set gives an empty partial (m = -inf, l = 0, o = 0)."""
+    D, H = 256, 2
+    layer, oc, B, cfg = _build_pair(L, oracle_lib, D, H, bk, bv, body, 0, True, 1500, 256, 512, 64, seed=13)
+    n_q, n_head, N = 4, 8, 1500
+    qpos0, rows, W = N - n_q, n_q * n_head, D + 2
+    q = synth.queries(21, 1, n_q, n_head, D)[0]
+    qr = oracle_lib.fwht_rows(q.reshape(-1, D).copy()).reshape(n_q, n_head, D)
+    dq = gu.dev(qr)
+    scale = np.float32(1.0 / 16.0)
+    view = sjk.view_of(layer)
+    need = L.sjk_attend_scratch_bytes(C.byref(view), N, n_q, n_head)
+    scratch = gu.dev_zeros(need)
+    parts = gu.dev_zeros(3 * rows * W * 4)
+
+    def partial(i, regions):
+        sjk.check(L.sjk_attend_partial(C.byref(view), B, N, qpos0, n_q, n_head, regions, gu.ptr(dq), scale,
+                                       C.c_void_p(parts.data_ptr() + i * rows * W * 4), gu.ptr(scratch), need, None))
+
+    partial(0, sjk.REGION_SINK | sjk.REGION_BODY)
+    partial(1, sjk.REGION_RING)
+    partial(2, 0)
+    dout = gu.dev_zeros(rows * D * 4)
+    sjk.check(L.sjk_attend_merge(gu.ptr(parts), 3, rows, D, gu.ptr(dout), None))
+    ref = oc.attend(B, N, qpos0, qr, scale)
+    assert gu.rel_err_rows(gu.host(dout, np.float32, (n_q, n_head, D)), ref) <= ATTN_TOL_TIGHT
+    p = gu.host(parts, np.float32, (3, rows, W))
+    assert np.all(np.isneginf(p[2, :, 0])) and np.all(p[2, :, 1:] == 0)
+    partial(0, sjk.REGION_ALL)
+    sjk.check(L.sjk_attend_merge(gu.ptr(parts), 1, rows, D, gu.ptr(dout), None))
+    d2 = gu.dev_zeros(rows * D * 4)
+    sjk.check(L.sjk_attend(C.byref(view), B, N, qpos0, n_q, n_head, gu.ptr(dq), scale, gu.ptr(d2), gu.ptr(scratch), need, None))
+    assert gu.rel_err_rows(gu.host(dout, np.float32, (rows, D)), gu.host(d2, np.float32, (rows, D))) <= 1e-6
+    assert L.sjk_device_status() == 0
+    L.sj_kvarn_layer_free(C.byref(layer))
+    oc.close()
+
+
 def _expected_states():
     exp = {}
     for ln in open(os.path.join(GOLDEN, "expected_state.txt")):
