@@ -410,6 +410,157 @@ def run_config4(args, torch, L, stream_obj, dist, rank, world):
                 exchange=rows * (D + 2) * 4, groups_per_rank=g1 - g0)
 
 
+CFG3 = dict(SEQS=64, CTX_LO=8192, CTX_HI=65536, LAYERS=16, NQ=1, ROWS=8192, MAX_STEPS=10)
+
+
+def run_config3(args, torch, L, stream_obj, dist, rank, world):
+    """a paged record pool of 64 sequences (contexts uniform in [8K, 64K], seed 3), 3/3 trellis
+    body, adaptive tail 4096 -> 8192, fp16 sink 128, 16 layers, decode width 1 (16 query heads, GQA 4). The sequences
+    are assigned to the ranks by longest-processing-time on their contexts (slices.lpt_assign) and every rank builds
+    its own in one pool through the product's sequence API (sj_kvarn_seq_begin_ubatch: policy, block reservation and
+    seals; sjk_seq_store: the ring / sink writes of each 512-token ubatch). One step appends one token to every
+    sequence of every layer (sj_kvarn_seq_begin_ubatch, sealing where the policy says, then one sjk_store_batch
+    launch for all (sequence, layer) pairs) and runs one sjk_attend_batch call per layer over all the rank's
+    sequences. K/V rows come from 8,192 seeded rows per layer drawn from config 0's distribution, reused cyclically."""
+    import numpy as np
+    import sjk
+    st = C.c_void_p(stream_obj.cuda_stream)
+    c, c3 = CFG1, CFG3
+    import slices
+    H, D, HQ, NL, NQ, R = c["H"], c["D"], c["HQ"], c3["LAYERS"], c3["NQ"], c3["ROWS"]
+    ctx = np.random.default_rng(3).integers(c3["CTX_LO"], c3["CTX_HI"] + 1, size=c3["SEQS"])
+    owner = slices.lpt_assign(ctx, world)
+    mine = [i for i in range(len(ctx)) if owner[i] == rank]
+    steps = min(max(3, args.steps), c3["MAX_STEPS"])
+    extra = args.warmup + steps + 8
+    t0 = time.time()
+    cfg = sjk.config(D, H, int(ctx.max()) + extra + 1024, c["N_UB"], bits_k=3, bits_v=3, body=1, tail=c["TAIL"],
+                     tail_max=c["TAIL_MAX"])
+    pool = sjk.Pool()
+    n_blocks = sum((int(ctx[i]) + extra) // 128 + 2 for i in mine)
+    sjk.check(L.sj_kvarn_pool_init(C.byref(pool), C.byref(cfg), NL, n_blocks), "pool_init")
+    seqs = []
+    for i in mine:
+        s = sjk.Seq()
+        sjk.check(L.sj_kvarn_seq_init(C.byref(s), C.byref(cfg), NL, C.byref(pool)), "seq_init")
+        s.stream = st.value
+        seqs.append(s)
+    # seeded rows of config 0's distribution, [NL][R][H][D]
+    import synth
+    kvs = synth.KVStream(3000 + rank, NL, H, D)
+    gen = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    with torch.cuda.stream(stream_obj):
+        scale = torch.from_numpy(kvs.scale).cuda()
+        krows = (torch.randn((NL, R, H, D), generator=gen, device="cuda") * scale[:, None]).contiguous()
+        vrows = torch.randn((NL, R, H, D), generator=gen, device="cuda")
+    lstride = R * H * D
+    n_ub = c["N_UB"]
+    for j, s in enumerate(seqs):
+        target, pos = int(ctx[mine[j]]), 0
+        while pos < target:
+            n = min(n_ub, target - pos)
+            sjk.check(L.sj_kvarn_seq_begin_ubatch(C.byref(s), pos, n), "seq_begin_ubatch")
+            o = (pos * 7 + 1031 * j) % (R - n_ub)
+            sjk.check(L.sjk_seq_store(C.byref(s), pos, n, C.c_void_p(krows.data_ptr() + o * H * D * 4),
+                                      C.c_void_p(vrows.data_ptr() + o * H * D * 4), lstride, 1, st), "seq_store")
+            pos += n
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+    n_seq = len(seqs)
+    # static views: per layer over the rank's sequences; the store items are (sequence, layer) pairs
+    views = [(sjk.View * n_seq)() for _ in range(NL)]
+    store_views = (sjk.View * (n_seq * NL))()
+    for j, s in enumerate(seqs):
+        for il in range(NL):
+            L.sjk_layer_view(C.byref(s.layers[il]), C.byref(views[il][j]))
+            L.sjk_layer_view(C.byref(s.layers[il]), C.byref(store_views[j * NL + il]))
+    idx = torch.arange(n_seq * NL, device="cuda")
+    k_step = krows.view(NL, R, H, D)[idx % NL, (idx * 13) % R].contiguous()      # [items][H][D]
+    v_step = vrows.view(NL, R, H, D)[idx % NL, (idx * 13) % R].contiguous()
+    q = torch.randn((NL, n_seq, NQ, HQ, D), generator=gen, device="cuda")
+    sjk.check(L.sjk_hadamard(C.c_void_p(q.data_ptr()), NL * n_seq * NQ * HQ, D, None))
+    out = torch.empty_like(q)
+    per_layer = n_seq * NQ * HQ * D * 4
+    need = L.sjk_attend_batch_scratch_bytes(C.byref(views[0][0]), max(n_seq, 1), NQ, HQ)
+    scratch = torch.empty(int(need), dtype=torch.uint8, device="cuda")
+    Bs, Ns, Qs = (C.c_uint32 * n_seq)(), (C.c_uint32 * n_seq)(), (C.c_uint32 * n_seq)()
+    pos_items = (C.c_uint32 * (n_seq * NL))()
+    stats = dict(seal_steps=0, bytes=0)
+    torch.cuda.synchronize()
+
+    def step():
+        sealed = False
+        for j, s in enumerate(seqs):
+            B_before = s.pol.B
+            sjk.check(L.sj_kvarn_seq_begin_ubatch(C.byref(s), s.n, 1), "seq_begin_ubatch")
+            sealed |= s.pol.B != B_before
+            for il in range(NL):
+                pos_items[j * NL + il] = s.n
+        sjk.check(L.sjk_store_batch(store_views, pos_items, n_seq * NL, C.c_void_p(k_step.data_ptr()),
+                                    C.c_void_p(v_step.data_ptr()), 1, st), "store_batch")
+        for j, s in enumerate(seqs):
+            s.n = s.n + 1
+            Bs[j], Ns[j], Qs[j] = s.pol.B, s.n, s.n - 1
+        stats["seal_steps"] += int(sealed)
+        for il in range(NL):
+            rc = L.sjk_attend_batch(views[il], Bs, Ns, Qs, n_seq, NQ, HQ, C.c_void_p(q.data_ptr() + il * per_layer), SCALE,
+                                    C.c_void_p(out.data_ptr() + il * per_layer), C.c_void_p(scratch.data_ptr()), need, st)
+            if rc:
+                raise sjk.SjkError(rc, "attend_batch")
+
+    def step_bytes():
+        # algorithmic bytes of one step's attention: every record, staged row and sink row of every sequence and layer
+        tot = 0
+        for s in seqs:
+            B, N = s.pol.B, s.n
+            tot += (B - 128) // 128 * H * 26880 + (N - B) * H * 392 + 128 * H * 1024 + 2 * NQ * HQ * D * 4
+        return tot * NL
+
+    barrier = (lambda: dist.barrier()) if dist else None
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    stats["seal_steps"] = 0
+    b0 = step_bytes()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream_obj)
+    for _ in range(steps):
+        step()
+    e1.record(stream_obj)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    b1 = step_bytes()
+    # attention alone (no appends), the same call shapes: bytes per step / time
+    def attend_only():
+        for il in range(NL):
+            rc = L.sjk_attend_batch(views[il], Bs, Ns, Qs, n_seq, NQ, HQ, C.c_void_p(q.data_ptr() + il * per_layer), SCALE,
+                                    C.c_void_p(out.data_ptr() + il * per_layer), C.c_void_p(scratch.data_ptr()), need, st)
+            if rc:
+                raise sjk.SjkError(rc, "attend_batch")
+
+    ms_attn = time_events(torch, stream_obj, attend_only, steps, 2, barrier)
+    abytes = step_bytes()
+    if dist:
+        t = torch.tensor([ms, ms_attn], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        tb = torch.tensor([float(abytes), float((b0 + b1) / 2)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        ms, ms_attn = float(t[0]), float(t[1])
+        abytes, sbytes = float(tb[0]), float(tb[1])
+    else:
+        sbytes = (b0 + b1) / 2
+    status = L.sjk_device_status()
+    for s in seqs:
+        L.sj_kvarn_seq_free(C.byref(s))
+    L.sj_kvarn_pool_free(C.byref(pool))
+    del krows, vrows, scratch
+    return dict(ms=ms, ms_attn=ms_attn, attn_bytes=abytes, step_bytes=sbytes, seqs=n_seq, steps=steps,
+                seal_steps=stats["seal_steps"], build_s=build_s, ctx_total=int(ctx.sum()), device_status=status,
+                launches_per_step=1 + 3 * NL)
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # reference CPU path (oracle/_ref: the reference sj_kvarn.h compiled from its own source)
 # ---------------------------------------------------------------------------------------------------------------
@@ -579,6 +730,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config2", action="store_true", help="skip the config-2 (3/2 trellis) side measurement")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 (1M context sliced over the ranks) measurement")
+    ap.add_argument("--no-config3", action="store_true", help="skip the config-3 (64-sequence paged pool) measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -605,6 +757,7 @@ def main():
         dist = td
     res = run_gpu_arm(args, torch, dist, rank, world, local_rank)
     cfg4 = None if args.no_config4 else run_config4(args, torch, sjk.lib(), torch.cuda.Stream(), dist, rank, world)
+    cfg3 = None if args.no_config3 else run_config3(args, torch, sjk.lib(), torch.cuda.Stream(), dist, rank, world)
     seal = run_seal(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 else None
     cfg2 = run_config2(args, torch, sjk.lib(), torch.cuda.Stream()) if rank == 0 and not args.no_config2 else None
 
@@ -674,6 +827,20 @@ def main():
             "attn_frac_of_all_ranks": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9 / (peak * world),
             "groups_per_rank": cfg4["groups_per_rank"], "exchange_bytes_per_rank": cfg4["exchange"],
             "scaling": "strong (fixed sequence)", "build_s": cfg4["build_s"]},
+        "config3": None if cfg3 is None else {
+            "workload": "config 3: paged pool of 64 sequences (contexts U[8K, 64K], seed 3), 3/3 trellis, tail 4096 -> 8192, "
+                        f"sink 128, 16 layers, decode width 1; sequences split over {world} rank(s) by LPT on context; one step "
+                        "= 1 appended token per sequence and layer (sealing as the policy says) + 1 batched attention call per layer",
+            "metric": "decode tokens/s (64 per step)", "value": 64.0 / (cfg3["ms"] * 1e-3), "unit": "tok/s",
+            "ms_per_step": cfg3["ms"], "steps": cfg3["steps"], "steps_with_seal": cfg3["seal_steps"],
+            "attn_ms_per_step": cfg3["ms_attn"], "attn_bytes_per_step": cfg3["attn_bytes"],
+            "attn_gbs": cfg3["attn_bytes"] / (cfg3["ms_attn"] * 1e-3) / 1e9,
+            "attn_frac_of_all_ranks": cfg3["attn_bytes"] / (cfg3["ms_attn"] * 1e-3) / 1e9 / (peak * world),
+            "step_gbs": cfg3["step_bytes"] / (cfg3["ms"] * 1e-3) / 1e9, "ctx_total": cfg3["ctx_total"],
+            "seqs_rank0": cfg3["seqs"], "gpu_launches_per_step": cfg3["launches_per_step"],
+            "kernel": "sjk_attend_batch: attend_trellis_ws_kernel (all records of all sequences) + attend_dense_tc_kernel "
+                      "(sinks + staging rings) + attend_batch_merge_kernel; store_batch_kernel",
+            "scaling": "strong (fixed 64 sequences)", "device_status": cfg3["device_status"], "build_s": cfg3["build_s"]},
         "cpu_baseline": cpu,
         "build_s": res["build_s"],
     }

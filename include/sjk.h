@@ -320,6 +320,13 @@ int sjk_unstage_rows(int staging, const uint8_t * src, size_t src_row_bytes, flo
 int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos,
               const float * k, const float * vv, int rotate, sjk_stream st);
 
+/* One position in each of n_items layer caches in one launch - the decode step's cache write across the layers and
+ * sequences of a batch (sj_kvarn.h:1475-1492 per item): item i stores the rows k + i*n_head_kv*D, vv + i*n_head_kv*D
+ * (rotated, or model basis with rotate = 1) at position pos[i] (host array) of views[i]'s sink or staging ring. All
+ * views share the layout, formats, sink length and ring capacity. No counterpart in the reference. */
+int sjk_store_batch(const sjk_view * views, const uint32_t * pos, int n_items, const float * k, const float * vv,
+                    int rotate, sjk_stream st);
+
 /* Seal n_groups x n_head_kv records from fp16 rows (sj_kvarn_cuda.cuh:136-152): record
  * r = g*n_head_kv + h reads rows k + g*G*row_stride + h*D. work is ignored (may be NULL). */
 int sjk_seal(const sj_kvarn_layout * lay, const uint16_t * k, const uint16_t * v, size_t row_stride,
@@ -352,6 +359,18 @@ int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos
                        const float * q, float scale, float * part_out, void * scratch, size_t scratch_bytes, sjk_stream st);
 int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st);
 
+/* Attention of a batch of sequences of one layer in one call: the decode step of a paged record pool, where
+ * sequence s (views[s]: its sink, staging ring, pool slab and device block table; every view has the same layout,
+ * formats, sink length and ring capacity) attends with query rows q + s*n_q*n_head*D at positions qpos0[s].. over
+ * [0, N[s]) with [S, B[s]) sealed, and writes out + s*n_q*n_head*D. Equivalent to n_seq sjk_attend calls
+ * (sj_kvarn.h:1535-1564 per sequence and head; the pool resolution of sj_kvarn.h:1429-1432, 1706-1739); trellis
+ * layers take three launches for the whole batch. B, N, qpos0 are host arrays; scratch: at least
+ * sjk_attend_batch_scratch_bytes() bytes. No counterpart in the reference, whose attention is per sequence. */
+size_t sjk_attend_batch_scratch_bytes(const sjk_view * v, int n_seq, int n_q, int n_head);
+int sjk_attend_batch(const sjk_view * views, const uint32_t * B, const uint32_t * N, const uint32_t * qpos0, int n_seq,
+                     int n_q, int n_head, const float * q, float scale, float * out, void * scratch, size_t scratch_bytes,
+                     sjk_stream st);
+
 /* sjk_attend for callers that cannot allocate device memory - code that runs where cudaMalloc is off
  * limits, such as inside a stream capture, a custom allocator's own callbacks or an engine whose memory
  * is planned ahead. No counterpart in the reference. The scratch for the split partials is a fixed 16 MiB
@@ -369,6 +388,12 @@ int sjk_layer_seal(sj_kvarn_layer * L, uint32_t B_from, uint32_t B_to, sjk_strea
 int sjk_layer_attend(const sj_kvarn_layer * L, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
                      const float * q, float scale, float * out, sjk_stream st);
 void sjk_layer_view(const sj_kvarn_layer * L, sjk_view * v);
+/* Prefill form of sj_kvarn_seq_store (sj_kvarn.h:1645-1700): positions pos0 .. pos0 + n_pos - 1 of every layer;
+ * layer il's rows are DEVICE [n_pos][n_head_kv][D] floats at k + il*layer_stride, v + il*layer_stride (layer_stride
+ * in floats; 0 means n_pos*n_head_kv*D), rotate as sjk_store. Raises the sequence's length to pos0 + n_pos. Call
+ * sj_kvarn_seq_begin_ubatch(s, pos0, n_pos) first, as for sj_kvarn_seq_store. */
+int sjk_seq_store(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_pos, const float * k, const float * v, size_t layer_stride,
+                  int rotate, sjk_stream st);
 /* copy record (g, h) to host memory (synchronous) */
 int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * host_dst);
 

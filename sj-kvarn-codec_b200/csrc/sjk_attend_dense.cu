@@ -33,17 +33,28 @@ constexpr int CH = 128;
 constexpr uint32_t TM_COLS = 256;
 constexpr uint32_t COL_AH = 0, COL_AL = 64, COL_S = 128, COL_O = 192;   // A hi | A lo | S0 S1 (2 x 32) | O0 O1
 
-struct DenseParams {
-    sjk_view v;
-    int kv0;
+constexpr int MAX_SEQS = 128;
+constexpr int MAX_ITEMS = 768;
+
+struct DenseSeq {                       // one sequence of the call
+    const uint8_t * sink;
+    const uint8_t * ring;
+    const float * q;                    // [n_q][n_head][D] rotated queries
     uint32_t B, N, qpos0;
+    uint32_t n_sink_chunks;             // chunk list: sink chunks first, then ring chunks from max(B, S)
+};
+struct DenseItem {                      // chunks [c0, c1) of KV head h of sequence seq, partial slot `slot`
+    uint32_t seq_hl;                    // seq | hl << 16 (hl: head index inside q and the partial rows)
+    uint32_t h_slot;                    // h | slot << 16
+    uint32_t c0, c1;
+};
+struct DenseParams {
+    sjk_view v;                         // layout, staging formats, S, cap (the per-sequence pointers are in seq[])
     int n_q, n_head, grp, rows;
-    const float * q;
     float scale;
-    float * part;
-    int split0;
-    uint32_t n_sink_chunks, n_chunks;   // chunk list: sink chunks first, then ring chunks from B
-    int chunks_per_split;
+    float * part;                       // [slots][n_q n_head][D + 2]
+    DenseSeq seq[MAX_SEQS];
+    DenseItem item[MAX_ITEMS];          // one per CTA
 };
 
 // B operand (K-major, no swizzle, 32 rows): element (n, k) at (k / 8) * HCH + n * 16 + (k % 8) * 2 with an 8-element
@@ -80,11 +91,13 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t w) {
     return __half22float2(h);
 }
 
-__global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
+__global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(const __grid_constant__ DenseParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;
-    const int hl = blockIdx.y, h = p.kv0 + hl, split = blockIdx.x;
+    const DenseItem & item = p.item[blockIdx.x];
+    const DenseSeq & sq = p.seq[item.seq_hl & 0xFFFFu];
+    const int hl = (int) (item.seq_hl >> 16), h = (int) (item.h_slot & 0xFFFFu), slot = (int) (item.h_slot >> 16);
     const sjk_view & v = p.v;
     const int H = v.n_head_kv;
     uint8_t * bq = sm + OFF_BQ;
@@ -98,8 +111,7 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     uint64_t * bar = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
 
-    const uint32_t c_begin = (uint32_t) split * (uint32_t) p.chunks_per_split;
-    const uint32_t c_end = min(c_begin + (uint32_t) p.chunks_per_split, p.n_chunks);
+    const uint32_t c_begin = item.c0, c_end = item.c1;
 
     if (warp == 0) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
     if (tid == 0) { tc::mbar_init(bar, 1); tc::mbar_fence_init(); }
@@ -109,15 +121,15 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
         cent2[tid] = pack_h2(__half2float(hi), c - __half2float(hi));
     }
     if (tid < NR) { row[ROW_M2 + tid] = -INFINITY; row[ROW_L + tid] = 0.0f; }
-    const uint32_t S_eff = v.S < p.N ? v.S : p.N;
-    const uint32_t t0_ring = p.B > v.S ? p.B : v.S;
+    const uint32_t S_eff = v.S < sq.N ? v.S : sq.N;
+    const uint32_t t0_ring = sq.B > v.S ? sq.B : v.S;
     const uint32_t idesc32 = tc::idesc_f16(128, NB), idesc16 = tc::idesc_f16(128, NR);
     const float sl2 = p.scale * LOG2E;
     uint32_t qlim[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int r = 8 * half + i;
-        qlim[i] = r < p.rows ? p.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
+        qlim[i] = r < p.rows ? sq.qpos0 + (uint32_t) (r / p.grp) + 1u : 0u;
     }
     float acc[NR];
 #pragma unroll
@@ -154,9 +166,9 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
 
     for (uint32_t ci = c_begin; ci < c_end && ok; ++ci) {
         // ---- chunk geometry and row kind ----
-        const bool in_sink = ci < p.n_sink_chunks;
-        const uint32_t p0 = in_sink ? ci * (uint32_t) CH : t0_ring + (ci - p.n_sink_chunks) * (uint32_t) CH;
-        const uint32_t len = min((uint32_t) CH, (in_sink ? S_eff : p.N) - p0);
+        const bool in_sink = ci < sq.n_sink_chunks;
+        const uint32_t p0 = in_sink ? ci * (uint32_t) CH : t0_ring + (ci - sq.n_sink_chunks) * (uint32_t) CH;
+        const uint32_t len = min((uint32_t) CH, (in_sink ? S_eff : sq.N) - p0);
         // f16 rows: the fp16 sink, or an fp16 staging ring / inherited sink; otherwise tq6_0 rows
         const bool f16 = (in_sink && v.sink_type == SJKVARN_SINK_F16) || v.staging == SJKVARN_STAGING_F16;
         const uint32_t side_off = (in_sink && v.sink_type == SJKVARN_SINK_F16) ? 2u * D : (uint32_t) v.stage_bytes;
@@ -165,9 +177,9 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
         if (tid < CH) {
             const uint32_t pos = p0 + (uint32_t) min(tid, (int) len - 1);
             const uint8_t * r;
-            if (in_sink && v.sink_type == SJKVARN_SINK_F16) r = v.sink + ((size_t) pos * H + h) * 4 * D;
-            else if (in_sink) r = v.sink + ((size_t) pos * H + h) * 2 * v.stage_bytes;
-            else r = v.ring + ((size_t) sjk_ring_slot(v.S, v.cap, pos) * H + h) * 2 * v.stage_bytes;
+            if (in_sink && v.sink_type == SJKVARN_SINK_F16) r = sq.sink + ((size_t) pos * H + h) * 4 * D;
+            else if (in_sink) r = sq.sink + ((size_t) pos * H + h) * 2 * v.stage_bytes;
+            else r = sq.ring + ((size_t) sjk_ring_slot(v.S, v.cap, pos) * H + h) * 2 * v.stage_bytes;
             rowp[tid] = r;
         }
         __syncthreads();
@@ -193,7 +205,7 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
         if (!bq_done) {
             // ---- B_Q = [q hi | q lo] (rotated rows), built while the first chunk's rows stream in ----
             const int d = tid;
-            const float * __restrict__ qg = p.q;
+            const float * __restrict__ qg = sq.q;
             float x[NR];                                         // all loads first: the stores below are shared
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
@@ -384,7 +396,7 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(DenseParams p) {
     for (int r = 0; r < NR; ++r) {
         if (r < p.rows) {
             const int iq = r / p.grp, hq = hl * p.grp + r % p.grp;
-            float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
+            float * dst = p.part + ((size_t) slot * p.n_q * p.n_head + (size_t) iq * p.n_head + hq) * (D + 2);
             if (tid == 0) {
                 const float m2 = row[ROW_M2 + r];
                 dst[0] = ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
@@ -414,17 +426,86 @@ int sjk_tc_dense_splits(uint32_t n_chunks, int n_kv, int * chunks_per_split) {
     return (int) ((n_chunks + (uint32_t) cps - 1) / (uint32_t) cps);
 }
 
+namespace {
+int dense_launch_params(const DenseParams & p, int n_items, sjk_stream st) {
+    cudaError_t e = cudaFuncSetAttribute(attend_dense_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    if (e != cudaSuccess) return sjk_check(e);
+    attend_dense_tc_kernel<<<(unsigned) n_items, NT, SMEM_TOTAL, st>>>(p);
+    return sjk_check_launch();
+}
+}  // namespace
+
+// One sequence: chunk list [0, n_chunks) (sink chunks first) of KV heads kv0 .. kv0 + n_kv - 1, `splits` items of
+// chunks_per_split chunks per head; item (head hl, split s) writes partial slot split0 + s.
 int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
                         const float * q, float scale, float * part, int split0, int splits, uint32_t n_sink_chunks,
                         uint32_t n_chunks, int chunks_per_split, sjk_stream st) {
-    DenseParams p;
-    p.v = *v; p.kv0 = kv0; p.B = B; p.N = N; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv;
-    p.rows = n_q * p.grp; p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
-    p.n_sink_chunks = n_sink_chunks; p.n_chunks = n_chunks; p.chunks_per_split = chunks_per_split;
-    cudaError_t e = cudaFuncSetAttribute(attend_dense_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
-    if (e != cudaSuccess) return sjk_check(e);
-    attend_dense_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
-    return sjk_check_launch();
+    if (splits <= 0) return 0;
+    if (splits * n_kv > MAX_ITEMS || split0 + splits > 0xFFFF) return SJK_ERR_UNSUPPORTED;
+    static thread_local DenseParams p;
+    p.v = *v; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp; p.scale = scale; p.part = part;
+    p.seq[0].sink = v->sink; p.seq[0].ring = v->ring; p.seq[0].q = q; p.seq[0].B = B; p.seq[0].N = N; p.seq[0].qpos0 = qpos0;
+    p.seq[0].n_sink_chunks = n_sink_chunks;
+    int k = 0;
+    for (int hl = 0; hl < n_kv; ++hl)
+        for (int s = 0; s < splits; ++s, ++k) {
+            DenseItem & it = p.item[k];
+            it.seq_hl = (uint32_t) hl << 16;
+            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
+            it.c0 = (uint32_t) s * (uint32_t) chunks_per_split;
+            it.c1 = it.c0 + (uint32_t) chunks_per_split < n_chunks ? it.c0 + (uint32_t) chunks_per_split : n_chunks;
+        }
+    return dense_launch_params(p, k, st);
+}
+
+// Many sequences of one layer (same layout and formats as *v): sequence s has sink / ring pointers views[s], query
+// rows q + s n_q n_head D and positions [0, N[s]) with B[s] sealed; its staged chunks (sink, then ring) are cut into
+// items of at most cps chunks per KV head. Items get partial slots slot0, slot0 + 1, ...; for pair (s, h) the items
+// are slots first[s H + h] .. first[s H + h + 1] - 1. Returns the item count in *n_items.
+int sjk_tc_dense_batch_launch(const sjk_view * views, const uint32_t * B, const uint32_t * N, const uint32_t * qpos0,
+                              int n_seq, int n_q, int n_head, const float * q, float scale, float * part, int slot0,
+                              uint16_t * first, int * n_items, sjk_stream st) {
+    const sjk_view & v0 = views[0];
+    const int H = v0.n_head_kv;
+    if (n_seq > MAX_SEQS) return SJK_ERR_UNSUPPORTED;
+    static thread_local DenseParams p;
+    p.v = v0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / H; p.rows = n_q * p.grp; p.scale = scale; p.part = part;
+    uint64_t total = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        const uint32_t S = v0.S, s_end = S < N[s] ? S : N[s], t0 = B[s] > S ? B[s] : S;
+        DenseSeq & d = p.seq[s];
+        d.sink = views[s].sink; d.ring = views[s].ring; d.q = q + (size_t) s * n_q * n_head * D;
+        d.B = B[s]; d.N = N[s]; d.qpos0 = qpos0[s];
+        d.n_sink_chunks = (s_end + 127u) / 128u;
+        total += (uint64_t) (d.n_sink_chunks + (N[s] > t0 ? (N[s] - t0 + 127u) / 128u : 0u)) * (uint32_t) H;
+    }
+    const int pairs = n_seq * H;
+    if (pairs >= MAX_ITEMS) return SJK_ERR_UNSUPPORTED;
+    // sum over pairs of ceil(c / cps) <= total / cps + pairs <= MAX_ITEMS; also at least ~2 CTAs per SM of work items
+    uint64_t cps = (total + (uint64_t) (MAX_ITEMS - pairs) - 1) / (uint64_t) (MAX_ITEMS - pairs);
+    const uint64_t cps_fill = (total + 2 * 148 - 1) / (2 * 148);
+    if (cps < cps_fill) cps = cps_fill;
+    if (cps < 1) cps = 1;
+    int k = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        const uint32_t S = v0.S, t0 = B[s] > S ? B[s] : S;
+        const uint32_t nc = p.seq[s].n_sink_chunks + (N[s] > t0 ? (N[s] - t0 + 127u) / 128u : 0u);
+        for (int h = 0; h < H; ++h) {
+            first[s * H + h] = (uint16_t) (slot0 + k);
+            for (uint32_t c = 0; c < nc; c += (uint32_t) cps, ++k) {
+                if (k >= MAX_ITEMS || slot0 + k > 0xFFFF) return SJK_ERR_UNSUPPORTED;
+                DenseItem & it = p.item[k];
+                it.seq_hl = (uint32_t) s | ((uint32_t) h << 16);
+                it.h_slot = (uint32_t) h | ((uint32_t) (slot0 + k) << 16);
+                it.c0 = c;
+                it.c1 = c + (uint32_t) cps < nc ? c + (uint32_t) cps : nc;
+            }
+        }
+    }
+    first[pairs] = (uint16_t) (slot0 + k);
+    *n_items = k;
+    if (k == 0) return 0;
+    return dense_launch_params(p, k, st);
 }
 
 SJK_STATUS_READER(sjk_tc_dense_status_take)

@@ -1,26 +1,32 @@
-// sjk_attend_trellis.cu - tensor-core (tcgen05, kind::f16) attention over the sealed body of a trellis layer
-// (3/3t, 3/2t, 2/2t records: sj_kvarn.h:1025-1109, 1176-1207).
+// sjk_attend_trellis.cu - tensor-core (tcgen05, kind::f16) attention over the sealed body of trellis layers
+// (3/3t, 3/2t, 2/2t records: sj_kvarn.h:1025-1109, 1176-1207), for one sequence or a batch of sequences.
 //
 // A trellis record stores, per channel d, the codes of its 128 tokens as one channel-major bit stream; the
 // value of token t is a codebook entry picked by the window of its code and the 6 stream bits before it
 // (sj_kvarn.h:879-900). The decoded rows are
 //   K[t, d] = (cb_K[w_K(d, t)] Ks[d] + Kz[d]) Kt[t],      V[t, d] = (cb_V[w_V(d, t)] Vs[t] + Vz[t]) Vc[d]
-// and regroup as in the 4-bit kernel:
+// and regroup so the codebook entries (fp16, exact) are the tensor-core A operands:
 //   S^T[t, r] = Kt[t] (sum_d cb_K[w_K(d, t)] Q'[r, d] + C[r]),   Q' = q Ks,  C = sum_d q Kz
 //   O^T[d, r] = Vc[d] (sum_t cb_V[w_V(d, t)] P'[r, t] + z[r]),   P' = p Vs,  z = sum_t p Vz
-// The codebook entries are fp16, so the A operands enter the tensor core exactly; Q' and P' enter as fp16
-// hi + lo halves side by side in N (B = [hi | lo], N = 32): one MMA per k step leaves the hi and lo products in
-// column groups 0..15 and 16..31, whose sum is the fp32 product to about 2^-22.
+// Q' and P' enter as fp16 hi + lo halves side by side in N (B = [hi | lo], N = 32): one MMA per k step leaves
+// the hi and lo products in column groups 0..15 and 16..31, whose sum is the fp32 product to about 2^-22.
 //
-// Decoding follows the streams: a thread walks 64 codes of one channel with the stream words in registers, so
-// every window is one shift and one mask at a compile-time offset. A_V is channel-major (lane = channel), so
-// the V values go straight into the thread's TMEM lane; A_K is token-major (lane = token), so the K values go
-// through a [token][channel] shared tile first. The codebooks sit in shared memory in 16 interleaved copies
-// (lookups by different lanes rarely share a bank).
+// Both A operands are decoded channel by channel, the order of the streams: a thread holds one channel's
+// stream words in registers and looks each window up in a shared table. The table keeps 32 copies of every
+// entry, one per bank, with the K codebook in the low and the V codebook in the high half of each word, so
+// every lookup of a warp is one conflict-free wavefront and both sides share 64 KB. A_K (token rows, channel
+// k) is stored MN-major in shared memory - a channel's 128 tokens are 16 contiguous 16-byte chunks - so the
+// decoded pairs leave with 16-byte stores; A_V (channel rows, token k) goes straight into the thread's TMEM lane.
 //
-// One CTA (512 threads, 16 warps) per SM walks a contiguous range of one KV head's records; the next record's
-// bytes arrive by cp.async.bulk (no multicast) while the current one is processed; the online softmax state
-// (m, l, o) per query row goes to the split partials that the merge kernel combines. Waits are bounded.
+// The kernel is persistent and warp-specialized. Each CTA walks a list of work items (a contiguous record
+// range of one KV head of one sequence), so one launch covers a single sequence split across the SMs or many
+// sequences of a paged pool. Roles, linked only by mbarriers, overlap consecutive records:
+//   warps 0-7    K side   B_K = [Q' hi | Q' lo] and the zero-point sums C, then A_K (shared, MN-major)
+//   warps 8-15   V side   A_V into TMEM (double-buffered), then the epilogue of the previous record
+//   warps 16-19  softmax  scores, online softmax per item, B_V = [P' hi | P' lo], the sums of p and p Vz
+//   warp 20      issuer   bulk copies of records into a 2-stage ring (no multicast), the MMAs, commits
+// Every wait is bounded; a role whose wait runs out raises a CTA abort flag, the others stop at their next
+// wait, and the issuer drains its own copies and MMAs before the TMEM is released.
 #include <cuda_fp16.h>
 
 #include "sjk_common.cuh"
@@ -31,29 +37,45 @@ namespace {
 
 using namespace tc::num;
 
-constexpr int NT = 512;
-constexpr int NR = 16;
+constexpr int NR = 16;                  // query rows per KV head, padded
 constexpr int NB = 2 * NR;              // B operands: hi rows 0..15, lo rows 16..31
 constexpr int D = 256;
 constexpr int G = 128;
+constexpr int NT = 672;                 // 8 K-side warps, 8 V-side warps, 4 softmax warps, 1 issuer warp
+constexpr int W_V = 8, W_S = 16, W_I = 20;
 constexpr uint32_t TM_COLS = 512;
-constexpr uint32_t COL_AK = 0, COL_AV = 128, COL_S = 256, COL_O = 288;   // A_K (256 ch) | A_V (2 tiles x 128 t) | S | O0 O1
-constexpr int MAX_SPLITS = 148;
+constexpr uint32_t COL_AV = 0, COL_S = 256, COL_O = 320;     // A_V [2 buffers][2 tiles][64] | S [2][32] | O [2 tiles][32]
 constexpr uint32_t REC_MAX = 26880;     // largest trellis record at D = 256 (3/3t)
-constexpr int CB_COPIES = 16;
+constexpr int MAX_SEQS = 128;
+constexpr int MAX_ITEMS = 672;
+constexpr int MAX_CTAS = 148;
 
-struct TrellisParams {
-    sjk_view v;
-    int kv0;
-    uint32_t S, B, N, qpos0, n_rec;
-    int n_q, n_head, grp, rows;
-    uint32_t row_iq[NR];        // r / grp
-    int row_q[NR];              // iq n_head + r % grp (q row and partial row of r, less hl grp)
-    const float * q;
+struct TwSeq {                          // one sequence of the call
+    const uint8_t * body;               // [blocks][n_head_kv][record]
+    const uint32_t * blocks;            // block table (null: record g is block g)
+    const float * q;                    // [n_q][n_head][D] rotated queries of this sequence
+    uint32_t S;                         // sink length: record g covers positions S + 128 g ..
+    uint32_t b_end;                     // min(B, N): positions at or past it are not in the body
+    uint32_t qpos0;                     // position of the first query row
+    uint32_t pad;
+};
+struct TwItem {                         // records [r0, r1) of KV head h of sequence seq, partial slot `slot`
+    uint32_t seq_hl;                    // seq | hl << 16 (hl: head index inside q and the partial rows)
+    uint32_t h_slot;                    // h | slot << 16
+    uint32_t r0, r1;
+};
+struct TwParams {
+    sj_kvarn_layout lay;
+    int n_head_kv;
+    int rows, grp, n_rows;              // query rows per KV head (n_q grp), GQA group, n_q n_head
+    uint32_t row_iq[NR];                // r / grp
+    int row_q[NR];                      // iq n_head + r % grp: q row and partial row of r, less hl grp
     float scale;
-    float * part;
-    int split0;
-    uint32_t rec_bounds[MAX_SPLITS + 1];
+    float * part;                       // [slots][n_rows][D + 2]: m, l, o[D]
+    int n_cta;
+    uint16_t cta_item[MAX_CTAS + 1];    // items of CTA c: [cta_item[c], cta_item[c + 1])
+    TwSeq seq[MAX_SEQS];
+    TwItem item[MAX_ITEMS];
 };
 
 // B operand (K-major, no swizzle, 32 rows): element (n, k) at (k / 8) * HCH + n * 16 + (k % 8) * 2 with an
@@ -62,342 +84,503 @@ constexpr uint32_t HCH = 528;
 constexpr uint32_t TILE_B = 16 * HCH;
 __device__ __forceinline__ uint32_t h_off(int n, int k) { return (uint32_t) (k >> 3) * HCH + (uint32_t) (n * 16 + (k & 7) * 2); }
 
+// A_K, MN-major without swizzle: element (t, d) at (t / 8) * 128 + (d / 8) * 2048 + (d % 8) * 16 + (t % 8) * 2,
+// i.e. 8 x 8 core matrices of 128 contiguous bytes, 128 bytes apart along t (SBO) and 2048 apart along d (LBO)
+constexpr uint32_t AK_SBO = 128, AK_LBO = 2048;
+
 // shared memory (bytes)
-constexpr uint32_t TRS = 2 * D + 16;                            // [token][channel] fp16 tile row (conflict-free LDS.128)
-constexpr uint32_t OFF_REC = 0;                                 // 2 x record
-constexpr uint32_t OFF_TR = OFF_REC + 2 * REC_MAX;              // K values, [128 tokens][256 channels]
-constexpr uint32_t OFF_BK = OFF_TR + G * TRS;                   // [Q' hi | Q' lo] over 256 channels: 2 x TILE_B
+constexpr uint32_t OFF_TBL = 0;                                 // u32 [512][32]: cb_K | cb_V << 16, 32 copies
+constexpr uint32_t OFF_AK = OFF_TBL + 512 * 32 * 4;             // 64 KB
+constexpr uint32_t OFF_REC = OFF_AK + 32 * AK_LBO;              // 2 x record
+constexpr uint32_t OFF_BK = OFF_REC + 2 * REC_MAX;              // [Q' hi | Q' lo] over 256 channels: 2 x TILE_B
 constexpr uint32_t OFF_BV = OFF_BK + 2 * TILE_B;                // [P' hi | P' lo] over 128 tokens: TILE_B
-constexpr uint32_t OFF_CBK = OFF_BV + TILE_B;                   // u32 [512][16]: K codebook, 16 copies
-constexpr uint32_t OFF_CBV = OFF_CBK + 512 * CB_COPIES * 4;     // u32 [512][16]: V codebook
-constexpr uint32_t OFF_ROW = OFF_CBV + 512 * CB_COPIES * 4;     // per-row floats
-constexpr uint32_t OFF_RED = OFF_ROW + 8 * NR * 4;              // reduction partials
-constexpr uint32_t OFF_BAR = OFF_RED + 3 * 256 * 4;
-constexpr uint32_t OFF_TMEM = OFF_BAR + 4 * 8;
-constexpr uint32_t SMEM_TOTAL = OFF_TMEM + 16;
+constexpr uint32_t OFF_F = OFF_BV + TILE_B;                     // floats below
+enum : uint32_t {
+    F_REDC = 0,         // [2][8 warps][8]   zero-point partials of the K side
+    F_REDM = 128,       // [4 warps][16]     score maxima
+    F_REDL = 192,       // [4][16]           sums of p
+    F_REDZ = 256,       // [4][16]           sums of p Vz
+    F_C = 320,          // [2][16]           C[r] per record parity
+    F_MN = 352,         // [16]              running max after the current record (log2 domain)
+    F_AL = 368,         // [3][16]           rescale of the running sums at the record (slot g % 3)
+    F_Z = 416,          // [3][16]           z[r] of the record (slot g % 3)
+    F_END = 464
+};
+constexpr uint32_t OFF_BAR = OFF_F + F_END * 4;
+enum : uint32_t {       // mbarriers
+    B_RFULL = 0, B_REMPTY = 2, B_AKFULL = 4, B_SFULL = 5, B_SFREE = 7, B_CFULL = 9, B_AZFULL = 11, B_AVFULL = 13,
+    B_VDONE = 15, B_OFREE = 17, B_COUNT = 18
+};
+constexpr uint32_t OFF_TMEM = OFF_BAR + B_COUNT * 8;
+constexpr uint32_t OFF_ABORT = OFF_TMEM + 4;
+constexpr uint32_t SMEM_TOTAL = OFF_ABORT + 12;
 static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
-enum { ROW_M2 = 0, ROW_MNEW = 16, ROW_ALPHA = 32, ROW_L = 48, ROW_C = 64, ROW_Z = 80 };
-enum { RED_MAX = 0, RED_L = 256, RED_Z = 512, RED_C = 512 };    // RED_C shares RED_Z's space (different phases)
-enum { BAR_REC = 0, BAR_MMA = 2 };
+static_assert(OFF_REC % 16 == 0 && REC_MAX % 16 == 0 && OFF_BK % 16 == 0 && OFF_BV % 16 == 0, "alignment");
 
-// The codes of tokens [64 TH, 64 TH + 64) of one channel: stream words from bit 64 TH BITS - 32 on, the word
-// before the channel's first reading as zero (the history before token 0). Token 64 TH + j then starts its
-// window at bit 26 + j BITS of W for both halves and both widths, since the window is 6 + BITS bits long and
-// ends with the token's code.
+// Wait for the phase of `bar` with the given parity. Gives up when the CTA's abort flag is raised or after about
+// 1 s of wall clock (then it raises the flag and records the timeout in the device status word).
+__device__ __forceinline__ bool wait_bar(uint64_t * bar, uint32_t parity, volatile int * abort) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = tc::globaltimer();
+    while (true) {
+        if (tc::mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (tc::globaltimer() - t0 > SJK_WAIT_NS) {
+            atomicExch(&sjk_dev_status, SJK_DEV_TIMEOUT);
+            *abort = 1;
+            return false;
+        }
+    }
+}
+// the same for a whole warp: true only if every lane saw the phase complete
+__device__ __forceinline__ bool warp_wait(uint64_t * bar, uint32_t parity, volatile int * abort) {
+    return __all_sync(0xFFFFFFFFu, wait_bar(bar, parity, abort));
+}
+__device__ __forceinline__ void warp_arrive(uint64_t * bar, int lane) {
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(bar);
+}
+
+// ---- stream decoding ----------------------------------------------------------------------------------------
+// The 4 BITS stream words of one channel (128 tokens), 16-byte aligned in shared memory.
 template <int BITS>
-constexpr int window_words() { return (26 + 63 * BITS + 6 + BITS + 31) / 32; }
-
-template <int BITS, int TH>
-__device__ __forceinline__ void load_stream(const uint32_t * ch_words, uint32_t (&W)[window_words<BITS>()]) {
-    constexpr int base = TH * 2 * BITS - 1;                     // word index of W[0] within the channel
+__device__ __forceinline__ void load_words(const uint8_t * src, uint32_t (&w)[4 * BITS]) {
 #pragma unroll
-    for (int i = 0; i < window_words<BITS>(); ++i) W[i] = (base + i < 0) ? 0u : ch_words[base + i];
+    for (int i = 0; i < BITS; ++i) {
+        const uint4 x = reinterpret_cast<const uint4 *>(src)[i];
+        w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+    }
 }
-
 template <int BITS>
-__device__ __forceinline__ uint32_t window_of(const uint32_t (&W)[window_words<BITS>()], int j) {
-    const int b = 26 + j * BITS, a = b >> 5, s = b & 31;
-    constexpr uint32_t MASK = (1u << (6 + BITS)) - 1u;
-    if (s + 6 + BITS <= 32) return (W[a] >> s) & MASK;
-    return __funnelshift_r(W[a], W[a + 1], s) & MASK;
+__device__ __forceinline__ uint32_t word_at(const uint32_t (&w)[4 * BITS], int i) { return i < 0 ? 0u : w[i < 0 ? 0 : i]; }
+
+// Byte offset in the lookup table of token 64 TH + j of the channel (copy `lane`): the window (the token's code
+// above the 6 stream bits before it, the bits before the stream reading as zero, sj_kvarn.h:879-900) times 128,
+// plus 4 lane. Token 64 TH + j starts its window at bit 26 + j BITS of the words from index 2 TH BITS - 1 on, for
+// both halves and both widths; with j a compile-time constant this is one shift and one LOP3.
+template <int BITS, int TH>
+__device__ __forceinline__ uint32_t tbl_off(const uint32_t (&w)[4 * BITS], int j, uint32_t lane4) {
+    const int b = 26 + j * BITS, a = b >> 5, s = b & 31, base = TH * 2 * BITS - 1;
+    constexpr uint32_t M7 = ((1u << (6 + BITS)) - 1u) << 7;
+    const uint32_t lo = word_at<BITS>(w, base + a);
+    uint32_t y;
+    if (s >= 7) y = (s + 6 + BITS <= 32) ? (lo >> (s - 7)) : __funnelshift_r(lo, word_at<BITS>(w, base + a + 1), s - 7);
+    else y = lo << (7 - s);
+    return (y & M7) | lane4;
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t * base, uint32_t off) {
+    return *reinterpret_cast<const uint32_t *>(base + off);
 }
 
-// fp16 bits of codebook entry idx (copy `c` of 16 interleaved copies)
-__device__ __forceinline__ uint32_t cb_at(const uint32_t * tbl, uint32_t idx, int c) { return tbl[idx * CB_COPIES + c]; }
-
-// K side: 64 tokens of channel d into the [token][channel] tile
+// K side: the 128 tokens of one channel as fp16 (low table halves) into its 16 MN-major chunks of A_K
 template <int BITS, int TH>
-__device__ __forceinline__ void decode_k(const uint32_t * ch_words, const uint32_t * tbl, int c, uint8_t * tr, int d) {
-    uint32_t W[window_words<BITS>()];
-    load_stream<BITS, TH>(ch_words, W);
+__device__ __forceinline__ void decode_k_half(const uint8_t * tbl, const uint32_t (&w)[4 * BITS], uint32_t lane4, uint8_t * ak_ch) {
 #pragma unroll
-    for (int j = 0; j < 64; ++j)
-        *reinterpret_cast<uint16_t *>(tr + (64 * TH + j) * TRS + 2 * d) = (uint16_t) cb_at(tbl, window_of<BITS>(W, j), c);
+    for (int c = 0; c < 8; ++c) {
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = 8 * c + 2 * i;
+            o[i] = prmt(lds32(tbl, tbl_off<BITS, TH>(w, j, lane4)), lds32(tbl, tbl_off<BITS, TH>(w, j + 1, lane4)), 0x5410u);
+        }
+        *reinterpret_cast<uint4 *>(ak_ch + (8 * TH + c) * AK_SBO) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
 }
-
-// V side: 64 tokens of channel d as fp16 pairs (token 2i low) into the thread's TMEM lane
+// V side: the 128 tokens of one channel as fp16 pairs (high table halves, token 2i low) into the thread's TMEM lane
 template <int BITS, int TH>
-__device__ __forceinline__ void decode_v(const uint32_t * ch_words, const uint32_t * tbl, int c, uint32_t taddr) {
-    uint32_t W[window_words<BITS>()];
-    load_stream<BITS, TH>(ch_words, W);
+__device__ __forceinline__ void decode_v_half(const uint8_t * tbl, const uint32_t (&w)[4 * BITS], uint32_t lane4, uint32_t taddr) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+    for (int hh = 0; hh < 2; ++hh) {
         uint32_t col[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const int j = 32 * h + 2 * i;
-            col[i] = prmt(cb_at(tbl, window_of<BITS>(W, j), c), cb_at(tbl, window_of<BITS>(W, j + 1), c), 0x5410u);
+            const int j = 32 * hh + 2 * i;
+            col[i] = prmt(lds32(tbl, tbl_off<BITS, TH>(w, j, lane4)), lds32(tbl, tbl_off<BITS, TH>(w, j + 1, lane4)), 0x7632u);
         }
-        tc::st_x16(taddr + 16 * h, col);
+        tc::st_x16(taddr + 32 * TH + 16 * hh, col);
     }
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u));
+}
+
+// The CTA's work as a sequence of records over its items: cursor over (item, record)
+struct Cursor {
+    int it, it_end;
+    uint32_t rec, r1;
+    __device__ __forceinline__ void start(const TwParams & p, int i0, int i1) {
+        it = i0; it_end = i1;
+        if (it < it_end) { rec = p.item[it].r0; r1 = p.item[it].r1; }
+    }
+    __device__ __forceinline__ bool first(const TwParams & p) const { return rec == p.item[it].r0; }
+    __device__ __forceinline__ bool last() const { return rec + 1 == r1; }
+    __device__ __forceinline__ void next(const TwParams & p) {
+        if (++rec == r1 && ++it < it_end) { rec = p.item[it].r0; r1 = p.item[it].r1; }
+    }
+};
+
 template <int BK, int BV>
-__global__ void __launch_bounds__(NT, 1) attend_trellis_tc_kernel(TrellisParams p) {
+__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int quarter = warp & 3, grp = warp >> 2, tl = quarter * 32 + lane;
-    const int hl = blockIdx.y, h = p.kv0 + hl, split = blockIdx.x;
-    const sjk_view & v = p.v;
-    const sj_kvarn_layout & l = v.lay;
-    uint8_t * tr = sm + OFF_TR;
-    uint8_t * bk = sm + OFF_BK;
-    uint8_t * bv = sm + OFF_BV;
-    uint32_t * cbk = reinterpret_cast<uint32_t *>(sm + OFF_CBK);
-    uint32_t * cbv = reinterpret_cast<uint32_t *>(sm + OFF_CBV);
-    float * row = reinterpret_cast<float *>(sm + OFF_ROW);
-    float * red = reinterpret_cast<float *>(sm + OFF_RED);
+    const sj_kvarn_layout & l = p.lay;
+    float * F = reinterpret_cast<float *>(sm + OFF_F);
     uint64_t * bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
-    const uint32_t r_begin = p.rec_bounds[split], r_end = p.rec_bounds[split + 1];
-    const uint32_t n = r_end > r_begin ? r_end - r_begin : 0u;
-    const uint32_t rb = l.bytes;
+    volatile int * abort = reinterpret_cast<volatile int *>(sm + OFF_ABORT);
+    const int i0 = p.cta_item[blockIdx.x], i1 = p.cta_item[blockIdx.x + 1];
+    uint32_t n = 0;
+    for (int i = i0; i < i1; ++i) n += p.item[i].r1 - p.item[i].r0;
 
-    if (warp == 0) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
-    if (tid == 0) {
-        tc::mbar_init(&bars[BAR_REC], 1); tc::mbar_init(&bars[BAR_REC + 1], 1); tc::mbar_init(&bars[BAR_MMA], 1);
+    if (warp == W_I) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
+    if (tid == W_I * 32) {
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&bars[B_RFULL + i], 1); tc::mbar_init(&bars[B_REMPTY + i], 20);
+            tc::mbar_init(&bars[B_SFULL + i], 1); tc::mbar_init(&bars[B_SFREE + i], 4);
+            tc::mbar_init(&bars[B_CFULL + i], 1); tc::mbar_init(&bars[B_AZFULL + i], 4);
+            tc::mbar_init(&bars[B_AVFULL + i], 8); tc::mbar_init(&bars[B_VDONE + i], 1);
+        }
+        tc::mbar_init(&bars[B_AKFULL], 8); tc::mbar_init(&bars[B_OFREE], 8);
+        *abort = 0;
         tc::mbar_fence_init();
     }
-    uint32_t issued = 0;                                        // thread 0: records requested so far
-    auto load = [&](uint32_t g) {                                // record g of the range into stage g % 2
-        const uint32_t rec = r_begin + g, blk = v.blocks ? v.blocks[rec] : rec;
-        tc::fence_proxy_async();
-        tc::mbar_expect_tx(&bars[BAR_REC + (g & 1u)], rb);
-        tc::bulk_g2s(sm + OFF_REC + (g & 1u) * REC_MAX, v.body + ((size_t) blk * v.n_head_kv + h) * rb, rb, &bars[BAR_REC + (g & 1u)]);
-        ++issued;
-    };
-    // codebooks (16 interleaved copies) and the per-row state
+    // lookup table: word [idx][c] = cb_K[idx] | cb_V[idx] << 16 for every copy c (rows past a 2-bit table unused)
     {
         const uint16_t * ck = sjk_codebook(BK, 0), * cv = sjk_codebook(BV, 1);
-        for (int i = tid; i < (1 << (6 + BK)) * CB_COPIES; i += NT) cbk[i] = ck[i / CB_COPIES];
-        for (int i = tid; i < (1 << (6 + BV)) * CB_COPIES; i += NT) cbv[i] = cv[i / CB_COPIES];
+        constexpr int NK = 1 << (6 + BK), NV = 1 << (6 + BV), NI = NK > NV ? NK : NV;
+        for (int i = tid; i < NI * 8; i += NT) {
+            const int idx = i >> 3;
+            const uint32_t w = (uint32_t) (idx < NK ? ck[idx] : 0) | ((uint32_t) (idx < NV ? cv[idx] : 0) << 16);
+            reinterpret_cast<uint4 *>(sm + OFF_TBL)[i] = make_uint4(w, w, w, w);
+        }
     }
-    if (tid < NR) { row[ROW_M2 + tid] = -INFINITY; row[ROW_L + tid] = 0.0f; }
-    // this thread's query values for the B_K build: channel tid % 256, rows 8 (tid / 256) ..
-    const int bd = tid & 255, brh = tid >> 8;
-    float q8[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int r = 8 * brh + i;
-        q8[i] = r < p.rows ? __ldg(p.q + (size_t) (p.row_q[r] + hl * p.grp) * D + bd) : 0.0f;
-    }
-    uint32_t qlim4[4];                                          // softmax rows 4 grp + i: positions < qlim4 are visible
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = 4 * grp + i;
-        qlim4[i] = r < p.rows ? p.qpos0 + p.row_iq[r] + 1u : 0u;
-    }
-    if (tid == 0 && n) load(0);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = (uint32_t) (quarter * 32) << 16;
-    const float sl2 = p.scale * LOG2E;
-    const uint32_t idesc = tc::idesc_f16(128, NB);
-    const int cc = lane & (CB_COPIES - 1);
-    float acc[NR];                                              // warps 0..7: running output of channel 128 grp + tl
+    const uint8_t * tbl = sm + OFF_TBL;
+    const uint32_t lane4 = (uint32_t) lane * 4u;
+    const uint32_t rb = l.bytes;
+    Cursor cur;
+    cur.start(p, i0, i1);
+
+    if (warp < W_V) {
+        // ================================ K side ================================
+        const int jp = tid & 127, rh = tid >> 7;               // B_K: channels 2 jp, 2 jp + 1; rows 8 rh ..
+        const int d = tid;                                      // decoding: channel d
+        uint8_t * bk = sm + OFF_BK + TILE_B * (jp >> 6) + h_off(0, (2 * jp) & 127);
+        uint8_t * ak_ch = sm + OFF_AK + (d >> 3) * AK_LBO + (d & 7) * 16;
+        float2 q2[8];
+        for (uint32_t g = 0; g < n; ++g, cur.next(p)) {
+            const TwItem & itm = p.item[cur.it];
+            if (cur.first(p)) {
+                const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
+                const int hl = (int) (itm.seq_hl >> 16);
 #pragma unroll
-    for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
-    bool ok = true, mma_pending = false;
-    uint32_t mma_phase = 0;
-    const uint32_t b_end = p.B < p.N ? p.B : p.N;
-    // everyone: operand stores visible to the async proxy, then thread 0 issues; wait_mma: everyone waits
-    auto issue = [&](bool k_side) {
-        tc::wait_st();
-        tc::fence_proxy_async();
-        tc::fence_before_sync();
-        __syncthreads();
-        tc::fence_after_sync();
-        if (tid == 0) {
-            if (k_side) {
+                for (int i = 0; i < 8; ++i) {
+                    const int r = 8 * rh + i;
+                    q2[i] = r < p.rows ? __ldg(reinterpret_cast<const float2 *>(sq.q + (size_t) (p.row_q[r] + hl * p.grp) * D) + jp)
+                                       : make_float2(0.0f, 0.0f);
+                }
+            }
+            const uint32_t s = g & 1u;
+            // every K warp reaches the group barrier below on every record, also after a wait gave up
+            bool ok = warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
+                      (g == 0 || warp_wait(&bars[B_SFULL + ((g - 1) & 1u)], ((g - 1) >> 1) & 1u, abort));
+            if (ok) {
+                tc::fence_after_sync();
+                const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
+                // B_K and the zero-point partials
+                {
+                    const float2 ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
+                    const float2 kz = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_zero + 4 * jp));
+                    float cz[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int r = 8 * rh + i;
+                        const float2 x = make_float2(q2[i].x * ks.x, q2[i].y * ks.y);
+                        const __half2 hi = __floats2half2_rn(x.x, x.y);
+                        const float2 hf = __half22float2(hi);
+                        const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
+                        *reinterpret_cast<__half2 *>(bk + r * 16) = hi;
+                        *reinterpret_cast<__half2 *>(bk + (NR + r) * 16) = lo;
+                        cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
+                    }
+                    const float cw = warp_rows8<false>(cz, lane);
+                    if ((lane & 3) == 0) F[F_REDC + s * 64 + warp * 8 + (lane >> 2)] = cw;
+                }
+                // A_K: channel d, all 128 tokens
+                {
+                    uint32_t w[4 * BK];
+                    load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
+                    decode_k_half<BK, 0>(tbl, w, lane4, ak_ch);
+                    decode_k_half<BK, 1>(tbl, w, lane4, ak_ch);
+                }
+                tc::fence_proxy_async();
+            }
+            if (!tc::nbar_and(1, 256, ok)) break;               // zero-point partials of all K warps in place
+            if (warp == 0 && lane < NR) {
+                const int r = lane, base = (r >> 3) * 4;
+                const float * rc = F + F_REDC + s * 64 + (r & 7);
+                F[F_C + s * NR + r] = (rc[8 * base] + rc[8 * (base + 1)]) + (rc[8 * (base + 2)] + rc[8 * (base + 3)]);
+            }
+            if (warp == 0) warp_arrive(&bars[B_CFULL + s], lane);
+            warp_arrive(&bars[B_AKFULL], lane);
+            warp_arrive(&bars[B_REMPTY + s], lane);
+        }
+    } else if (warp < W_S) {
+        // ================================ V side ================================
+        const int vw = warp - W_V, tile = vw >> 2, quarter = warp & 3;
+        const int d = 128 * tile + 32 * quarter + lane;
+        const uint32_t lane_base = (uint32_t) (32 * quarter) << 16;
+        float acc[NR];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+        float vc_prev = 0.0f;
+        Cursor ecur = cur;                                      // the epilogue's cursor lags one record
+        // epilogue of record e: acc = acc alpha + Vc (O + z); at the end of an item its outputs leave as partials
+        uint32_t e3 = 0;                                        // e % 3: the softmax's alpha / z slot of record e
+        auto epilogue = [&](uint32_t e, float vc) -> bool {
+            const uint32_t es = e & 1u;
+            if (!warp_wait(&bars[B_VDONE + es], (e >> 1) & 1u, abort)) return false;
+            if (!warp_wait(&bars[B_AZFULL + es], (e >> 1) & 1u, abort)) return false;
+            tc::fence_after_sync();
+            float o[16], ol[16], al[16], z[16];
+            tc::ld_x16(tmem + lane_base + COL_O + 32 * tile, o);
+            tc::ld_x16(tmem + lane_base + COL_O + 32 * tile + NR, ol);
+            ld8(F + F_AL + e3 * NR, *reinterpret_cast<float (*)[8]>(al));
+            ld8(F + F_AL + e3 * NR + 8, *reinterpret_cast<float (*)[8]>(al + 8));
+            ld8(F + F_Z + e3 * NR, *reinterpret_cast<float (*)[8]>(z));
+            ld8(F + F_Z + e3 * NR + 8, *reinterpret_cast<float (*)[8]>(z + 8));
+            tc::wait_ld();
+            tc::fence_before_sync();
+            warp_arrive(&bars[B_OFREE], lane);
+            e3 = e3 == 2 ? 0 : e3 + 1;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], al[r], vc * ((o[r] + ol[r]) + z[r]));
+            if (ecur.last()) {
+                const TwItem & itm = p.item[ecur.it];
+                const int hl = (int) (itm.seq_hl >> 16), slot = (int) (itm.h_slot >> 16);
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    if (r < p.rows)
+                        p.part[((size_t) slot * p.n_rows + (size_t) (p.row_q[r] + hl * p.grp)) * (D + 2) + 2 + d] = acc[r];
+                    acc[r] = 0.0f;
+                }
+            }
+            ecur.next(p);
+            return true;
+        };
+        bool ok = true;
+        for (uint32_t g = 0; g < n; ++g) {
+            const uint32_t s = g & 1u;
+            if (!warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort)) { ok = false; break; }
+            if (g > 1 && !warp_wait(&bars[B_VDONE + s], ((g - 2) >> 1) & 1u, abort)) { ok = false; break; }
+            tc::fence_after_sync();
+            const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
+            {
+                uint32_t w[4 * BV];
+                load_words<BV>(rec + l.v_payload + d * (16 * BV), w);
+                const uint32_t ta = tmem + lane_base + COL_AV + 128 * s + 64 * tile;
+                decode_v_half<BV, 0>(tbl, w, lane4, ta);
+                decode_v_half<BV, 1>(tbl, w, lane4, ta);
+            }
+            const float vc = h2f_at(rec + l.v_ch + 2 * d);
+            tc::wait_st();
+            tc::fence_before_sync();
+            warp_arrive(&bars[B_AVFULL + s], lane);
+            warp_arrive(&bars[B_REMPTY + s], lane);
+            if (g > 0 && !epilogue(g - 1, vc_prev)) { ok = false; break; }
+            vc_prev = vc;
+        }
+        if (ok && n > 0) epilogue(n - 1, vc_prev);
+    } else if (warp < W_I) {
+        // ================================ softmax ================================
+        const int quarter = warp & 3, t = 32 * quarter + lane;
+        const uint32_t lane_base = (uint32_t) (32 * quarter) << 16;
+        const float sl2 = p.scale * LOG2E;
+        float M = -INFINITY, L = 0.0f;                          // warp W_S, lane r < 16: running max / sum of row r
+        uint32_t g3 = 0;                                        // g % 3: slot of alpha / z (the epilogue of g - 3 is done)
+        for (uint32_t g = 0; g < n; ++g, cur.next(p), g3 = g3 == 2 ? 0 : g3 + 1) {
+            const TwItem & itm = p.item[cur.it];
+            const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
+            if (cur.first(p)) { M = -INFINITY; L = 0.0f; }
+            const uint32_t s = g & 1u;
+            // every softmax warp reaches the group barriers below on every record, also after a wait gave up
+            bool ok = warp_wait(&bars[B_SFULL + s], (g >> 1) & 1u, abort) && warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
+                      warp_wait(&bars[B_CFULL + s], (g >> 1) & 1u, abort);
+            float sc[16], vsc = 0.0f, vz = 0.0f;
+            if (ok) {
+                tc::fence_after_sync();
+                uint32_t a[16], al[16];
+                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
+                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + NR, al);
+                tc::wait_ld();
+                tc::fence_before_sync();
+                warp_arrive(&bars[B_SFREE + s], lane);
+                const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
+                const float kt = h2f_at(rec + l.k_tok + 2 * t);
+                vsc = h2f_at(rec + l.v_scale + 2 * t);
+                vz = h2f_at(rec + l.v_zero + 2 * t);
+                float c[16];
+                ld8(F + F_C + s * NR, *reinterpret_cast<float (*)[8]>(c));
+                ld8(F + F_C + s * NR + 8, *reinterpret_cast<float (*)[8]>(c + 8));
+                warp_arrive(&bars[B_REMPTY + s], lane);
+                const uint32_t pos = sq.S + cur.rec * (uint32_t) G + (uint32_t) t;
+                const bool in = pos < sq.b_end;
+                const float kts = kt * sl2;
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    const bool vis = in && r < p.rows && pos < sq.qpos0 + p.row_iq[r] + 1u;
+                    sc[r] = vis ? kts * ((__uint_as_float(a[r]) + __uint_as_float(al[r])) + c[r]) : -INFINITY;
+                }
+                const float mw = warp_rows16<true>(sc, lane);
+                if ((lane & 1) == 0) F[F_REDM + quarter * NR + (lane >> 1)] = mw;
+            }
+            if (!tc::nbar_and(2, 128, ok)) break;
+            if (warp == W_S && lane < NR) {
+                const int r = lane;
+                const float mrec = fmaxf(fmaxf(F[F_REDM + r], F[F_REDM + NR + r]), fmaxf(F[F_REDM + 2 * NR + r], F[F_REDM + 3 * NR + r]));
+                const float mnew = fmaxf(M, mrec);
+                F[F_AL + g3 * NR + r] = mnew == -INFINITY ? 1.0f : ex2(M - mnew);
+                F[F_MN + r] = mnew;
+                M = mnew;
+            }
+            tc::nbar_sync(2, 128);
+            float mn[16];
+            ld8(F + F_MN, *reinterpret_cast<float (*)[8]>(mn));
+            ld8(F + F_MN + 8, *reinterpret_cast<float (*)[8]>(mn + 8));
+            // B_V is free once the V MMAs of the previous record completed
+            ok = g == 0 || warp_wait(&bars[B_VDONE + (s ^ 1u)], ((g - 1) >> 1) & 1u, abort);
+            if (ok) {
+                uint8_t * bv = sm + OFF_BV;
+                float ls[16], zs[16];
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {
+                    const float pw = mn[r] == -INFINITY ? 0.0f : ex2(sc[r] - mn[r]);
+                    ls[r] = pw;
+                    zs[r] = pw * vz;
+                    const float x = pw * vsc;
+                    const __half hi = __float2half_rn(x);
+                    *reinterpret_cast<__half *>(bv + h_off(r, t)) = hi;
+                    *reinterpret_cast<__half *>(bv + h_off(NR + r, t)) = __float2half_rn(x - __half2float(hi));
+                }
+                const float lw = warp_rows16<false>(ls, lane), zw = warp_rows16<false>(zs, lane);
+                if ((lane & 1) == 0) { F[F_REDL + quarter * NR + (lane >> 1)] = lw; F[F_REDZ + quarter * NR + (lane >> 1)] = zw; }
+                tc::fence_proxy_async();
+            }
+            if (!tc::nbar_and(2, 128, ok)) break;
+            if (warp == W_S && lane < NR) {
+                const int r = lane;
+                const float lsum = (F[F_REDL + r] + F[F_REDL + NR + r]) + (F[F_REDL + 2 * NR + r] + F[F_REDL + 3 * NR + r]);
+                L = L * F[F_AL + g3 * NR + r] + lsum;
+                F[F_Z + g3 * NR + r] = (F[F_REDZ + r] + F[F_REDZ + NR + r]) + (F[F_REDZ + 2 * NR + r] + F[F_REDZ + 3 * NR + r]);
+                if (cur.last() && r < p.rows) {
+                    const int hl = (int) (itm.seq_hl >> 16), slot = (int) (itm.h_slot >> 16);
+                    float * dst = p.part + ((size_t) slot * p.n_rows + (size_t) (p.row_q[r] + hl * p.grp)) * (D + 2);
+                    dst[0] = M == -INFINITY ? M : M * LN2;
+                    dst[1] = L;
+                }
+            }
+            warp_arrive(&bars[B_AZFULL + s], lane);
+        }
+    } else if (lane == 0) {
+        // ================================ issuer ================================
+        const uint32_t idesc_k = tc::idesc_f16(128, NB) | (1u << 15);    // A MN-major (tokens contiguous per channel)
+        const uint32_t idesc_v = tc::idesc_f16(128, NB);
+        uint32_t nl = 0, nk = 0, nv = 0;
+        Cursor lc = cur;
+        int last_commit = -1;                                   // barrier index of the last commit
+        uint32_t last_parity = 0;
+        uint64_t t_last = tc::globaltimer();
+        while (nv < n) {
+            bool progress = false;
+            if (nl < n && (nl < 2 || tc::mbar_test(&bars[B_REMPTY + (nl & 1u)], ((nl - 2) >> 1) & 1u))) {
+                const TwItem & itm = p.item[lc.it];
+                const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
+                const uint32_t blk = sq.blocks ? sq.blocks[lc.rec] : lc.rec;
+                const uint32_t h = itm.h_slot & 0xFFFFu;
+                tc::mbar_expect_tx(&bars[B_RFULL + (nl & 1u)], rb);
+                tc::bulk_g2s(sm + OFF_REC + (nl & 1u) * REC_MAX, sq.body + ((size_t) blk * p.n_head_kv + h) * rb, rb,
+                             &bars[B_RFULL + (nl & 1u)]);
+                ++nl;
+                lc.next(p);
+                progress = true;
+            }
+            if (nk < nl && tc::mbar_test(&bars[B_AKFULL], nk & 1u) &&
+                (nk < 2 || tc::mbar_test(&bars[B_SFREE + (nk & 1u)], ((nk - 2) >> 1) & 1u))) {
+                tc::fence_after_sync();
+                const uint32_t dcol = tmem + COL_S + 32 * (nk & 1u);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const uint64_t db = tc::smem_desc(bk + TILE_B * (j >> 3), HCH, 128) + (uint64_t) ((2 * HCH * (j & 7)) >> 4);
-                    tc::mma_ts(tmem + COL_S, tmem + COL_AK + 8 * j, db, idesc, j ? 1u : 0u);
+                    const uint64_t da = tc::smem_desc(sm + OFF_AK + 2 * AK_LBO * j, AK_LBO, AK_SBO);
+                    const uint64_t db = tc::smem_desc(sm + OFF_BK + TILE_B * (j >> 3), HCH, 128) + (uint64_t) ((2 * HCH * (j & 7)) >> 4);
+                    mma_ss(dcol, da, db, idesc_k, j ? 1u : 0u);
                 }
-            } else {
+                tc::mma_commit(&bars[B_SFULL + (nk & 1u)]);
+                last_commit = (int) (B_SFULL + (nk & 1u)); last_parity = (nk >> 1) & 1u;
+                ++nk;
+                progress = true;
+            }
+            if (nv < nk && tc::mbar_test(&bars[B_AZFULL + (nv & 1u)], (nv >> 1) & 1u) &&
+                tc::mbar_test(&bars[B_AVFULL + (nv & 1u)], (nv >> 1) & 1u) && (nv < 1 || tc::mbar_test(&bars[B_OFREE], (nv - 1) & 1u))) {
+                tc::fence_after_sync();
 #pragma unroll
                 for (int tile = 0; tile < 2; ++tile)
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
-                        const uint64_t db = tc::smem_desc(bv, HCH, 128) + (uint64_t) ((2 * HCH * k) >> 4);
-                        tc::mma_ts(tmem + COL_O + 32 * tile, tmem + COL_AV + 64 * tile + 8 * k, db, idesc, k ? 1u : 0u);
+                        const uint64_t db = tc::smem_desc(sm + OFF_BV, HCH, 128) + (uint64_t) ((2 * HCH * k) >> 4);
+                        tc::mma_ts(tmem + COL_O + 32 * tile, tmem + COL_AV + 128 * (nv & 1u) + 64 * tile + 8 * k, db, idesc_v, k ? 1u : 0u);
                     }
+                tc::mma_commit(&bars[B_VDONE + (nv & 1u)]);
+                last_commit = (int) (B_VDONE + (nv & 1u)); last_parity = (nv >> 1) & 1u;
+                ++nv;
+                progress = true;
             }
-            tc::mma_commit(&bars[BAR_MMA]);
+            const uint64_t now = tc::globaltimer();
+            if (progress) t_last = now;
+            else if (*abort) break;
+            else if (now - t_last > SJK_WAIT_NS) { atomicExch(&sjk_dev_status, SJK_DEV_TIMEOUT); *abort = 1; break; }
         }
-        mma_pending = true;
-    };
-    auto wait_mma = [&]() -> bool {
-        const bool got = __syncthreads_and(tc::mbar_wait(&bars[BAR_MMA], mma_phase));
-        if (got) { mma_phase ^= 1u; mma_pending = false; }
-        tc::fence_after_sync();
-        return got;
-    };
-
-    uint32_t arrived = 0;                                       // records whose bytes every thread has seen land
-    for (uint32_t g = 0; g < n && ok; ++g) {
-        const uint32_t s = g & 1u;
-        const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
-        ok = __syncthreads_and(tc::mbar_wait(&bars[BAR_REC + s], (g >> 1) & 1u));
-        if (!ok) break;
-        arrived = g + 1;
-        if (tid == 0 && g + 1 < n) load(g + 1);                 // the other stage was released at the end of g - 1
-        const uint32_t gg = r_begin + g, p0 = p.S + gg * (uint32_t) G;
-        const uint32_t len = min((uint32_t) G, b_end - p0);
-        // ---- B_K = [Q' hi | Q' lo] (channel bd, rows 8 brh ..) and the zero-point partials ----
-        {
-            const float ks = h2f_at(rec + l.k_scale + 2 * bd), kz = h2f_at(rec + l.k_zero + 2 * bd);
-            uint8_t * bt = bk + TILE_B * (bd >> 7);
-            float cz[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = 8 * brh + i;
-                const float x = q8[i] * ks;
-                const __half hi = __float2half_rn(x);
-                *reinterpret_cast<__half *>(bt + h_off(r, bd & 127)) = hi;
-                *reinterpret_cast<__half *>(bt + h_off(NR + r, bd & 127)) = __float2half_rn(x - __half2float(hi));
-                cz[i] = q8[i] * kz;
-            }
-            const float cw = warp_rows8<false>(cz, lane);
-            if ((lane & 3) == 0) red[RED_C + warp * 8 + (lane >> 2)] = cw;
-        }
-        // ---- K values of channel bd, tokens 64 brh .. into the [token][channel] tile ----
-        {
-            const uint32_t * cw = reinterpret_cast<const uint32_t *>(rec + l.k_payload) + bd * (4 * BK);
-            if (brh == 0) decode_k<BK, 0>(cw, cbk, cc, tr, bd);
-            else decode_k<BK, 1>(cw, cbk, cc, tr, bd);
-        }
-        __syncthreads();
-        if (tid < NR) {                                        // C[r]: the eight warps of the row's half
-            const int r = tid, base = (r >> 3) * 8;
-            float c = 0.0f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) c += red[RED_C + (base + w) * 8 + (r & 7)];
-            row[ROW_C + r] = c;
-        }
-        // ---- A_K: token tl, channels 64 grp .. 64 grp + 63 ----
-        {
-            const uint4 * src = reinterpret_cast<const uint4 *>(tr + tl * TRS + 128 * grp);
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                uint32_t col[16];
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const uint4 x = src[4 * hh + c4];
-                    col[4 * c4] = x.x; col[4 * c4 + 1] = x.y; col[4 * c4 + 2] = x.z; col[4 * c4 + 3] = x.w;
-                }
-                tc::st_x16(tmem + lane_base + COL_AK + 32 * grp + 16 * hh, col);
-            }
-        }
-        issue(true);
-        // ---- A_V (while the K MMAs run): channel 128 (grp / 2) + tl, tokens 64 (grp % 2) .. ----
-        {
-            const int d = 128 * (grp >> 1) + tl;
-            const uint32_t * cw = reinterpret_cast<const uint32_t *>(rec + l.v_payload) + d * (4 * BV);
-            const uint32_t ta = tmem + lane_base + COL_AV + 64 * (grp >> 1) + 32 * (grp & 1);
-            if (grp & 1) decode_v<BV, 1>(cw, cbv, cc, ta);
-            else decode_v<BV, 0>(cw, cbv, cc, ta);
-        }
-        ok = wait_mma();
-        if (!ok) break;
-        // ---- scores of token tl for rows 4 grp .. 4 grp + 3 (log2 domain), row maxima ----
-        float s2[4];
-        const float kt = h2f_at(rec + l.k_tok + 2 * tl), vsc = h2f_at(rec + l.v_scale + 2 * tl), vz = h2f_at(rec + l.v_zero + 2 * tl);
-        {
-            uint32_t a[4], al[4];
-            tc::ld_x4_u(tmem + lane_base + COL_S + 4 * grp, a);
-            tc::ld_x4_u(tmem + lane_base + COL_S + NR + 4 * grp, al);
-            tc::wait_ld();
-            const float kts = kt * sl2;
-            const uint32_t pos = p0 + (uint32_t) tl;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float dot = kts * ((__uint_as_float(a[i]) + __uint_as_float(al[i])) + row[ROW_C + 4 * grp + i]);
-                s2[i] = ((uint32_t) tl < len && pos < qlim4[i]) ? dot : -INFINITY;
-            }
-            const float mw = warp_rows4<true>(s2, lane);
-            if ((lane & 7) == 0) red[RED_MAX + (grp * 4 + quarter) * 4 + (lane >> 3)] = mw;
-        }
-        __syncthreads();
-        if (tid < NR) {
-            const int r = tid, gq = (r >> 2) * 16 + (r & 3);
-            const float mrec = fmaxf(fmaxf(red[RED_MAX + gq], red[RED_MAX + gq + 4]), fmaxf(red[RED_MAX + gq + 8], red[RED_MAX + gq + 12]));
-            const float mold = row[ROW_M2 + r], mnew = fmaxf(mold, mrec);
-            row[ROW_MNEW + r] = mnew;
-            row[ROW_ALPHA + r] = mnew == -INFINITY ? 1.0f : ex2(mold - mnew);
-            row[ROW_M2 + r] = mnew;
-        }
-        __syncthreads();
-        // ---- P' = p Vscale as [hi | lo] (B of the V MMAs), row sums of p and p Vzero ----
-        {
-            float ls[4], zs[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = 4 * grp + i;
-                const float mnew = row[ROW_MNEW + r];
-                const float pw = mnew == -INFINITY ? 0.0f : ex2(s2[i] - mnew);
-                ls[i] = pw;
-                zs[i] = pw * vz;
-                const float x = pw * vsc;
-                const __half hi = __float2half_rn(x);
-                *reinterpret_cast<__half *>(bv + h_off(r, tl)) = hi;
-                *reinterpret_cast<__half *>(bv + h_off(NR + r, tl)) = __float2half_rn(x - __half2float(hi));
-            }
-            const float lw = warp_rows4<false>(ls, lane), zw = warp_rows4<false>(zs, lane);
-            if ((lane & 7) == 0) {
-                red[RED_L + (grp * 4 + quarter) * 4 + (lane >> 3)] = lw;
-                red[RED_Z + (grp * 4 + quarter) * 4 + (lane >> 3)] = zw;
-            }
-        }
-        issue(false);                                           // (its barrier makes the row sums visible)
-        if (tid < NR) {
-            const int r = tid, gq = (r >> 2) * 16 + (r & 3);
-            const float lsum = (red[RED_L + gq] + red[RED_L + gq + 4]) + (red[RED_L + gq + 8] + red[RED_L + gq + 12]);
-            row[ROW_L + r] = row[ROW_L + r] * row[ROW_ALPHA + r] + lsum;
-            row[ROW_Z + r] = (red[RED_Z + gq] + red[RED_Z + gq + 4]) + (red[RED_Z + gq + 8] + red[RED_Z + gq + 12]);
-        }
-        ok = wait_mma();
-        if (!ok) break;
-        // ---- epilogue (warps 0..7): channel 128 grp + tl, all rows ----
-        if (grp < 2) {
-            const float vc = h2f_at(rec + l.v_ch + 2 * (128 * grp + tl));
-            float o[16], ol[16];
-            tc::ld_x16(tmem + lane_base + COL_O + 32 * grp, o);
-            tc::ld_x16(tmem + lane_base + COL_O + 32 * grp + NR, ol);
-            tc::wait_ld();
-#pragma unroll
-            for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], row[ROW_ALPHA + r], vc * ((o[r] + ol[r]) + row[ROW_Z + r]));
-        }
-        tc::fence_before_sync();
-        __syncthreads();                                        // stage s, the B operands and TMEM free again
-        tc::fence_after_sync();
-    }
-    if (mma_pending) tc::mbar_wait(&bars[BAR_MMA], mma_phase);  // a record that gave up: its MMAs first (bounded)
-    if (tid == 0)                                               // and a copy still in flight lands before the CTA exits
-        for (uint32_t j = arrived; j < issued; ++j) tc::mbar_wait(&bars[BAR_REC + (j & 1u)], (j >> 1) & 1u);
-    __syncthreads();
-    // ---- partials (m in the natural-log domain, l, o[D]) per real query row ----
-    if (grp < 2) {
-#pragma unroll
-        for (int r = 0; r < NR; ++r) {
-            if (r < p.rows) {
-                float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) (p.row_q[r] + hl * p.grp)) * (D + 2);
-                dst[2 + 128 * grp + tl] = ok ? acc[r] : 0.0f;
-            }
-        }
-    }
-    if (tid < p.rows) {
-        const int r = tid;
-        float * dst = p.part + ((size_t) (p.split0 + split) * p.n_q * p.n_head + (size_t) (p.row_q[r] + hl * p.grp)) * (D + 2);
-        const float m2 = row[ROW_M2 + r];
-        dst[0] = ok ? (m2 == -INFINITY ? m2 : m2 * LN2) : -INFINITY;
-        dst[1] = ok ? row[ROW_L + r] : 0.0f;
+        // drain: the copies still in flight (at most the last two) and the MMAs behind the last commit
+        for (uint32_t j = nl > 2 ? nl - 2 : 0; j < nl; ++j) tc::mbar_wait(&bars[B_RFULL + (j & 1u)], (j >> 1) & 1u);
+        if (last_commit >= 0) tc::mbar_wait(&bars[last_commit], last_parity);
     }
     tc::fence_before_sync();
     __syncthreads();
-    if (warp == 0) tc::tmem_dealloc(tmem, TM_COLS);
+    tc::fence_after_sync();
+    if (warp == W_I) tc::tmem_dealloc(tmem, TM_COLS);
+}
+
+template <int BK, int BV>
+int launch_kernel(const TwParams & p, sjk_stream st) {
+    auto kfn = attend_trellis_ws_kernel<BK, BV>;
+    const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    if (e != cudaSuccess) return sjk_check(e);
+    kfn<<<(unsigned) p.n_cta, NT, SMEM_TOTAL, st>>>(p);
+    return sjk_check_launch();
+}
+
+int launch(const TwParams & p, sjk_stream st) {
+    const int bk = p.lay.bits_k, bv = p.lay.bits_v;
+    if (bk == 3) return bv == 3 ? launch_kernel<3, 3>(p, st) : launch_kernel<3, 2>(p, st);
+    return bv == 3 ? launch_kernel<2, 3>(p, st) : launch_kernel<2, 2>(p, st);
+}
+
+void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
+    p.grp = n_head / n_kv;
+    p.rows = n_q * p.grp;
+    p.n_rows = n_q * n_head;
+    for (int r = 0; r < NR; ++r) {
+        const int iq = r < p.rows ? r / p.grp : 0, g = r < p.rows ? r % p.grp : 0;
+        p.row_iq[r] = (uint32_t) iq;
+        p.row_q[r] = iq * n_head + g;
+    }
 }
 
 }  // namespace
@@ -410,39 +593,101 @@ int sjk_tc_trellis_supported(const sjk_view * v, int n_q, int grp) {
     const sj_kvarn_layout & l = v->lay;
     const bool bits_ok = (l.bits_k == 2 || l.bits_k == 3) && (l.bits_v == 2 || l.bits_v == 3);
     return l.D == D && l.G == G && l.body == SJKVARN_BODY_TRELLIS && bits_ok && n_q * grp <= NR && l.bytes <= REC_MAX &&
-           l.bytes % 16 == 0 && l.k_payload % 16 == 0 && l.v_payload % 16 == 0;
+           l.bytes % 16 == 0 && l.k_payload % 16 == 0 && l.v_payload % 16 == 0 && l.k_scale % 4 == 0 && l.k_zero % 4 == 0 &&
+           v->n_head_kv <= MAX_CTAS;
 }
 
-// Splits (persistent CTAs) per KV head: one CTA per SM over the call's KV heads.
+// Splits (persistent CTAs) per KV head of a one-sequence call: one CTA per SM over the call's KV heads.
 int sjk_tc_trellis_max_splits(int n_kv) {
-    const int t = (148 + (n_kv > 0 ? n_kv : 1) - 1) / (n_kv > 0 ? n_kv : 1);
-    return t < MAX_SPLITS ? t : MAX_SPLITS;
+    const int t = (MAX_CTAS + (n_kv > 0 ? n_kv : 1) - 1) / (n_kv > 0 ? n_kv : 1);
+    return t < MAX_CTAS ? t : MAX_CTAS;
 }
 
+// One sequence: records [0, n_rec) of KV heads kv0 .. kv0 + n_kv - 1, each head split into `splits` contiguous
+// ranges; item (head, split) is CTA hl * splits + split and writes partial slot split0 + split.
 int sjk_tc_trellis_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head,
                           int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                           sjk_stream st) {
-    TrellisParams p;
-    p.v = *v; p.kv0 = kv0; p.S = v->S; p.B = B; p.N = N; p.qpos0 = qpos0; p.n_rec = n_rec;
-    p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
-    for (int r = 0; r < NR; ++r) {
-        const int iq = r < p.rows ? r / p.grp : 0, g = r < p.rows ? r % p.grp : 0;
-        p.row_iq[r] = (uint32_t) iq;
-        p.row_q[r] = iq * n_head + g;
-    }
-    p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
     int splits = sjk_tc_trellis_max_splits(n_kv);
     if ((uint32_t) splits > n_rec) splits = (int) n_rec;
+    while (splits * n_kv > MAX_CTAS) --splits;
     *splits_out = splits;
-    if (splits == 0) return 0;
-    for (int s = 0; s <= splits; ++s) p.rec_bounds[s] = (uint32_t) (((uint64_t) n_rec * (uint32_t) s) / (uint32_t) splits);
-    const int bk = v->lay.bits_k, bv = v->lay.bits_v;
-    auto kfn = bk == 3 ? (bv == 3 ? attend_trellis_tc_kernel<3, 3> : attend_trellis_tc_kernel<3, 2>)
-                       : (bv == 3 ? attend_trellis_tc_kernel<2, 3> : attend_trellis_tc_kernel<2, 2>);
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
-    if (e != cudaSuccess) return sjk_check(e);
-    kfn<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
-    return sjk_check_launch();
+    if (splits <= 0) return 0;
+    if (split0 + splits > 0xFFFF) return SJK_ERR_UNSUPPORTED;
+    static thread_local TwParams p;
+    p.lay = v->lay; p.n_head_kv = v->n_head_kv; p.scale = scale; p.part = part;
+    fill_rows(p, n_q, n_head, n_kv);
+    p.seq[0].body = v->body; p.seq[0].blocks = v->blocks; p.seq[0].q = q; p.seq[0].S = v->S;
+    p.seq[0].b_end = B < N ? B : N; p.seq[0].qpos0 = qpos0; p.seq[0].pad = 0;
+    int k = 0;
+    for (int hl = 0; hl < n_kv; ++hl)
+        for (int s = 0; s < splits; ++s, ++k) {
+            TwItem & it = p.item[k];
+            it.seq_hl = (uint32_t) hl << 16;
+            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
+            it.r0 = (uint32_t) (((uint64_t) n_rec * (uint32_t) s) / (uint32_t) splits);
+            it.r1 = (uint32_t) (((uint64_t) n_rec * (uint32_t) (s + 1)) / (uint32_t) splits);
+            p.cta_item[k] = (uint16_t) k;
+        }
+    p.cta_item[k] = (uint16_t) k;
+    p.n_cta = k;
+    return launch(p, st);
+}
+
+// Many sequences of one layer (same layout as views[0]): sequence s attends with query rows q + s n_q n_head D over its
+// body records [0, ceil((min(B, N) - S) / 128)). The records of all (sequence, KV head) pairs, in that order, are cut
+// into at most one contiguous range per SM, each range into items that stay inside one pair; items get partial slots
+// slot0, slot0 + 1, ...; for pair (s, h) the items are slots first[s H + h] .. first[s H + h + 1] - 1.
+int sjk_tc_trellis_batch_launch(const sjk_view * views, const uint32_t * B, const uint32_t * N, const uint32_t * qpos0,
+                                int n_seq, int n_q, int n_head, const float * q, float scale, float * part, int slot0,
+                                uint16_t * first, int * n_items, sjk_stream st) {
+    const sjk_view & v0 = views[0];
+    const int H = v0.n_head_kv;
+    if (n_seq > MAX_SEQS || n_seq * H + MAX_CTAS > MAX_ITEMS) return SJK_ERR_UNSUPPORTED;
+    static thread_local TwParams p;
+    static thread_local uint32_t n_rec[MAX_SEQS];
+    p.lay = v0.lay; p.n_head_kv = H; p.scale = scale; p.part = part;
+    fill_rows(p, n_q, n_head, H);
+    uint64_t total = 0;
+    for (int s = 0; s < n_seq; ++s) {
+        const uint32_t b_end = B[s] < N[s] ? B[s] : N[s];
+        TwSeq & sq = p.seq[s];
+        sq.body = views[s].body; sq.blocks = views[s].blocks; sq.q = q + (size_t) s * n_q * n_head * D;
+        sq.S = v0.S; sq.b_end = b_end; sq.qpos0 = qpos0[s]; sq.pad = 0;
+        n_rec[s] = b_end > v0.S ? (b_end - v0.S + 127u) / 128u : 0u;
+        total += (uint64_t) n_rec[s] * (uint32_t) H;
+    }
+    const int n_cta = total < (uint64_t) MAX_CTAS ? (int) total : MAX_CTAS;
+    int k = 0, cta = 0;
+    if (n_cta > 0) {
+        const uint64_t per = (total + (uint64_t) n_cta - 1) / (uint64_t) n_cta;
+        uint64_t filled = 0;
+        p.cta_item[0] = 0;
+        for (int s = 0; s < n_seq; ++s)
+            for (int h = 0; h < H; ++h) {
+                first[s * H + h] = (uint16_t) (slot0 + k);
+                uint32_t r = 0;
+                while (r < n_rec[s]) {
+                    const uint32_t take = (uint32_t) (per - filled < (uint64_t) (n_rec[s] - r) ? per - filled : (uint64_t) (n_rec[s] - r));
+                    if (k >= MAX_ITEMS || slot0 + k > 0xFFFF) return SJK_ERR_UNSUPPORTED;
+                    TwItem & it = p.item[k++];
+                    it.seq_hl = (uint32_t) s | ((uint32_t) h << 16);
+                    it.h_slot = (uint32_t) h | ((uint32_t) (slot0 + k - 1) << 16);
+                    it.r0 = r; it.r1 = r + take;
+                    r += take;
+                    filled += take;
+                    if (filled == per) { p.cta_item[++cta] = (uint16_t) k; filled = 0; }
+                }
+            }
+        if (filled > 0) p.cta_item[++cta] = (uint16_t) k;
+    } else {
+        for (int i = 0; i < n_seq * H; ++i) first[i] = (uint16_t) slot0;
+    }
+    first[n_seq * H] = (uint16_t) (slot0 + k);
+    *n_items = k;
+    p.n_cta = cta;
+    if (cta == 0) return 0;
+    return launch(p, st);
 }
 
 SJK_STATUS_READER(sjk_tc_trellis_status_take)

@@ -631,6 +631,22 @@ extern "C" void sj_kvarn_seq_store(sj_kvarn_seq * s, uint32_t pos, const float *
     if (pos + 1u > s->n) s->n = pos + 1u;
 }
 
+// Prefill form of sj_kvarn_seq_store: n_pos consecutive positions of every layer in one call per layer. Layer il's rows
+// are DEVICE [n_pos][n_head_kv][D] floats at k + il layer_stride (0: n_pos n_head_kv D), rotated (rotate = 0) or in
+// the model basis (rotate = 1).
+extern "C" int sjk_seq_store(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_pos, const float * k, const float * v,
+                             size_t layer_stride, int rotate, sjk_stream st) {
+    if (!s || !k || !v || pos0 > s->n) return SJKVARN_ERR_ARG;
+    if (n_pos == 0) return 0;
+    const size_t stride = layer_stride ? layer_stride : (size_t) n_pos * (size_t) s->cfg.n_head_kv * (size_t) s->cfg.head_dim;
+    for (int il = 0; il < s->n_layers; ++il) {
+        const int rc = sjk_layer_store(&s->layers[il], pos0, n_pos, k + (size_t) il * stride, v + (size_t) il * stride, rotate, st);
+        if (rc) return rc;
+    }
+    if (pos0 + n_pos > s->n) s->n = pos0 + n_pos;
+    return 0;
+}
+
 extern "C" int sj_kvarn_seq_idle(sj_kvarn_seq * s, uint32_t keep_recent) {
     const sj_kvarn_policy before = s->pol;
     sj_kvarn_policy_idle(&s->pol, s->n, keep_recent);

@@ -160,9 +160,37 @@ SJK_DEV void copy_out(uint8_t * dst, const uint8_t * src, uint32_t n, int tid, i
     }
 }
 
+// Batched cache write (sjk_store_batch): one position per item, each in its own cache (sink and ring of one layer of
+// one sequence); the rows of item i are k, v + i H D.
+constexpr int STORE_BATCH_MAX = 1024;
+struct StoreBatchParams {
+    StoreParams c;                          // shared fields (k, v, formats, S, cap, H); sink / ring / pos0 per item
+    uint8_t * sink[STORE_BATCH_MAX];
+    uint8_t * ring[STORE_BATCH_MAX];
+    uint32_t pos[STORE_BATCH_MAX];
+};
+
 // One CTA per position: its 2H rows (head-major, K then V) are rotated, staged and written.
 template <int D>
+__global__ void __launch_bounds__(256) store_kernel(StoreParams p);
+template <int D>
+__device__ __forceinline__ void store_position(const StoreParams & p, uint32_t pos, uint8_t * sink, uint8_t * ring,
+                                               size_t row0);
+
+template <int D>
+__global__ void __launch_bounds__(256) store_batch_kernel(const __grid_constant__ StoreBatchParams b) {
+    store_position<D>(b.c, b.pos[blockIdx.x], b.sink[blockIdx.x], b.ring[blockIdx.x], blockIdx.x);
+}
+
+template <int D>
 __global__ void __launch_bounds__(256) store_kernel(StoreParams p) {
+    store_position<D>(p, p.pos0 + blockIdx.x, p.sink, p.ring, blockIdx.x);
+}
+
+// Position pos of one cache; its rows are row0 .. of k and v ([*][H][D]).
+template <int D>
+__device__ __forceinline__ void store_position(const StoreParams & p, uint32_t pos, uint8_t * sink, uint8_t * ring,
+                                               size_t row0) {
     constexpr int VPL = D / 32;
     extern __shared__ __align__(16) uint8_t smem[];
     float * mid = reinterpret_cast<float *>(smem);
@@ -172,16 +200,15 @@ __global__ void __launch_bounds__(256) store_kernel(StoreParams p) {
     if (threadIdx.x < 63) mid[threadIdx.x] = sjk_tq6_mid[threadIdx.x];
     if (threadIdx.x < 64) cent[threadIdx.x] = sjk_tq6_cent[threadIdx.x];
     __syncthreads();
-    const uint32_t pos = p.pos0 + blockIdx.x;
     const bool in_sink = pos < p.S;
     const bool f16_out = in_sink ? p.sink_f16 || p.staging == SJKVARN_STAGING_F16 : p.staging == SJKVARN_STAGING_F16;
     const uint32_t row_bytes = (in_sink && p.sink_f16) ? (uint32_t) D * 2u : p.stage_bytes;
-    uint8_t * base = in_sink ? p.sink + (size_t) pos * p.H * 2 * row_bytes
-                             : p.ring + (size_t) sjk_ring_slot(p.S, p.cap, pos) * p.H * 2 * row_bytes;
+    uint8_t * base = in_sink ? sink + (size_t) pos * p.H * 2 * row_bytes
+                             : ring + (size_t) sjk_ring_slot(p.S, p.cap, pos) * p.H * 2 * row_bytes;
     for (int r = warp; r < 2 * p.H; r += nwarp) {
         const int h = r >> 1, side = r & 1;
         float x[VPL];
-        load_row<VPL>((side ? p.v : p.k) + ((size_t) blockIdx.x * p.H + h) * D, lane, x);
+        load_row<VPL>((side ? p.v : p.k) + (row0 * p.H + h) * D, lane, x);
         if (p.rotate) fwht_warp<VPL>(x, lane, p.fwht_scale);
         if (f16_out) f16_row<VPL>(x, lane, base + (size_t) r * row_bytes);
         else tq6_row<VPL>(x, lane, rows + (size_t) r * row_bytes, mid, cent);
@@ -297,6 +324,51 @@ extern "C" int sjk_unstage_rows(int staging, const uint8_t * src, size_t src_row
     const size_t n = (size_t) n_rows * D;
     unstage_rows_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, st>>>(staging, src, src_row_bytes, x, D, n_rows);
     return sjk_check_launch();
+}
+
+// One position in each of n_items caches (the decode step's cache write across layers and sequences): item i
+// stores rows k, vv + i H D at position pos[i] of views[i]'s sink / ring. Batches above STORE_BATCH_MAX take several
+// launches.
+extern "C" int sjk_store_batch(const sjk_view * views, const uint32_t * pos, int n_items, const float * k, const float * vv,
+                               int rotate, sjk_stream st) {
+    if (!views || !pos || !k || !vv || n_items < 0) return SJKVARN_ERR_ARG;
+    if (n_items == 0) return 0;
+    const sjk_view & v0 = views[0];
+    if (v0.n_head_kv <= 0 || v0.cap == 0) return SJKVARN_ERR_ARG;
+    for (int i = 0; i < n_items; ++i) {
+        const sjk_view & v = views[i];
+        if (!v.sink || !v.ring || v.lay.D != v0.lay.D || v.n_head_kv != v0.n_head_kv || v.staging != v0.staging ||
+            v.sink_type != v0.sink_type || v.S != v0.S || v.cap != v0.cap || v.stage_bytes != v0.stage_bytes)
+            return SJKVARN_ERR_ARG;
+    }
+    static thread_local StoreBatchParams b;
+    StoreParams & p = b.c;
+    p.S = v0.S; p.cap = v0.cap; p.H = v0.n_head_kv; p.pos0 = 0;
+    p.staging = v0.staging; p.sink_f16 = v0.sink_type == SJKVARN_SINK_F16; p.rotate = rotate;
+    p.fwht_scale = host_fwht_scale(v0.lay.D); p.stage_bytes = (uint32_t) v0.stage_bytes;
+    p.sink = nullptr; p.ring = nullptr;
+    const int warps = 2 * p.H < 8 ? 2 * p.H : 8;
+    const size_t smem = 128 * sizeof(float) + (size_t) 2 * p.H * p.stage_bytes;
+    if (smem > 48 * 1024) return SJK_ERR_UNSUPPORTED;
+    const size_t row = (size_t) p.H * v0.lay.D;
+    for (int i0 = 0; i0 < n_items; i0 += STORE_BATCH_MAX) {
+        const int n = n_items - i0 < STORE_BATCH_MAX ? n_items - i0 : STORE_BATCH_MAX;
+        p.k = k + (size_t) i0 * row; p.v = vv + (size_t) i0 * row;
+        for (int i = 0; i < n; ++i) {
+            b.sink[i] = const_cast<uint8_t *>(views[i0 + i].sink);
+            b.ring[i] = const_cast<uint8_t *>(views[i0 + i].ring);
+            b.pos[i] = pos[i0 + i];
+        }
+        switch (v0.lay.D) {
+            case 128: store_batch_kernel<128><<<n, 32 * warps, smem, st>>>(b); break;
+            case 256: store_batch_kernel<256><<<n, 32 * warps, smem, st>>>(b); break;
+            case 512: store_batch_kernel<512><<<n, 32 * warps, smem, st>>>(b); break;
+            default: return SJK_ERR_UNSUPPORTED;
+        }
+        const int rc = sjk_check_launch();
+        if (rc) return rc;
+    }
+    return 0;
 }
 
 extern "C" int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos,

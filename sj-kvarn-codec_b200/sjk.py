@@ -138,6 +138,11 @@ SIGNATURES = {
     "sjk_attend_static": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sjk_attend_partial": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, C.c_uint, vp, C.c_float, vp, vp, C.c_size_t, vp]),
     "sjk_attend_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, vp]),
+    "sjk_store_batch": (C.c_int, [P(View), P(u32), C.c_int, vp, vp, C.c_int, vp]),
+    "sjk_seq_store": (C.c_int, [P(Seq), u32, u32, vp, vp, C.c_size_t, C.c_int, vp]),
+    "sjk_attend_batch_scratch_bytes": (C.c_size_t, [P(View), C.c_int, C.c_int, C.c_int]),
+    "sjk_attend_batch": (C.c_int, [P(View), P(u32), P(u32), P(u32), C.c_int, C.c_int, C.c_int, vp, C.c_float, vp, vp,
+                                   C.c_size_t, vp]),
     "sjk_layer_store": (C.c_int, [P(Layer), u32, u32, vp, vp, C.c_int, vp]),
     "sjk_layer_seal": (C.c_int, [P(Layer), u32, u32, vp]),
     "sjk_layer_attend": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),

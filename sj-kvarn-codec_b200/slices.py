@@ -1,4 +1,10 @@
-"""Context slicing of one long sequence across GPUs.
+"""Work partitions across GPUs: context slices of one long sequence and whole sequences of a
+paged pool.
+
+Pool (config 3): sequences are independent, so each rank owns whole sequences, assigned by longest-processing-time
+on their context lengths (largest first, each to the least-loaded rank); no collective touches the data path.
+
+Context slices (config 4):
 
 Every rank holds a contiguous range of the sealed groups of each layer. Rank 0 also holds the sink, and the last
 rank holds the staging ring (the newest positions). Each rank attends over its own regions with
@@ -62,3 +68,16 @@ def partial_np(q, k, v, scale):
     m = s.max(axis=1)
     p = np.exp(s - m[:, None])
     return np.concatenate([m[:, None], p.sum(axis=1)[:, None], p @ v.astype(np.float64)], axis=1)
+
+
+def lpt_assign(costs, world):
+    """Owner rank of every item: items in decreasing cost order (ties by index) go to the least-loaded rank (ties by
+    rank index). Deterministic, so every rank computes the same assignment."""
+    order = sorted(range(len(costs)), key=lambda i: (-float(costs[i]), i))
+    load = [0.0] * world
+    owner = [0] * len(costs)
+    for i in order:
+        r = min(range(world), key=lambda j: (load[j], j))
+        owner[i] = r
+        load[r] += float(costs[i])
+    return owner

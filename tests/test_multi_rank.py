@@ -89,3 +89,52 @@ def test_group_ranges_and_regions(world):
     assert sum(1 for r in regs if r & slices.SJK_REGION_SINK) == 1 and regs[0] & slices.SJK_REGION_SINK
     assert sum(1 for r in regs if r & slices.SJK_REGION_RING) == 1 and regs[-1] & slices.SJK_REGION_RING
     assert all(r & slices.SJK_REGION_BODY for r in regs)
+
+
+def _pool_worker(rank, world, port, q):
+    """Config-3 partition on one rank: the LPT owner table of the 64 seeded contexts, gathered from every rank."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ctx = np.random.default_rng(3).integers(8192, 65536 + 1, size=64)
+        owner = torch.tensor(slices.lpt_assign(ctx, world), dtype=torch.int64)
+        allo = [torch.zeros_like(owner) for _ in range(world)]
+        dist.all_gather(allo, owner)
+        q.put((rank, [a.tolist() for a in allo]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pool_partition_lpt_two_ranks():
+    """Every rank computes the same sequence-to-rank table (no exchange needed), each sequence has one owner,
+    and the context loads of the ranks differ by at most the smallest context (the LPT bound for this case)."""
+    import multiprocessing as mp
+    ctx_ = mp.get_context("spawn")
+    q = ctx_.Queue()
+    port = _free_port()
+    procs = [ctx_.Process(target=_pool_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    tables = [t for _, ts in res for t in ts]
+    assert all(t == tables[0] for t in tables)
+    ctx = np.random.default_rng(3).integers(8192, 65536 + 1, size=64)
+    owner = np.array(tables[0])
+    loads = [int(ctx[owner == r].sum()) for r in range(2)]
+    assert set(owner.tolist()) == {0, 1} and abs(loads[0] - loads[1]) <= int(ctx.min())
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_lpt_assign_balance(world):
+    ctx = np.random.default_rng(3).integers(8192, 65536 + 1, size=64)
+    owner = np.array(slices.lpt_assign(ctx, world))
+    loads = np.array([ctx[owner == r].sum() for r in range(world)])
+    assert owner.min() >= 0 and owner.max() < world
+    assert loads.max() - loads.min() <= ctx.max()
+    assert slices.lpt_assign(ctx, world) == owner.tolist()
