@@ -91,7 +91,7 @@ constexpr uint32_t AK_SBO = 128, AK_LBO = 2048;
 // shared memory (bytes)
 constexpr uint32_t OFF_TBL = 0;                                 // u32 [512][32]: cb_K | cb_V << 16, 32 copies
 constexpr uint32_t OFF_AK = OFF_TBL + 512 * 32 * 4;             // 64 KB
-constexpr uint32_t OFF_REC = OFF_AK + 32 * AK_LBO;              // 2 x record
+constexpr uint32_t OFF_REC = OFF_AK + 32 * AK_LBO;              // 2 x record (bulk copies)
 constexpr uint32_t OFF_BK = OFF_REC + 2 * REC_MAX;              // [Q' hi | Q' lo] over 256 channels: 2 x TILE_B
 constexpr uint32_t OFF_BV = OFF_BK + 2 * TILE_B;                // [P' hi | P' lo] over 128 tokens: TILE_B
 constexpr uint32_t OFF_F = OFF_BV + TILE_B;                     // floats below
@@ -115,10 +115,11 @@ constexpr uint32_t OFF_TMEM = OFF_BAR + B_COUNT * 8;
 constexpr uint32_t OFF_ABORT = OFF_TMEM + 4;
 constexpr uint32_t SMEM_TOTAL = OFF_ABORT + 12;
 static_assert(SMEM_TOTAL <= 227 * 1024, "shared memory");
-static_assert(OFF_REC % 16 == 0 && REC_MAX % 16 == 0 && OFF_BK % 16 == 0 && OFF_BV % 16 == 0, "alignment");
+static_assert(OFF_REC % 16 == 0 && REC_MAX % 16 == 0 && OFF_BK % 16 == 0 && OFF_BV % 16 == 0 && OFF_F % 16 == 0, "alignment");
 
-// Wait for the phase of `bar` with the given parity. Gives up when the CTA's abort flag is raised or after about
-// 1 s of wall clock (then it raises the flag and records the timeout in the device status word).
+// Wait for the phase of `bar` with the given parity (try_wait suspends the thread until the phase completes or
+// about 1 us passes). Gives up when the CTA's abort flag is raised or after about 1 s of wall clock (then it raises
+// the flag and records the timeout in the device status word).
 __device__ __forceinline__ bool wait_bar(uint64_t * bar, uint32_t parity, volatile int * abort) {
     if (tc::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = tc::globaltimer();
@@ -141,74 +142,7 @@ __device__ __forceinline__ void warp_arrive(uint64_t * bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
-// ---- stream decoding ----------------------------------------------------------------------------------------
-// The 4 BITS stream words of one channel (128 tokens), 16-byte aligned in shared memory.
-template <int BITS>
-__device__ __forceinline__ void load_words(const uint8_t * src, uint32_t (&w)[4 * BITS]) {
-#pragma unroll
-    for (int i = 0; i < BITS; ++i) {
-        const uint4 x = reinterpret_cast<const uint4 *>(src)[i];
-        w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
-    }
-}
-template <int BITS>
-__device__ __forceinline__ uint32_t word_at(const uint32_t (&w)[4 * BITS], int i) { return i < 0 ? 0u : w[i < 0 ? 0 : i]; }
-
-// Byte offset in the lookup table of token 64 TH + j of the channel (copy `lane`): the window (the token's code
-// above the 6 stream bits before it, the bits before the stream reading as zero, sj_kvarn.h:879-900) times 128,
-// plus 4 lane. Token 64 TH + j starts its window at bit 26 + j BITS of the words from index 2 TH BITS - 1 on, for
-// both halves and both widths; with j a compile-time constant this is one shift and one LOP3.
-template <int BITS, int TH>
-__device__ __forceinline__ uint32_t tbl_off(const uint32_t (&w)[4 * BITS], int j, uint32_t lane4) {
-    const int b = 26 + j * BITS, a = b >> 5, s = b & 31, base = TH * 2 * BITS - 1;
-    constexpr uint32_t M7 = ((1u << (6 + BITS)) - 1u) << 7;
-    const uint32_t lo = word_at<BITS>(w, base + a);
-    uint32_t y;
-    if (s >= 7) y = (s + 6 + BITS <= 32) ? (lo >> (s - 7)) : __funnelshift_r(lo, word_at<BITS>(w, base + a + 1), s - 7);
-    else y = lo << (7 - s);
-    return (y & M7) | lane4;
-}
-__device__ __forceinline__ uint32_t lds32(const uint8_t * base, uint32_t off) {
-    return *reinterpret_cast<const uint32_t *>(base + off);
-}
-
-// K side: the 128 tokens of one channel as fp16 (low table halves) into its 16 MN-major chunks of A_K
-template <int BITS, int TH>
-__device__ __forceinline__ void decode_k_half(const uint8_t * tbl, const uint32_t (&w)[4 * BITS], uint32_t lane4, uint8_t * ak_ch) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int j = 8 * c + 2 * i;
-            o[i] = prmt(lds32(tbl, tbl_off<BITS, TH>(w, j, lane4)), lds32(tbl, tbl_off<BITS, TH>(w, j + 1, lane4)), 0x5410u);
-        }
-        *reinterpret_cast<uint4 *>(ak_ch + (8 * TH + c) * AK_SBO) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-}
-// V side: the 128 tokens of one channel as fp16 pairs (high table halves, token 2i low) into the thread's TMEM lane
-template <int BITS, int TH>
-__device__ __forceinline__ void decode_v_half(const uint8_t * tbl, const uint32_t (&w)[4 * BITS], uint32_t lane4, uint32_t taddr) {
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-        uint32_t col[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int j = 32 * hh + 2 * i;
-            col[i] = prmt(lds32(tbl, tbl_off<BITS, TH>(w, j, lane4)), lds32(tbl, tbl_off<BITS, TH>(w, j + 1, lane4)), 0x7632u);
-        }
-        tc::st_x16(taddr + 32 * TH + 16 * hh, col);
-    }
-}
-
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u));
-}
-
+// ---- record streams -----------------------------------------------------------------------------------------
 // The CTA's work as a sequence of records over its items: cursor over (item, record)
 struct Cursor {
     int it, it_end;
@@ -223,6 +157,102 @@ struct Cursor {
         if (++rec == r1 && ++it < it_end) { rec = p.item[it].r0; r1 = p.item[it].r1; }
     }
 };
+// block id of the cursor's record (a load from the sequence's block table, or the record index itself)
+__device__ __forceinline__ uint32_t blk_of(const TwParams & p, const Cursor & c) {
+    const TwSeq & sq = p.seq[p.item[c.it].seq_hl & 0xFFFFu];
+    return sq.blocks ? __ldg(sq.blocks + c.rec) : c.rec;
+}
+__device__ __forceinline__ const uint8_t * rec_ptr(const TwParams & p, const Cursor & c, uint32_t blk) {
+    const TwItem & it = p.item[c.it];
+    return p.seq[it.seq_hl & 0xFFFFu].body + ((size_t) blk * p.n_head_kv + (it.h_slot & 0xFFFFu)) * p.lay.bytes;
+}
+
+// The 4 BITS stream words of one channel (128 tokens), 16-byte aligned in shared memory.
+template <int BITS>
+__device__ __forceinline__ void load_words(const uint8_t * src, uint32_t (&w)[4 * BITS]) {
+#pragma unroll
+    for (int i = 0; i < BITS; ++i) {
+        const uint4 x = reinterpret_cast<const uint4 *>(src)[i];
+        w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+    }
+}
+
+// ---- stream decoding ----------------------------------------------------------------------------------------
+// 32 tokens are BITS whole stream words. Token j of the 32 starts its window (its code above the 6 stream bits
+// before it, the bits before the stream reading as zero, sj_kvarn.h:879-900) at bit 26 + j BITS of
+// win = {word before the 32 tokens, their BITS words}. Byte offset of the window's table row (copy `lane`):
+// window * 128 + 4 lane, one shift and one LOP3 at a compile-time bit offset.
+template <int BITS>
+__device__ __forceinline__ uint32_t tbl_off(const uint32_t (&win)[BITS + 1], int j, uint32_t lane4) {
+    const int b = 26 + j * BITS, a = b >> 5, s = b & 31;
+    constexpr uint32_t M7 = ((1u << (6 + BITS)) - 1u) << 7;
+    uint32_t y;
+    if (s >= 7) y = (s + 6 + BITS <= 32) ? (win[a] >> (s - 7)) : __funnelshift_r(win[a], win[a + 1 <= BITS ? a + 1 : BITS], s - 7);
+    else y = win[a] << (7 - s);
+    return (y & M7) | lane4;
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t * base, uint32_t off) {
+    return *reinterpret_cast<const uint32_t *>(base + off);
+}
+// fp16 pair of tokens j, j + 1 (token j low) from the table half selected by sel (0x5410 K, 0x7632 V)
+template <int BITS>
+__device__ __forceinline__ uint32_t pair_at(const uint8_t * tbl, const uint32_t (&win)[BITS + 1], int j, uint32_t lane4, uint32_t sel) {
+    return prmt(lds32(tbl, tbl_off<BITS>(win, j, lane4)), lds32(tbl, tbl_off<BITS>(win, j + 1, lane4)), sel);
+}
+
+// K side: the 128 tokens of one channel as fp16 into its 16 MN-major chunks of A_K (a rolled loop over 4 x 32)
+template <int BITS>
+__device__ __forceinline__ void decode_k(const uint8_t * tbl, uint32_t (&w)[4 * BITS], uint32_t lane4, uint8_t * ak_ch) {
+    uint32_t prev = 0;
+#pragma unroll 1
+    for (int sc = 0; sc < 4; ++sc) {
+        uint32_t win[BITS + 1];
+        win[0] = prev;
+#pragma unroll
+        for (int i = 0; i < BITS; ++i) win[1 + i] = w[i];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = pair_at<BITS>(tbl, win, 8 * c + 2 * i, lane4, 0x5410u);
+            *reinterpret_cast<uint4 *>(ak_ch + (4 * sc + c) * AK_SBO) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        prev = w[BITS - 1];
+#pragma unroll
+        for (int i = 0; i < 3 * BITS; ++i) w[i] = w[i + BITS];
+    }
+}
+// V side: the 128 tokens of one channel as fp16 pairs (token 2i low) into the thread's TMEM lane
+template <int BITS>
+__device__ __forceinline__ void decode_v(const uint8_t * tbl, uint32_t (&w)[4 * BITS], uint32_t lane4, uint32_t taddr) {
+    uint32_t prev = 0;
+#pragma unroll 1
+    for (int sc = 0; sc < 4; ++sc) {
+        uint32_t win[BITS + 1];
+        win[0] = prev;
+#pragma unroll
+        for (int i = 0; i < BITS; ++i) win[1 + i] = w[i];
+        uint32_t col[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) col[i] = pair_at<BITS>(tbl, win, 2 * i, lane4, 0x7632u);
+        tc::st_x16(taddr + 16 * sc, col);
+        prev = w[BITS - 1];
+#pragma unroll
+        for (int i = 0; i < 3 * BITS; ++i) w[i] = w[i + BITS];
+    }
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u));
+}
+// global -> L2 prefetch of `bytes` (multiple of 16) at a 16-byte aligned address
+__device__ __forceinline__ void prefetch_l2(const void * src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 
 template <int BK, int BV>
 __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
@@ -265,7 +295,6 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
     const uint32_t tmem = *tmem_slot;
     const uint8_t * tbl = sm + OFF_TBL;
     const uint32_t lane4 = (uint32_t) lane * 4u;
-    const uint32_t rb = l.bytes;
     Cursor cur;
     cur.start(p, i0, i1);
 
@@ -290,37 +319,32 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             }
             const uint32_t s = g & 1u;
             // every K warp reaches the group barrier below on every record, also after a wait gave up
-            bool ok = warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
-                      (g == 0 || warp_wait(&bars[B_SFULL + ((g - 1) & 1u)], ((g - 1) >> 1) & 1u, abort));
+            const bool ok = warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
+                            (g == 0 || warp_wait(&bars[B_SFULL + ((g - 1) & 1u)], ((g - 1) >> 1) & 1u, abort));
             if (ok) {
                 tc::fence_after_sync();
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
                 // B_K and the zero-point partials
-                {
-                    const float2 ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
-                    const float2 kz = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_zero + 4 * jp));
-                    float cz[8];
+                const float2 ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
+                const float2 kz = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_zero + 4 * jp));
+                float cz[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int r = 8 * rh + i;
-                        const float2 x = make_float2(q2[i].x * ks.x, q2[i].y * ks.y);
-                        const __half2 hi = __floats2half2_rn(x.x, x.y);
-                        const float2 hf = __half22float2(hi);
-                        const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
-                        *reinterpret_cast<__half2 *>(bk + r * 16) = hi;
-                        *reinterpret_cast<__half2 *>(bk + (NR + r) * 16) = lo;
-                        cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
-                    }
-                    const float cw = warp_rows8<false>(cz, lane);
-                    if ((lane & 3) == 0) F[F_REDC + s * 64 + warp * 8 + (lane >> 2)] = cw;
+                for (int i = 0; i < 8; ++i) {
+                    const int r = 8 * rh + i;
+                    const float2 x = make_float2(q2[i].x * ks.x, q2[i].y * ks.y);
+                    const __half2 hi = __floats2half2_rn(x.x, x.y);
+                    const float2 hf = __half22float2(hi);
+                    const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
+                    *reinterpret_cast<__half2 *>(bk + r * 16) = hi;
+                    *reinterpret_cast<__half2 *>(bk + (NR + r) * 16) = lo;
+                    cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
                 }
-                // A_K: channel d, all 128 tokens
-                {
-                    uint32_t w[4 * BK];
-                    load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
-                    decode_k_half<BK, 0>(tbl, w, lane4, ak_ch);
-                    decode_k_half<BK, 1>(tbl, w, lane4, ak_ch);
-                }
+                const float cw = warp_rows8<false>(cz, lane);
+                if ((lane & 3) == 0) F[F_REDC + s * 64 + warp * 8 + (lane >> 2)] = cw;
+                uint32_t w[4 * BK];
+                load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
+                warp_arrive(&bars[B_REMPTY + s], lane);
+                decode_k<BK>(tbl, w, lane4, ak_ch);
                 tc::fence_proxy_async();
             }
             if (!tc::nbar_and(1, 256, ok)) break;               // zero-point partials of all K warps in place
@@ -331,7 +355,6 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             }
             if (warp == 0) warp_arrive(&bars[B_CFULL + s], lane);
             warp_arrive(&bars[B_AKFULL], lane);
-            warp_arrive(&bars[B_REMPTY + s], lane);
         }
     } else if (warp < W_S) {
         // ================================ V side ================================
@@ -343,26 +366,30 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
         for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
         float vc_prev = 0.0f;
         Cursor ecur = cur;                                      // the epilogue's cursor lags one record
-        // epilogue of record e: acc = acc alpha + Vc (O + z); at the end of an item its outputs leave as partials
         uint32_t e3 = 0;                                        // e % 3: the softmax's alpha / z slot of record e
+        // epilogue of record e: acc = acc alpha + Vc (O + z), in two halves of 8 rows; at the end of an item the
+        // outputs leave as partials
         auto epilogue = [&](uint32_t e, float vc) -> bool {
             const uint32_t es = e & 1u;
             if (!warp_wait(&bars[B_VDONE + es], (e >> 1) & 1u, abort)) return false;
             if (!warp_wait(&bars[B_AZFULL + es], (e >> 1) & 1u, abort)) return false;
             tc::fence_after_sync();
-            float o[16], ol[16], al[16], z[16];
-            tc::ld_x16(tmem + lane_base + COL_O + 32 * tile, o);
-            tc::ld_x16(tmem + lane_base + COL_O + 32 * tile + NR, ol);
-            ld8(F + F_AL + e3 * NR, *reinterpret_cast<float (*)[8]>(al));
-            ld8(F + F_AL + e3 * NR + 8, *reinterpret_cast<float (*)[8]>(al + 8));
-            ld8(F + F_Z + e3 * NR, *reinterpret_cast<float (*)[8]>(z));
-            ld8(F + F_Z + e3 * NR + 8, *reinterpret_cast<float (*)[8]>(z + 8));
-            tc::wait_ld();
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t o[8], ol[8];
+                float al[8], z[8];
+                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + 8 * hh, o);
+                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + NR + 8 * hh, ol);
+                ld8(F + F_AL + e3 * NR + 8 * hh, al);
+                ld8(F + F_Z + e3 * NR + 8 * hh, z);
+                tc::wait_ld();
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    acc[8 * hh + r] = fmaf(acc[8 * hh + r], al[r], vc * ((__uint_as_float(o[r]) + __uint_as_float(ol[r])) + z[r]));
+            }
             tc::fence_before_sync();
             warp_arrive(&bars[B_OFREE], lane);
             e3 = e3 == 2 ? 0 : e3 + 1;
-#pragma unroll
-            for (int r = 0; r < NR; ++r) acc[r] = fmaf(acc[r], al[r], vc * ((o[r] + ol[r]) + z[r]));
             if (ecur.last()) {
                 const TwItem & itm = p.item[ecur.it];
                 const int hl = (int) (itm.seq_hl >> 16), slot = (int) (itm.h_slot >> 16);
@@ -383,18 +410,14 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             if (g > 1 && !warp_wait(&bars[B_VDONE + s], ((g - 2) >> 1) & 1u, abort)) { ok = false; break; }
             tc::fence_after_sync();
             const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
-            {
-                uint32_t w[4 * BV];
-                load_words<BV>(rec + l.v_payload + d * (16 * BV), w);
-                const uint32_t ta = tmem + lane_base + COL_AV + 128 * s + 64 * tile;
-                decode_v_half<BV, 0>(tbl, w, lane4, ta);
-                decode_v_half<BV, 1>(tbl, w, lane4, ta);
-            }
+            uint32_t w[4 * BV];
+            load_words<BV>(rec + l.v_payload + d * (16 * BV), w);
             const float vc = h2f_at(rec + l.v_ch + 2 * d);
+            warp_arrive(&bars[B_REMPTY + s], lane);
+            decode_v<BV>(tbl, w, lane4, tmem + lane_base + COL_AV + 128 * s + 64 * tile);
             tc::wait_st();
             tc::fence_before_sync();
             warp_arrive(&bars[B_AVFULL + s], lane);
-            warp_arrive(&bars[B_REMPTY + s], lane);
             if (g > 0 && !epilogue(g - 1, vc_prev)) { ok = false; break; }
             vc_prev = vc;
         }
@@ -417,12 +440,6 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             float sc[16], vsc = 0.0f, vz = 0.0f;
             if (ok) {
                 tc::fence_after_sync();
-                uint32_t a[16], al[16];
-                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
-                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + NR, al);
-                tc::wait_ld();
-                tc::fence_before_sync();
-                warp_arrive(&bars[B_SFREE + s], lane);
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
                 const float kt = h2f_at(rec + l.k_tok + 2 * t);
                 vsc = h2f_at(rec + l.v_scale + 2 * t);
@@ -430,7 +447,14 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 float c[16];
                 ld8(F + F_C + s * NR, *reinterpret_cast<float (*)[8]>(c));
                 ld8(F + F_C + s * NR + 8, *reinterpret_cast<float (*)[8]>(c + 8));
+                // the record stage and C[s] are rewritten only after this arrival (record g + 2)
                 warp_arrive(&bars[B_REMPTY + s], lane);
+                uint32_t a[16], al[16];
+                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
+                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + NR, al);
+                tc::wait_ld();
+                tc::fence_before_sync();
+                warp_arrive(&bars[B_SFREE + s], lane);
                 const uint32_t pos = sq.S + cur.rec * (uint32_t) G + (uint32_t) t;
                 const bool in = pos < sq.b_end;
                 const float kts = kt * sl2;
@@ -491,62 +515,65 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
         }
     } else if (lane == 0) {
         // ================================ issuer ================================
+        // In program order: the K MMAs of record g, the V MMAs of record g - 1, the bulk copy of record g + 2; each
+        // after blocking waits. Records up to four ahead are prefetched into L2, so the bulk copies read from it.
         const uint32_t idesc_k = tc::idesc_f16(128, NB) | (1u << 15);    // A MN-major (tokens contiguous per channel)
         const uint32_t idesc_v = tc::idesc_f16(128, NB);
-        uint32_t nl = 0, nk = 0, nv = 0;
-        Cursor lc = cur;
-        int last_commit = -1;                                   // barrier index of the last commit
+        const uint32_t rb = l.bytes;
+        Cursor pc = cur, lc = cur;                              // L2 prefetch and load cursors
+        uint32_t np = 0, nl = 0;                                // records prefetched / loaded
+        int last_commit = -1;                                   // barrier index and parity of the last commit
         uint32_t last_parity = 0;
-        uint64_t t_last = tc::globaltimer();
-        while (nv < n) {
-            bool progress = false;
-            if (nl < n && (nl < 2 || tc::mbar_test(&bars[B_REMPTY + (nl & 1u)], ((nl - 2) >> 1) & 1u))) {
-                const TwItem & itm = p.item[lc.it];
-                const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
-                const uint32_t blk = sq.blocks ? sq.blocks[lc.rec] : lc.rec;
-                const uint32_t h = itm.h_slot & 0xFFFFu;
-                tc::mbar_expect_tx(&bars[B_RFULL + (nl & 1u)], rb);
-                tc::bulk_g2s(sm + OFF_REC + (nl & 1u) * REC_MAX, sq.body + ((size_t) blk * p.n_head_kv + h) * rb, rb,
-                             &bars[B_RFULL + (nl & 1u)]);
-                ++nl;
-                lc.next(p);
-                progress = true;
-            }
-            if (nk < nl && tc::mbar_test(&bars[B_AKFULL], nk & 1u) &&
-                (nk < 2 || tc::mbar_test(&bars[B_SFREE + (nk & 1u)], ((nk - 2) >> 1) & 1u))) {
-                tc::fence_after_sync();
-                const uint32_t dcol = tmem + COL_S + 32 * (nk & 1u);
+        auto prefetch_to = [&](uint32_t upto) {
+            for (; np < n && np < upto; ++np, pc.next(p)) prefetch_l2(rec_ptr(p, pc, blk_of(p, pc)), rb);
+        };
+        auto mma_v = [&](uint32_t e) -> bool {
+            if (!wait_bar(&bars[B_AZFULL + (e & 1u)], (e >> 1) & 1u, abort)) return false;
+            if (!wait_bar(&bars[B_AVFULL + (e & 1u)], (e >> 1) & 1u, abort)) return false;
+            if (e > 0 && !wait_bar(&bars[B_OFREE], (e - 1) & 1u, abort)) return false;
+            tc::fence_after_sync();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint64_t da = tc::smem_desc(sm + OFF_AK + 2 * AK_LBO * j, AK_LBO, AK_SBO);
-                    const uint64_t db = tc::smem_desc(sm + OFF_BK + TILE_B * (j >> 3), HCH, 128) + (uint64_t) ((2 * HCH * (j & 7)) >> 4);
-                    mma_ss(dcol, da, db, idesc_k, j ? 1u : 0u);
+            for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint64_t db = tc::smem_desc(sm + OFF_BV, HCH, 128) + (uint64_t) ((2 * HCH * k) >> 4);
+                    tc::mma_ts(tmem + COL_O + 32 * tile, tmem + COL_AV + 128 * (e & 1u) + 64 * tile + 8 * k, db, idesc_v, k ? 1u : 0u);
                 }
-                tc::mma_commit(&bars[B_SFULL + (nk & 1u)]);
-                last_commit = (int) (B_SFULL + (nk & 1u)); last_parity = (nk >> 1) & 1u;
-                ++nk;
-                progress = true;
+            tc::mma_commit(&bars[B_VDONE + (e & 1u)]);
+            last_commit = (int) (B_VDONE + (e & 1u)); last_parity = (e >> 1) & 1u;
+            return true;
+        };
+        // record j into stage j % 2, once the roles released record j - 2
+        auto load_to = [&](uint32_t upto) -> bool {
+            for (; nl < n && nl < upto; ++nl, lc.next(p)) {
+                if (nl >= 2 && !wait_bar(&bars[B_REMPTY + (nl & 1u)], ((nl - 2) >> 1) & 1u, abort)) return false;
+                tc::mbar_expect_tx(&bars[B_RFULL + (nl & 1u)], rb);
+                tc::bulk_g2s(sm + OFF_REC + (nl & 1u) * REC_MAX, rec_ptr(p, lc, blk_of(p, lc)), rb, &bars[B_RFULL + (nl & 1u)]);
             }
-            if (nv < nk && tc::mbar_test(&bars[B_AZFULL + (nv & 1u)], (nv >> 1) & 1u) &&
-                tc::mbar_test(&bars[B_AVFULL + (nv & 1u)], (nv >> 1) & 1u) && (nv < 1 || tc::mbar_test(&bars[B_OFREE], (nv - 1) & 1u))) {
-                tc::fence_after_sync();
+            return true;
+        };
+        prefetch_to(4);
+        bool ok = load_to(2);
+        for (uint32_t g = 0; g < n && ok; ++g) {
+            prefetch_to(g + 5);
+            ok = wait_bar(&bars[B_AKFULL], g & 1u, abort) && (g < 2 || wait_bar(&bars[B_SFREE + (g & 1u)], ((g - 2) >> 1) & 1u, abort));
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t dcol = tmem + COL_S + 32 * (g & 1u);
 #pragma unroll
-                for (int tile = 0; tile < 2; ++tile)
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const uint64_t db = tc::smem_desc(sm + OFF_BV, HCH, 128) + (uint64_t) ((2 * HCH * k) >> 4);
-                        tc::mma_ts(tmem + COL_O + 32 * tile, tmem + COL_AV + 128 * (nv & 1u) + 64 * tile + 8 * k, db, idesc_v, k ? 1u : 0u);
-                    }
-                tc::mma_commit(&bars[B_VDONE + (nv & 1u)]);
-                last_commit = (int) (B_VDONE + (nv & 1u)); last_parity = (nv >> 1) & 1u;
-                ++nv;
-                progress = true;
+            for (int j = 0; j < 16; ++j) {
+                const uint64_t da = tc::smem_desc(sm + OFF_AK + 2 * AK_LBO * j, AK_LBO, AK_SBO);
+                const uint64_t db = tc::smem_desc(sm + OFF_BK + TILE_B * (j >> 3), HCH, 128) + (uint64_t) ((2 * HCH * (j & 7)) >> 4);
+                mma_ss(dcol, da, db, idesc_k, j ? 1u : 0u);
             }
-            const uint64_t now = tc::globaltimer();
-            if (progress) t_last = now;
-            else if (*abort) break;
-            else if (now - t_last > SJK_WAIT_NS) { atomicExch(&sjk_dev_status, SJK_DEV_TIMEOUT); *abort = 1; break; }
+            tc::mma_commit(&bars[B_SFULL + (g & 1u)]);
+            last_commit = (int) (B_SFULL + (g & 1u)); last_parity = (g >> 1) & 1u;
+            if (g > 0) ok = mma_v(g - 1);
+            // record g + 2 into the stage of record g, as soon as the roles released it (the softmax reads its last
+            // bytes right after the K MMAs above complete)
+            if (ok) ok = load_to(g + 3);
         }
+        if (ok && n > 0) mma_v(n - 1);
         // drain: the copies still in flight (at most the last two) and the MMAs behind the last commit
         for (uint32_t j = nl > 2 ? nl - 2 : 0; j < nl; ++j) tc::mbar_wait(&bars[B_RFULL + (j & 1u)], (j >> 1) & 1u);
         if (last_commit >= 0) tc::mbar_wait(&bars[last_commit], last_parity);
