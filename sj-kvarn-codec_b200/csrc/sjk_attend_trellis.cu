@@ -37,8 +37,7 @@ namespace {
 
 using namespace tc::num;
 
-constexpr int NR = 16;                  // query rows per KV head, padded
-constexpr int NB = 2 * NR;              // B operands: hi rows 0..15, lo rows 16..31
+constexpr int NR = 16;                  // most query rows per KV head (the kernels pad to 8 or 16; B = [hi | lo] rows)
 constexpr int D = 256;
 constexpr int G = 128;
 constexpr int NT = 672;                 // 8 K-side warps, 8 V-side warps, 4 softmax warps, 1 issuer warp
@@ -242,6 +241,14 @@ __device__ __forceinline__ void decode_v(const uint8_t * tbl, uint32_t (&w)[4 * 
     }
 }
 
+// Reduce R per-thread row values across the 32 lanes; afterwards lanes (32 / R) r .. hold row r.
+template <int R, bool MAX>
+__device__ __forceinline__ float warp_rows(const float (&v)[R], int lane) {
+    if constexpr (R == 16) return warp_rows16<MAX>(v, lane);
+    else if constexpr (R == 8) return warp_rows8<MAX>(v, lane);
+    else return warp_rows4<MAX>(v, lane);
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -254,8 +261,11 @@ __device__ __forceinline__ void prefetch_l2(const void * src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-template <int BK, int BV>
+// R: query rows per KV head the kernel computes (8 or 16, padded; the MMA N is 2 R)
+template <int BK, int BV, int R>
 __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
+    constexpr int RH = R / 2;                                   // B_K rows per thread (two row halves)
+    constexpr int LPR = 32 / R, LPH = 32 / RH;                  // lanes per row after a warp_rows<R> / <RH>
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const sj_kvarn_layout & l = p.lay;
@@ -300,19 +310,19 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
 
     if (warp < W_V) {
         // ================================ K side ================================
-        const int jp = tid & 127, rh = tid >> 7;               // B_K: channels 2 jp, 2 jp + 1; rows 8 rh ..
+        const int jp = tid & 127, rh = tid >> 7;               // B_K: channels 2 jp, 2 jp + 1; rows RH rh ..
         const int d = tid;                                      // decoding: channel d
         uint8_t * bk = sm + OFF_BK + TILE_B * (jp >> 6) + h_off(0, (2 * jp) & 127);
         uint8_t * ak_ch = sm + OFF_AK + (d >> 3) * AK_LBO + (d & 7) * 16;
-        float2 q2[8];
+        float2 q2[RH];
         for (uint32_t g = 0; g < n; ++g, cur.next(p)) {
             const TwItem & itm = p.item[cur.it];
             if (cur.first(p)) {
                 const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
                 const int hl = (int) (itm.seq_hl >> 16);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int r = 8 * rh + i;
+                for (int i = 0; i < RH; ++i) {
+                    const int r = RH * rh + i;
                     q2[i] = r < p.rows ? __ldg(reinterpret_cast<const float2 *>(sq.q + (size_t) (p.row_q[r] + hl * p.grp) * D) + jp)
                                        : make_float2(0.0f, 0.0f);
                 }
@@ -327,20 +337,20 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 // B_K and the zero-point partials
                 const float2 ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
                 const float2 kz = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_zero + 4 * jp));
-                float cz[8];
+                float cz[RH];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int r = 8 * rh + i;
+                for (int i = 0; i < RH; ++i) {
+                    const int r = RH * rh + i;
                     const float2 x = make_float2(q2[i].x * ks.x, q2[i].y * ks.y);
                     const __half2 hi = __floats2half2_rn(x.x, x.y);
                     const float2 hf = __half22float2(hi);
                     const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
                     *reinterpret_cast<__half2 *>(bk + r * 16) = hi;
-                    *reinterpret_cast<__half2 *>(bk + (NR + r) * 16) = lo;
+                    *reinterpret_cast<__half2 *>(bk + (R + r) * 16) = lo;
                     cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
                 }
-                const float cw = warp_rows8<false>(cz, lane);
-                if ((lane & 3) == 0) F[F_REDC + s * 64 + warp * 8 + (lane >> 2)] = cw;
+                const float cw = warp_rows<RH, false>(cz, lane);
+                if (lane % LPH == 0) F[F_REDC + s * 64 + warp * 8 + lane / LPH] = cw;
                 uint32_t w[4 * BK];
                 load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
                 warp_arrive(&bars[B_REMPTY + s], lane);
@@ -348,9 +358,9 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 tc::fence_proxy_async();
             }
             if (!tc::nbar_and(1, 256, ok)) break;               // zero-point partials of all K warps in place
-            if (warp == 0 && lane < NR) {
-                const int r = lane, base = (r >> 3) * 4;
-                const float * rc = F + F_REDC + s * 64 + (r & 7);
+            if (warp == 0 && lane < R) {
+                const int r = lane, base = (r / RH) * 4;
+                const float * rc = F + F_REDC + s * 64 + (r % RH);
                 F[F_C + s * NR + r] = (rc[8 * base] + rc[8 * (base + 1)]) + (rc[8 * (base + 2)] + rc[8 * (base + 3)]);
             }
             if (warp == 0) warp_arrive(&bars[B_CFULL + s], lane);
@@ -361,9 +371,9 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
         const int vw = warp - W_V, tile = vw >> 2, quarter = warp & 3;
         const int d = 128 * tile + 32 * quarter + lane;
         const uint32_t lane_base = (uint32_t) (32 * quarter) << 16;
-        float acc[NR];
+        float acc[R];
 #pragma unroll
-        for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
         float vc_prev = 0.0f;
         Cursor ecur = cur;                                      // the epilogue's cursor lags one record
         uint32_t e3 = 0;                                        // e % 3: the softmax's alpha / z slot of record e
@@ -375,11 +385,11 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             if (!warp_wait(&bars[B_AZFULL + es], (e >> 1) & 1u, abort)) return false;
             tc::fence_after_sync();
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
+            for (int hh = 0; hh < R / 8; ++hh) {
                 uint32_t o[8], ol[8];
                 float al[8], z[8];
                 tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + 8 * hh, o);
-                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + NR + 8 * hh, ol);
+                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + R + 8 * hh, ol);
                 ld8(F + F_AL + e3 * NR + 8 * hh, al);
                 ld8(F + F_Z + e3 * NR + 8 * hh, z);
                 tc::wait_ld();
@@ -394,7 +404,7 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 const TwItem & itm = p.item[ecur.it];
                 const int hl = (int) (itm.seq_hl >> 16), slot = (int) (itm.h_slot >> 16);
 #pragma unroll
-                for (int r = 0; r < NR; ++r) {
+                for (int r = 0; r < R; ++r) {
                     if (r < p.rows)
                         p.part[((size_t) slot * p.n_rows + (size_t) (p.row_q[r] + hl * p.grp)) * (D + 2) + 2 + d] = acc[r];
                     acc[r] = 0.0f;
@@ -437,21 +447,26 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
             // every softmax warp reaches the group barriers below on every record, also after a wait gave up
             bool ok = warp_wait(&bars[B_SFULL + s], (g >> 1) & 1u, abort) && warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
                       warp_wait(&bars[B_CFULL + s], (g >> 1) & 1u, abort);
-            float sc[16], vsc = 0.0f, vz = 0.0f;
+            float sc[R], vsc = 0.0f, vz = 0.0f;
             if (ok) {
                 tc::fence_after_sync();
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
                 const float kt = h2f_at(rec + l.k_tok + 2 * t);
                 vsc = h2f_at(rec + l.v_scale + 2 * t);
                 vz = h2f_at(rec + l.v_zero + 2 * t);
-                float c[16];
-                ld8(F + F_C + s * NR, *reinterpret_cast<float (*)[8]>(c));
-                ld8(F + F_C + s * NR + 8, *reinterpret_cast<float (*)[8]>(c + 8));
+                float c[R];
+#pragma unroll
+                for (int i = 0; i < R / 8; ++i) ld8(F + F_C + s * NR + 8 * i, *reinterpret_cast<float (*)[8]>(c + 8 * i));
                 // the record stage and C[s] are rewritten only after this arrival (record g + 2)
                 warp_arrive(&bars[B_REMPTY + s], lane);
-                uint32_t a[16], al[16];
-                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
-                tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + NR, al);
+                uint32_t a[R], al[R];
+                if constexpr (R == 16) {
+                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
+                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + R, al);
+                } else {
+                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s, a);
+                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + R, al);
+                }
                 tc::wait_ld();
                 tc::fence_before_sync();
                 warp_arrive(&bars[B_SFREE + s], lane);
@@ -459,15 +474,15 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 const bool in = pos < sq.b_end;
                 const float kts = kt * sl2;
 #pragma unroll
-                for (int r = 0; r < NR; ++r) {
+                for (int r = 0; r < R; ++r) {
                     const bool vis = in && r < p.rows && pos < sq.qpos0 + p.row_iq[r] + 1u;
                     sc[r] = vis ? kts * ((__uint_as_float(a[r]) + __uint_as_float(al[r])) + c[r]) : -INFINITY;
                 }
-                const float mw = warp_rows16<true>(sc, lane);
-                if ((lane & 1) == 0) F[F_REDM + quarter * NR + (lane >> 1)] = mw;
+                const float mw = warp_rows<R, true>(sc, lane);
+                if (lane % LPR == 0) F[F_REDM + quarter * NR + lane / LPR] = mw;
             }
             if (!tc::nbar_and(2, 128, ok)) break;
-            if (warp == W_S && lane < NR) {
+            if (warp == W_S && lane < R) {
                 const int r = lane;
                 const float mrec = fmaxf(fmaxf(F[F_REDM + r], F[F_REDM + NR + r]), fmaxf(F[F_REDM + 2 * NR + r], F[F_REDM + 3 * NR + r]));
                 const float mnew = fmaxf(M, mrec);
@@ -476,30 +491,30 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
                 M = mnew;
             }
             tc::nbar_sync(2, 128);
-            float mn[16];
-            ld8(F + F_MN, *reinterpret_cast<float (*)[8]>(mn));
-            ld8(F + F_MN + 8, *reinterpret_cast<float (*)[8]>(mn + 8));
+            float mn[R];
+#pragma unroll
+            for (int i = 0; i < R / 8; ++i) ld8(F + F_MN + 8 * i, *reinterpret_cast<float (*)[8]>(mn + 8 * i));
             // B_V is free once the V MMAs of the previous record completed
             ok = g == 0 || warp_wait(&bars[B_VDONE + (s ^ 1u)], ((g - 1) >> 1) & 1u, abort);
             if (ok) {
                 uint8_t * bv = sm + OFF_BV;
-                float ls[16], zs[16];
+                float ls[R], zs[R];
 #pragma unroll
-                for (int r = 0; r < NR; ++r) {
+                for (int r = 0; r < R; ++r) {
                     const float pw = mn[r] == -INFINITY ? 0.0f : ex2(sc[r] - mn[r]);
                     ls[r] = pw;
                     zs[r] = pw * vz;
                     const float x = pw * vsc;
                     const __half hi = __float2half_rn(x);
                     *reinterpret_cast<__half *>(bv + h_off(r, t)) = hi;
-                    *reinterpret_cast<__half *>(bv + h_off(NR + r, t)) = __float2half_rn(x - __half2float(hi));
+                    *reinterpret_cast<__half *>(bv + h_off(R + r, t)) = __float2half_rn(x - __half2float(hi));
                 }
-                const float lw = warp_rows16<false>(ls, lane), zw = warp_rows16<false>(zs, lane);
-                if ((lane & 1) == 0) { F[F_REDL + quarter * NR + (lane >> 1)] = lw; F[F_REDZ + quarter * NR + (lane >> 1)] = zw; }
+                const float lw = warp_rows<R, false>(ls, lane), zw = warp_rows<R, false>(zs, lane);
+                if (lane % LPR == 0) { F[F_REDL + quarter * NR + lane / LPR] = lw; F[F_REDZ + quarter * NR + lane / LPR] = zw; }
                 tc::fence_proxy_async();
             }
             if (!tc::nbar_and(2, 128, ok)) break;
-            if (warp == W_S && lane < NR) {
+            if (warp == W_S && lane < R) {
                 const int r = lane;
                 const float lsum = (F[F_REDL + r] + F[F_REDL + NR + r]) + (F[F_REDL + 2 * NR + r] + F[F_REDL + 3 * NR + r]);
                 L = L * F[F_AL + g3 * NR + r] + lsum;
@@ -517,8 +532,8 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
         // ================================ issuer ================================
         // In program order: the K MMAs of record g, the V MMAs of record g - 1, the bulk copy of record g + 2; each
         // after blocking waits. Records up to four ahead are prefetched into L2, so the bulk copies read from it.
-        const uint32_t idesc_k = tc::idesc_f16(128, NB) | (1u << 15);    // A MN-major (tokens contiguous per channel)
-        const uint32_t idesc_v = tc::idesc_f16(128, NB);
+        const uint32_t idesc_k = tc::idesc_f16(128, 2 * R) | (1u << 15);  // A MN-major (tokens contiguous per channel)
+        const uint32_t idesc_v = tc::idesc_f16(128, 2 * R);
         const uint32_t rb = l.bytes;
         Cursor pc = cur, lc = cur;                              // L2 prefetch and load cursors
         uint32_t np = 0, nl = 0;                                // records prefetched / loaded
@@ -584,20 +599,24 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
     if (warp == W_I) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
-template <int BK, int BV>
+template <int BK, int BV, int R>
 int launch_kernel(const TwParams & p, sjk_stream st) {
-    auto kfn = attend_trellis_ws_kernel<BK, BV>;
+    auto kfn = attend_trellis_ws_kernel<BK, BV, R>;
     const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
     kfn<<<(unsigned) p.n_cta, NT, SMEM_TOTAL, st>>>(p);
     return sjk_check_launch();
 }
 
-int launch(const TwParams & p, sjk_stream st) {
+template <int R>
+int launch_rows(const TwParams & p, sjk_stream st) {
     const int bk = p.lay.bits_k, bv = p.lay.bits_v;
-    if (bk == 3) return bv == 3 ? launch_kernel<3, 3>(p, st) : launch_kernel<3, 2>(p, st);
-    return bv == 3 ? launch_kernel<2, 3>(p, st) : launch_kernel<2, 2>(p, st);
+    if (bk == 3) return bv == 3 ? launch_kernel<3, 3, R>(p, st) : launch_kernel<3, 2, R>(p, st);
+    return bv == 3 ? launch_kernel<2, 3, R>(p, st) : launch_kernel<2, 2, R>(p, st);
 }
+
+// the 8-row kernel for up to 8 query rows per KV head (decode width 1 or 2 at GQA 4), else the 16-row one
+int launch(const TwParams & p, sjk_stream st) { return p.rows <= 8 ? launch_rows<8>(p, st) : launch_rows<16>(p, st); }
 
 void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
     p.grp = n_head / n_kv;
