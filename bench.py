@@ -9,7 +9,8 @@ group-aligned tail to the config's 6,144). A step = one attention call per layer
 
   value    device time per layer call (us), inputs resident in HBM; CUDA events on the launching stream
   e2e      the same through the C-ABI with HOST buffers: per step the queries go host->device from pinned memory
-           and the outputs come back, inside the timed region
+           and the outputs come back, inside the timed region (layer by layer on two copy streams, overlapping the
+           attention of the neighbouring layers)
   seal     BASELINE config 0: seal one 4096-token commit (32 groups x 4 heads = 128 records, 4/4) out of an
            8,320-position tq6_0 ring; Mtok/s = 4096 / time; plus the ring write of those 8,320 positions
   cpu_baseline  the reference's own CPU attention (oracle/_ref, sj_kvarn_layer_attend_row) on the host cores, on
@@ -247,12 +248,29 @@ def run_gpu_arm(args, torch, dist, rank, world, local_rank):
     q_h = q.cpu().pin_memory()
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
 
+    # every step, the queries go host -> device and the outputs come back, layer by layer on two copy streams: layer
+    # il's copy in overlaps the attention of the layers before it and its copy out the layers after it; the step ends
+    # on `s` once the last output has landed in host memory
+    cs_in, cs_out = torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(c["LAYERS"])]
+    ev_out = [torch.cuda.Event() for _ in range(c["LAYERS"])]
+
     def step_e2e():
-        with torch.cuda.stream(s):
-            q.copy_(q_h, non_blocking=True)
-        step()
-        with torch.cuda.stream(s):
-            out_h.copy_(out, non_blocking=True)
+        cs_in.wait_stream(s)                                   # the previous step's reads of q are done
+        for il, lay in enumerate(m.layers):
+            with torch.cuda.stream(cs_in):
+                q[il].copy_(q_h[il], non_blocking=True)
+                ev_in[il].record(cs_in)
+            s.wait_event(ev_in[il])
+            rc = L.sjk_layer_attend(C.byref(lay), B, N, N - n_q, n_q, n_head, C.c_void_p(q.data_ptr() + il * per * 4),
+                                    SCALE, C.c_void_p(out.data_ptr() + il * per * 4), st)
+            if rc:
+                raise sjk.SjkError(rc, "attend")
+            ev_out[il].record(s)
+            cs_out.wait_event(ev_out[il])
+            with torch.cuda.stream(cs_out):
+                out_h[il].copy_(out[il], non_blocking=True)
+        s.wait_stream(cs_out)
 
     ms_e2e = time_events(torch, s, step_e2e, args.steps, args.warmup, barrier)
     if dist:
