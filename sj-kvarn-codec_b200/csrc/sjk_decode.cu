@@ -170,3 +170,42 @@ int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, f
     kv_row_kernel<<<1, 256, 0, st>>>(*v, B, pos, h, k, vo);
     return sjk_check_launch();
 }
+
+// ---- record groups moved through a block table (state save / restore, truncation) ----------------------------
+// Group g (the n_head_kv records of one 128-token group of a layer) lives at body + blk(g) * group_bytes with
+// blk(g) = blocks ? blocks[g] : g (sj_kvarn.h:1429-1432, 1706-1739). One CTA per group moves it in words of T
+// (16, 4 or 1 bytes, the widest that divides group_bytes): op 0 gathers groups [g0, g0 + n) into buf (group order),
+// op 1 scatters buf into them, op 2 zeroes them; groups whose block is SJKVARN_NO_BLOCK are skipped (op 0 writes
+// zeros for them).
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256) group_move_kernel(uint8_t * body, const uint32_t * blocks, uint32_t g0, size_t group_bytes,
+                                                         uint8_t * buf, int op) {
+    const uint32_t g = g0 + blockIdx.x;
+    const uint32_t blk = blocks ? blocks[g] : g;
+    const size_t nw = group_bytes / sizeof(T);
+    T * b = reinterpret_cast<T *>(buf + (size_t) blockIdx.x * group_bytes);
+    const T zero{};
+    if (blk == SJKVARN_NO_BLOCK) {
+        if (op == 0)
+            for (size_t i = threadIdx.x; i < nw; i += blockDim.x) b[i] = zero;
+        return;
+    }
+    T * d = reinterpret_cast<T *>(body + (size_t) blk * group_bytes);
+    for (size_t i = threadIdx.x; i < nw; i += blockDim.x) {
+        if (op == 0) b[i] = d[i];
+        else if (op == 1) d[i] = b[i];
+        else d[i] = zero;
+    }
+}
+}  // namespace
+
+int sjk_group_move(uint8_t * body, const uint32_t * blocks, uint32_t g0, uint32_t n, size_t group_bytes, uint8_t * buf, int op,
+                   sjk_stream st) {
+    if (n == 0) return 0;
+    if (!body || (op != 2 && !buf) || op < 0 || op > 2) return SJKVARN_ERR_ARG;
+    if (group_bytes % 16 == 0) group_move_kernel<uint4><<<n, 256, 0, st>>>(body, blocks, g0, group_bytes, buf, op);
+    else if (group_bytes % 4 == 0) group_move_kernel<uint32_t><<<n, 256, 0, st>>>(body, blocks, g0, group_bytes, buf, op);
+    else group_move_kernel<uint8_t><<<n, 256, 0, st>>>(body, blocks, g0, group_bytes, buf, op);
+    return sjk_check_launch();
+}

@@ -447,10 +447,14 @@ extern "C" void sj_kvarn_layer_truncate(sj_kvarn_layer * L, uint32_t B_old, uint
     const int H = L->cfg.n_head_kv;
     int rc = 0;
     if (B_new < B_old) {
-        for (uint32_t g = (B_new - S) / G; g < (B_old - S) / G && !rc; ++g) {
-            if (L->blocks && L->blocks[g] == SJKVARN_NO_BLOCK) continue;
-            rc = ck(cudaMemsetAsync(sj_kvarn_layer_record(L, g, 0), 0, (size_t) H * L->lay.bytes, L->stream));
-        }
+        // the dropped groups: one memset over a contiguous body, one scrub launch through a pool's block table
+        const uint32_t g0 = (B_new - S) / G, g1 = (B_old - S) / G;
+        const size_t grp = (size_t) H * L->lay.bytes;
+        if (!L->blocks) rc = ck(cudaMemsetAsync(L->body + (size_t) g0 * grp, 0, (size_t) (g1 - g0) * grp, L->stream));
+        else if (L->d_blocks) rc = sjk_group_move(L->body, L->d_blocks, g0, g1 - g0, grp, NULL, 2, L->stream);
+        else
+            for (uint32_t g = g0; g < g1 && !rc; ++g)
+                if (L->blocks[g] != SJKVARN_NO_BLOCK) rc = ck(cudaMemsetAsync(L->body + (size_t) L->blocks[g] * grp, 0, grp, L->stream));
     }
     if (resume < n_old && resume < S && !rc) {
         const uint32_t end = n_old < S ? n_old : S;
@@ -745,9 +749,29 @@ static int ring_span(const sj_kvarn_layer * L, uint32_t pos_from, uint32_t pos_t
     return 0;
 }
 
-// Copy records of groups [0, n_rec) between device and host; runs of consecutive blocks move in one copy.
+// Copy records of groups [0, n_rec) between device and host. A contiguous body moves in one copy; a pool's
+// scattered blocks are gathered into (or scattered from) a stream-ordered device staging buffer by one kernel, so
+// the host sees one copy per layer instead of one per run of consecutive blocks.
 static int record_span(const sj_kvarn_layer * L, uint32_t n_rec, uint8_t * host, int to_host, sjk_stream st) {
     const size_t grp = (size_t) L->cfg.n_head_kv * L->lay.bytes;
+    if (n_rec == 0) return 0;
+    uint32_t runs = 1;
+    for (uint32_t g = 1; g < n_rec && L->blocks; ++g) runs += L->blocks[g] != L->blocks[g - 1] + 1u;
+    if (L->blocks && L->d_blocks && runs > 1) {
+        uint8_t * stage = NULL;
+        const size_t bytes = (size_t) n_rec * grp;
+        int rc = ck(cudaMallocAsync((void **) &stage, bytes, st));
+        if (rc) return rc;
+        if (to_host) {
+            rc = sjk_group_move(L->body, L->d_blocks, 0, n_rec, grp, stage, 0, st);
+            if (!rc) rc = ck(cudaMemcpyAsync(host, stage, bytes, cudaMemcpyDeviceToHost, st));
+        } else {
+            rc = ck(cudaMemcpyAsync(stage, host, bytes, cudaMemcpyHostToDevice, st));
+            if (!rc) rc = sjk_group_move(L->body, L->d_blocks, 0, n_rec, grp, stage, 1, st);
+        }
+        const int rf = ck(cudaFreeAsync(stage, st));
+        return rc ? rc : rf;
+    }
     uint32_t g = 0;
     while (g < n_rec) {
         const uint32_t b0 = L->blocks ? L->blocks[g] : g;

@@ -46,3 +46,9 @@ int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpo
 int sjk_tc_body_status_take(void);
 int sjk_tc_dense_status_take(void);
 int sjk_tc_trellis_status_take(void);
+
+// Move the record groups [g0, g0 + n) of one layer (group_bytes = n_head_kv x record bytes) through
+// an optional device block table: op 0 gathers them into buf (group order), op 1 scatters buf into them, op 2
+// zeroes them. Groups with no block are skipped (op 0 writes zeros for them). One launch (sjk_decode.cu).
+int sjk_group_move(uint8_t * body, const uint32_t * blocks, uint32_t g0, uint32_t n, size_t group_bytes, uint8_t * buf, int op,
+                   sjk_stream st);

@@ -203,3 +203,47 @@ def test_seq_store_prefill_matches_per_position(L):
     assert np.array_equal(a.state(), b.state())
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("bk,bv,body", [(3, 3, 1), (4, 4, 0)])
+def test_state_pool_interleaved(L, oracle_lib, bk, bv, body):
+    """Sequences whose pool blocks interleave: their state streams (records gathered on the device, one copy per
+    layer) equal the oracle's contiguous caches byte for byte; a truncation zeroes exactly the dropped blocks (one
+    scrub launch through the block table, sj_kvarn.h:1581-1603); a stream restored into the scattered blocks the
+    truncation freed (scatter on the device) writes back identically and attends like the original."""
+    pool, devs, oras = _build(L, oracle_lib, bk, bv, body, seed=57 + bk)
+    extra = []
+    try:
+        states = [d.state() for d in devs]
+        for i, (st, o) in enumerate(zip(states, oras)):
+            assert np.array_equal(st, o.state()), i
+        # the long sequence's blocks are interleaved with the others': more than one run of consecutive ids
+        d3 = devs[3]
+        n_rec = (d3.pol.B - 128) // 128
+        ids = [d3.s.blocks[g] for g in range(n_rec)]
+        assert sum(ids[g] != ids[g - 1] + 1 for g in range(1, n_rec)) > 1
+        grp = H * pool.lay.bytes
+        layer0 = lambda: gu.d2h_ptr(pool.body, pool.n_blocks * grp).reshape(pool.n_blocks, grp)
+        before = layer0()
+        cut = 128 + 3 * 128 + 40
+        r = d3.truncate(cut)
+        assert r == 128 + 3 * 128
+        dropped = ids[3:]
+        after = layer0()
+        assert not after[dropped].any()
+        keep = [b for b in range(pool.n_blocks) if b not in dropped]
+        assert np.array_equal(after[keep], before[keep])
+        # restore sequence 2 into the freed blocks (popped in reverse: descending ids)
+        r2 = gu.DevSeq(devs[2].cfg, 1, pool)
+        extra.append(r2)
+        assert r2.read_state(states[2]) == 0
+        ids2 = [r2.s.blocks[g] for g in range((r2.pol.B - 128) // 128)]
+        assert sum(ids2[g] != ids2[g - 1] + 1 for g in range(1, len(ids2))) > 1
+        assert np.array_equal(r2.state(), states[2])
+        _attend_case(L, [r2], [oras[2]], 2, 4, False, 9)
+    finally:
+        for d in devs + extra:
+            d.close()
+        for o in oras:
+            o.close()
+        L.sj_kvarn_pool_free(C.byref(pool))
