@@ -299,8 +299,9 @@ typedef struct sjk_view {
 } sjk_view;
 
 int          sjk_last_error(void);          /* sticky status of the void-returning calls; clears it */
-/* Device status word of the kernels (synchronizes the device): 0 = fine, 1 = a bounded in-kernel wait ran
- * out (the kernel skipped its remaining work and released its resources). Reading clears it. */
+/* Device status word of the kernels (synchronizes the device): 0 = fine, bit 1 (SJK_DEVICE_TIMEOUT) = a bounded
+ * in-kernel wait ran out (the kernel skipped its remaining work and released its resources), bit 2
+ * (SJK_DEVICE_DESC) = a descriptor-driven call met a descriptor that does not fit its cache. Reading clears it. */
 int          sjk_device_status(void);
 int          sjk_last_cuda_error(void);     /* cudaError_t of the last failed CUDA call */
 const char * sjk_version(void);
@@ -380,6 +381,42 @@ int sjk_attend_batch(const sjk_view * views, const uint32_t * B, const uint32_t 
  * stream capture. All calls share the array: calls that overlap on the GPU race. Allocates nothing. */
 int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
                       float scale, float * out, sjk_stream st);
+
+/* ---- descriptor-driven calls: the reference's ggml op boundary (INTEGRATION_LLAMACPP.md:44-74) ----
+ * A descriptor is SJK_DESC_N_ENTRIES int32 values in DEVICE memory describing one sequence's cache for one
+ * ubatch, in the reference's entry order (ggml_sjkvarn_desc). The calls below read it when their kernels run,
+ * not when they are issued: their launch shapes depend only on the cache and on fixed maxima, so a CUDA graph
+ * captured once (seal, store and attention of every layer) replays for every decode step with only the
+ * descriptor's contents changing (INTEGRATION_LLAMACPP.md:72-74). TYPE_K / TYPE_V hold the cache's
+ * SJKVARN_STAGING_* value, BODY_TYPE its SJKVARN_BODY_*, SINK_TYPE its SJKVARN_SINK_*; entries 14 and 15 are
+ * reserved (0). Every kernel checks the static entries (S, CAP, G, D, RECBYTES, HKV, the types) against the view
+ * it was launched on, B and B_OLD for group boundaries at or past the sink with B_OLD <= B, and that the staged
+ * positions [max(B, S), N) fit the ring; a descriptor that fails makes the call write nothing (sjk_attend_dyn: a
+ * zero output) and sets bit SJK_DEVICE_DESC in sjk_device_status(). */
+enum {
+    SJK_DESC_S = 0, SJK_DESC_CAP, SJK_DESC_B, SJK_DESC_N, SJK_DESC_QPOS0, SJK_DESC_G, SJK_DESC_D, SJK_DESC_RECBYTES,
+    SJK_DESC_HKV, SJK_DESC_B_OLD, SJK_DESC_TYPE_K, SJK_DESC_TYPE_V, SJK_DESC_BODY_TYPE, SJK_DESC_SINK_TYPE,
+    SJK_DESC_N_ENTRIES = 16
+};
+enum { SJK_DEVICE_TIMEOUT = 1, SJK_DEVICE_DESC = 2 };
+/* Fill a host descriptor for view v: seal [B_old, B) this ubatch, positions [0, N) visible, first query row at
+ * qpos0. Returns SJKVARN_ERR_ARG for values that the kernels would reject. */
+int sjk_desc_fill(const sjk_view * v, uint32_t B_old, uint32_t B, uint32_t N, uint32_t qpos0, int32_t * desc);
+/* ggml_sjkvarn_seal_dyn (INTEGRATION_LLAMACPP.md:49): seal the groups covering [B_OLD, B) out of the staging ring
+ * into v->body (records at v->blocks), as sjk_seal_ring. The launch covers n_groups_max groups; a descriptor asking
+ * for more is rejected. */
+int sjk_seal_dyn(const sjk_view * v, const int32_t * desc, uint32_t n_groups_max, int iters, sjk_stream st);
+/* ggml_set_rows_stage (INTEGRATION_LLAMACPP.md:48): store n_pos positions QPOS0 .. QPOS0 + n_pos - 1 as sjk_store
+ * (k, vv: [n_pos][n_head_kv][D] device floats; rotate as sjk_store). */
+int sjk_store_dyn(const sjk_view * v, const int32_t * desc, uint32_t n_pos, const float * k, const float * vv, int rotate,
+                  sjk_stream st);
+/* The region-aware flash attention (INTEGRATION_LLAMACPP.md:50): sjk_attend with B, N and qpos0 taken from the
+ * descriptor. Same kernels and the same work split as sjk_attend for the same values, so the output is identical.
+ * scratch: at least sjk_attend_dyn_scratch_bytes() bytes (the launch plans and the split partials); allocates
+ * nothing. */
+size_t sjk_attend_dyn_scratch_bytes(const sjk_view * v, int n_q, int n_head);
+int sjk_attend_dyn(const sjk_view * v, const int32_t * desc, int n_q, int n_head, const float * q, float scale, float * out,
+                   void * scratch, size_t scratch_bytes, sjk_stream st);
 
 /* Whole-layer helpers over a device-backed sj_kvarn_layer (its stream is ignored; st used). */
 int sjk_layer_store(sj_kvarn_layer * L, uint32_t pos0, uint32_t n_pos, const float * k, const float * v, int rotate,

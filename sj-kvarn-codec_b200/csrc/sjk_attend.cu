@@ -14,6 +14,7 @@
 
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
+#include "sjk_plan.cuh"
 
 namespace {
 
@@ -33,6 +34,7 @@ struct AttnParams {
     int chunks_per_split, n_chunks;
     uint32_t n_sink_chunks, n_body_chunks;
     uint32_t body_skip;             // leading body records handled by the tensor-core kernel
+    int n_splits;                   // splits per KV head (the descriptor-driven grid may be wider)
 };
 
 struct Chunk { int region; uint32_t p0, len, g; };   // region 0 sink, 1 body, 2 ring
@@ -106,7 +108,7 @@ SJK_DEV void load_rows(const AttnParams & p, const Chunk & c, uint32_t t0, uint3
 }
 
 template <int D>
-__global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
+SJK_DEV void split_body(const AttnParams & p) {
     extern __shared__ __align__(16) float sm[];
     float * Ks = sm;                                  // [SUB][D+1]
     float * Vs = Ks + SUB * (D + 1);                  // [SUB][D+1]
@@ -227,6 +229,16 @@ __global__ void __launch_bounds__(NT) attend_split_kernel(AttnParams p) {
     }
 }
 
+template <int D>
+__global__ void __launch_bounds__(NT) attend_split_kernel(const __grid_constant__ AttnParams p) { split_body<D>(p); }
+
+// the descriptor-driven form: the plan was made on the device (attend_dyn_plan_kernel)
+template <int D>
+__global__ void __launch_bounds__(NT) attend_split_dyn_kernel(const AttnParams * __restrict__ pp) {
+    if ((int) blockIdx.x >= pp->n_splits) return;
+    split_body<D>(*pp);
+}
+
 // out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m). Grid (query row x head, channel tiles of
 // 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
 constexpr int MERGE_SPLITS = 768;                     // >= the most splits a call can make (148 + 296 + 296)
@@ -234,14 +246,16 @@ constexpr int MERGE_PRE = 24;                         // outputs per thread load
 
 // part_out (optional): instead of out, write the combined partial (m, l, o[D]) of each row (o not normalized), the
 // form sjk_attend_partial returns
+// splits_dev (optional): read the split count from device memory (the descriptor-driven call's plan)
 __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out,
-                                                           float * part_out) {
+                                                           float * part_out, const int * splits_dev) {
     extern __shared__ float wts[];                     // [splits] weights, then [4][64] partial sums
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // launched as a programmatic dependent of the kernels that write the partials: wait until they completed
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (splits_dev) splits = *splits_dev;
     // the outputs of the first MERGE_PRE splits of this thread's group go in flight with the (m, l) loads
     const int dl = tid & 63, grp4 = tid >> 6;
     const bool live = d0 + dl < D;
@@ -308,35 +322,6 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     }
 }
 
-struct Plan { int splits, chunks_per_split, n_chunks; uint32_t n_sink, n_body; };
-
-// upper bound of the split count: about two CTAs per SM over the call's KV heads
-int split_target(int n_kv) {
-    const int H = n_kv > 0 ? n_kv : 1;
-    const int t = (2 * 148 + H - 1) / H;
-    return t < 1 ? 1 : t;
-}
-
-// chunks left to the CUDA-core kernel: the body after the first body_skip records, plus the sink and the
-// staging ring unless the dense tensor-core kernel takes them (no_staged)
-Plan make_plan(const sjk_view * v, uint32_t B, uint32_t N, int n_kv, uint32_t body_skip, bool no_staged, unsigned regions) {
-    Plan pl;
-    const uint32_t S = v->S;
-    const uint32_t s_end = S < N ? S : N;
-    pl.n_sink = (no_staged || !(regions & SJK_REGION_SINK)) ? 0u : (s_end + 127u) / 128u;
-    const uint32_t b_end = B < N ? B : N;
-    pl.n_body = (b_end > S && (regions & SJK_REGION_BODY)) ? (b_end - S + 127u) / 128u : 0u;
-    pl.n_body = pl.n_body > body_skip ? pl.n_body - body_skip : 0u;
-    const uint32_t t0 = B > S ? B : S;
-    const uint32_t n_tail = (N > t0 && !no_staged && (regions & SJK_REGION_RING)) ? (N - t0 + 127u) / 128u : 0u;
-    pl.n_chunks = (int) (pl.n_sink + pl.n_body + n_tail);
-    const int target = split_target(n_kv);
-    pl.chunks_per_split = (pl.n_chunks + target - 1) / target;
-    if (pl.chunks_per_split < 1) pl.chunks_per_split = 1;
-    pl.splits = pl.n_chunks > 0 ? (pl.n_chunks + pl.chunks_per_split - 1) / pl.chunks_per_split : 1;
-    return pl;
-}
-
 template <int D>
 size_t split_smem() {
     return (size_t) (2 * SUB * (D + 1) + MAXROWS * D + MAXROWS * SUB + 3 * D + 384 + 1024 + 3 * MAXROWS) * sizeof(float);
@@ -347,7 +332,7 @@ size_t split_smem() {
 size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv) {
     if (!v || n_q <= 0 || n_head <= 0) return 0;
     // CUDA-core, tensor-core body and tensor-core staged-row splits, each bounded by the per-call target
-    return (size_t) 3 * split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    return (size_t) 3 * sjk_split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
 }
 
 extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head) {
@@ -355,6 +340,72 @@ extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n
     if (!v) return 0;
     return sjk_attend_heads_scratch_bytes(v, n_q, n_head, v->n_head_kv);
 }
+
+namespace {
+
+sjk_paths paths_of(const sjk_view * v, int n_q, int grp) {
+    sjk_paths pa;
+    pa.tc_body = sjk_tc_body_supported(v, n_q, grp) != 0;
+    pa.tc_trellis = !pa.tc_body && sjk_tc_trellis_supported(v, n_q, grp) != 0;
+    pa.dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
+    pa.fused = pa.tc_body && pa.dense;
+    return pa;
+}
+
+// the CUDA-core kernel over the chunks of p (grid: splits x KV heads); dyn: its plan in device memory instead
+int launch_split(const AttnParams & p, const AttnParams * dyn, int splits, int n_kv, sjk_stream st) {
+    const dim3 grid((unsigned) splits, (unsigned) n_kv);
+    cudaError_t e = cudaSuccess;
+    switch (p.v.lay.D) {
+        case 128: {
+            const size_t sm = split_smem<128>();
+            if (dyn) {
+                e = cudaFuncSetAttribute(attend_split_dyn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_dyn_kernel<128><<<grid, NT, sm, st>>>(dyn);
+            } else {
+                e = cudaFuncSetAttribute(attend_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_kernel<128><<<grid, NT, sm, st>>>(p);
+            }
+            break;
+        }
+        case 256: {
+            const size_t sm = split_smem<256>();
+            if (dyn) {
+                e = cudaFuncSetAttribute(attend_split_dyn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_dyn_kernel<256><<<grid, NT, sm, st>>>(dyn);
+            } else {
+                e = cudaFuncSetAttribute(attend_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
+                if (e == cudaSuccess) attend_split_kernel<256><<<grid, NT, sm, st>>>(p);
+            }
+            break;
+        }
+        default: return SJK_ERR_UNSUPPORTED;
+    }
+    if (sjk_check(e)) return SJK_ERR_DEVICE;
+    return sjk_check_launch() ? SJK_ERR_DEVICE : 0;
+}
+
+// Programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them on the
+// device (griddepcontrol.wait), so the launch gap between the two kernels disappears. splits_dev: the split count
+// is read from device memory (shared memory sized for max_splits).
+int launch_merge(const float * part, int splits, const int * splits_dev, int max_splits, int n_rows, int D, float * out,
+                 float * part_out, sjk_stream st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t) ((splits_dev ? max_splits : splits) + 256) * sizeof(float);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, part, splits, n_rows, D, out, part_out, splits_dev)))
+        return SJK_ERR_DEVICE;
+    return sjk_check_launch();
+}
+
+}  // namespace
 
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
                      const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
@@ -367,89 +418,150 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (n_q * grp > MAXROWS) return SJK_ERR_UNSUPPORTED;
     // sealed records [0, n_tc) go to the tensor-core kernel when it supports the body format; when it also supports
     // the staged-row formats, the same kernel takes the sink and the staging ring, else the dense kernel does
-    const uint32_t b_end = B < N ? B : N;
-    const bool tc_body = sjk_tc_body_supported(v, n_q, grp) != 0;
-    const bool tc_trellis = !tc_body && sjk_tc_trellis_supported(v, n_q, grp) != 0;
-    const bool dense = sjk_tc_dense_supported(v, n_q, grp) != 0;
-    const bool fused = tc_body && dense;
-    const bool body_on = (regions & SJK_REGION_BODY) != 0;
-    const uint32_t n_tc = ((tc_body || tc_trellis) && body_on && b_end > v->S) ? (b_end - v->S) / 128u : 0u;
-    const unsigned staged = regions & (SJK_REGION_SINK | SJK_REGION_RING);
-    uint32_t n_sink_d = 0, n_dense = 0;
-    if (dense && !fused) {
-        const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
-        n_sink_d = (regions & SJK_REGION_SINK) ? (s_end + 127u) / 128u : 0u;
-        n_dense = n_sink_d + ((regions & SJK_REGION_RING) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
-    }
-    int cps_d = 1;
-    const int splits_d = (dense && !fused) ? sjk_tc_dense_splits(n_dense, n_kv, &cps_d) : 0;
-    const Plan pl = make_plan(v, B, N, n_kv, n_tc, dense, regions);
-    const int splits_v1 = pl.n_chunks > 0 ? pl.splits : 0;
+    const sjk_paths pa = paths_of(v, n_q, grp);
+    sjk_dyn_state d;
+    sjk_plan_counts(pa, v->S, B, N, regions, n_kv, &d);
     // the tensor-core kernel's split count is known after its launch plan; bound it for the scratch check
-    const int splits_tc_max = (tc_body && (n_tc > 0 || (fused && staged))) ? sjk_tc_body_max_splits(n_kv)
-                              : (tc_trellis && n_tc > 0)      ? sjk_tc_trellis_max_splits(n_kv)
-                                                              : 0;
-    const size_t need = (size_t) (splits_tc_max + splits_d + splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
+    const unsigned staged = regions & (SJK_REGION_SINK | SJK_REGION_RING);
+    const int splits_tc_max = (pa.tc_body && (d.n_tc > 0 || (pa.fused && staged))) ? sjk_tc_body_max_splits(n_kv)
+                              : (pa.tc_trellis && d.n_tc > 0)                       ? sjk_tc_trellis_max_splits(n_kv)
+                                                                                    : 0;
+    const size_t need = (size_t) (splits_tc_max + d.splits_d + d.splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
-    if (splits_tc_max + splits_d + splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
+    if (splits_tc_max + d.splits_d + d.splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
     int splits_tc = 0;
     if (splits_tc_max) {
-        const unsigned dense_regions = fused ? ((regions & SJK_REGION_SINK) ? 1u : 0u) | ((regions & SJK_REGION_RING) ? 2u : 0u) : 0u;
-        const int rc = tc_body ? sjk_tc_body_launch(v, B, N, n_tc, (int) dense_regions, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
-                                                    (float *) scratch, 0, &splits_tc, st)
-                               : sjk_tc_trellis_launch(v, B, N, n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
-                                                       (float *) scratch, 0, &splits_tc, st);
+        const int rc = pa.tc_body ? sjk_tc_body_launch(v, B, N, d.n_tc, (int) d.dense_regions, qpos0, n_q, n_head, kv_head0, n_kv, q,
+                                                       scale, (float *) scratch, 0, &splits_tc, st)
+                                  : sjk_tc_trellis_launch(v, B, N, d.n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
+                                                          (float *) scratch, 0, &splits_tc, st);
         if (rc) return rc;
     }
-    const int splits = splits_tc + splits_d + splits_v1;
+    const int splits = splits_tc + d.splits_d + d.splits_v1;
     // nothing to attend to: a zero output; an empty partial (m = -inf, l = 0, o = 0) comes from the merge kernel
     if (splits == 0 && !part_out) return sjk_check(cudaMemsetAsync(out, 0, (size_t) n_q * n_head * v->lay.D * sizeof(float), st));
-    if (splits_d) {
+    if (d.splits_d) {
         const int rc = sjk_tc_dense_launch(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch,
-                                           splits_tc, splits_d, n_sink_d, n_dense, cps_d, st);
+                                           splits_tc, d.splits_d, d.n_sink_d, d.n_dense, d.cps_d, st);
         if (rc) return rc;
     }
     AttnParams p;
     p.v = *v; p.kv0 = kv_head0; p.B = B; p.N = N; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = grp;
-    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch; p.split0 = splits_tc + splits_d;
-    p.chunks_per_split = pl.chunks_per_split; p.n_chunks = pl.n_chunks; p.n_sink_chunks = pl.n_sink; p.n_body_chunks = pl.n_body;
-    p.body_skip = n_tc;
-    if (splits_v1) {
-        const dim3 grid((unsigned) splits_v1, (unsigned) n_kv);
-        cudaError_t e = cudaSuccess;
-        switch (v->lay.D) {
-            case 128: {
-                const size_t sm = split_smem<128>();
-                e = cudaFuncSetAttribute(attend_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
-                if (e == cudaSuccess) attend_split_kernel<128><<<grid, NT, sm, st>>>(p);
-                break;
-            }
-            case 256: {
-                const size_t sm = split_smem<256>();
-                e = cudaFuncSetAttribute(attend_split_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sm);
-                if (e == cudaSuccess) attend_split_kernel<256><<<grid, NT, sm, st>>>(p);
-                break;
-            }
-            default: return SJK_ERR_UNSUPPORTED;
-        }
-        if (sjk_check(e)) return SJK_ERR_DEVICE;
-        if (sjk_check_launch()) return SJK_ERR_DEVICE;
+    p.rows = n_q * grp; p.q = q; p.scale = scale; p.part = (float *) scratch; p.split0 = splits_tc + d.splits_d;
+    p.chunks_per_split = d.v1.chunks_per_split; p.n_chunks = d.v1.n_chunks; p.n_sink_chunks = d.v1.n_sink;
+    p.n_body_chunks = d.v1.n_body; p.body_skip = d.n_tc; p.n_splits = d.splits_v1;
+    if (d.splits_v1) {
+        const int rc = launch_split(p, nullptr, d.splits_v1, n_kv, st);
+        if (rc) return rc;
     }
-    // programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them
-    // on the device (griddepcontrol.wait), so the launch gap between the two kernels disappears
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned) (n_q * n_head), (unsigned) ((v->lay.D + 63) / 64));
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t) (splits + 256) * sizeof(float);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, (const float *) p.part, splits, n_q * n_head, v->lay.D, out, part_out)))
-        return SJK_ERR_DEVICE;
-    return sjk_check_launch();
+    return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, part_out, st);
+}
+
+// ---- descriptor-driven attention (the reference's region-aware flash attention op, INTEGRATION_LLAMACPP.md:50) ----
+// The call's scratch: the device-side plan (counts, then each kernel's launch plan), then the split partials.
+namespace {
+
+constexpr size_t DYN_ALIGN = 256;
+size_t dyn_align(size_t x) { return (x + DYN_ALIGN - 1) & ~(DYN_ALIGN - 1); }
+struct DynLayout { size_t state, v1, body, dense, part, total_hdr; };
+DynLayout dyn_layout() {
+    DynLayout L;
+    L.state = 0;
+    L.v1 = dyn_align(sizeof(sjk_dyn_state));
+    L.body = L.v1 + dyn_align(sizeof(AttnParams));
+    const size_t tb = sjk_tc_body_params_bytes(), tt = sjk_tc_trellis_params_bytes();
+    L.dense = L.body + dyn_align(tb > tt ? tb : tt);
+    L.part = L.dense + dyn_align(sjk_tc_dense_params_bytes());
+    L.total_hdr = L.part;
+    return L;
+}
+
+// The counts of the call from the descriptor (sjk_plan_counts, as sjk_attend_heads makes them on the host) and the
+// CUDA-core kernel's plan. A descriptor that fails its checks plans no work (a zero output).
+__global__ void attend_dyn_plan_kernel(const int32_t * desc, sjk_desc_ref ref, sjk_paths pa, int n_kv, AttnParams tmpl,
+                                       sjk_dyn_state * ds, AttnParams * v1) {
+    if (threadIdx.x != 0) return;
+    sjk_desc_vals dv;
+    sjk_dyn_state d;
+    memset(&d, 0, sizeof d);
+    if (sjk_desc_read(desc, ref, &dv)) {
+        d.ok = 1;
+        sjk_plan_counts(pa, ref.S, dv.B, dv.N, SJK_REGION_ALL, n_kv, &d);
+        d.qpos0 = dv.qpos0;
+    } else {
+        sjk_desc_fault();
+        d.B = ref.S; d.N = 0;
+    }
+    *ds = d;
+    AttnParams p = tmpl;
+    p.B = d.B; p.N = d.N; p.qpos0 = d.qpos0; p.split0 = d.splits_tc + d.splits_d;
+    p.chunks_per_split = d.v1.chunks_per_split; p.n_chunks = d.v1.n_chunks; p.n_sink_chunks = d.v1.n_sink;
+    p.n_body_chunks = d.v1.n_body; p.body_skip = d.n_tc; p.n_splits = d.ok ? d.splits_v1 : 0;
+    *v1 = p;
+}
+
+}  // namespace
+
+extern "C" size_t sjk_attend_dyn_scratch_bytes(const sjk_view * v, int n_q, int n_head) {
+    if (!v || n_q <= 0 || n_head <= 0) return 0;
+    return dyn_layout().total_hdr + sjk_attend_heads_scratch_bytes(v, n_q, n_head, v->n_head_kv);
+}
+
+extern "C" int sjk_desc_fill(const sjk_view * v, uint32_t B_old, uint32_t B, uint32_t N, uint32_t qpos0, int32_t * desc) {
+    if (!v || !desc || B_old > 0x7FFFFFFFu || B > 0x7FFFFFFFu || N > 0x7FFFFFFFu || qpos0 > 0x7FFFFFFFu) return SJKVARN_ERR_ARG;
+    int32_t e[SJK_DESC_N_ENTRIES] = {0};
+    e[SJK_DESC_S] = (int32_t) v->S; e[SJK_DESC_CAP] = (int32_t) v->cap; e[SJK_DESC_B] = (int32_t) B; e[SJK_DESC_N] = (int32_t) N;
+    e[SJK_DESC_QPOS0] = (int32_t) qpos0; e[SJK_DESC_G] = v->lay.G; e[SJK_DESC_D] = v->lay.D;
+    e[SJK_DESC_RECBYTES] = (int32_t) v->lay.bytes; e[SJK_DESC_HKV] = v->n_head_kv; e[SJK_DESC_B_OLD] = (int32_t) B_old;
+    e[SJK_DESC_TYPE_K] = v->staging; e[SJK_DESC_TYPE_V] = v->staging; e[SJK_DESC_BODY_TYPE] = v->lay.body;
+    e[SJK_DESC_SINK_TYPE] = v->sink_type;
+    sjk_desc_vals dv;
+    if (!sjk_desc_check(e, sjk_desc_ref_of(*v), &dv)) return SJKVARN_ERR_ARG;
+    memcpy(desc, e, sizeof e);
+    return 0;
+}
+
+// Launch shapes depend only on the cache, n_q and n_head: the planner kernel writes the counts and every kernel's
+// plan into the scratch, each kernel reads its plan there and its CTAs past the plan return at once.
+extern "C" int sjk_attend_dyn(const sjk_view * v, const int32_t * desc, int n_q, int n_head, const float * q, float scale,
+                              float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
+    if (!v || !desc || !q || !out || n_q <= 0 || n_head <= 0 || v->n_head_kv <= 0 || n_head % v->n_head_kv) return SJKVARN_ERR_ARG;
+    const int n_kv = v->n_head_kv, grp = n_head / n_kv;
+    if (n_q * grp > MAXROWS) return SJK_ERR_UNSUPPORTED;
+    if (!scratch || scratch_bytes < sjk_attend_dyn_scratch_bytes(v, n_q, n_head)) return SJKVARN_ERR_ARG;
+    if (((uintptr_t) scratch) % DYN_ALIGN) return SJKVARN_ERR_ARG;
+    const sjk_paths pa = paths_of(v, n_q, grp);
+    const DynLayout L = dyn_layout();
+    uint8_t * base = static_cast<uint8_t *>(scratch);
+    sjk_dyn_state * ds = reinterpret_cast<sjk_dyn_state *>(base + L.state);
+    AttnParams * v1p = reinterpret_cast<AttnParams *>(base + L.v1);
+    float * part = reinterpret_cast<float *>(base + L.part);
+    AttnParams t;
+    memset(&t, 0, sizeof t);
+    t.v = *v; t.kv0 = 0; t.n_q = n_q; t.n_head = n_head; t.grp = grp; t.rows = n_q * grp; t.q = q; t.scale = scale; t.part = part;
+    attend_dyn_plan_kernel<<<1, 32, 0, st>>>(desc, sjk_desc_ref_of(*v), pa, n_kv, t, ds, v1p);
+    if (sjk_check_launch()) return SJK_ERR_DEVICE;
+    int rc = 0;
+    if (pa.tc_body) rc = sjk_tc_body_dyn_launch(v, n_q, n_head, 0, n_kv, q, scale, part, ds, base + L.body, st);
+    else if (pa.tc_trellis) rc = sjk_tc_trellis_dyn_launch(v, n_q, n_head, 0, n_kv, q, scale, part, ds, base + L.body, st);
+    if (rc) return rc;
+    const int target = sjk_split_target(n_kv);
+    if (pa.dense && !pa.fused) {
+        // the most items a plan can have: the dense split count never exceeds the target, nor the chunks of the sink
+        // and of a full ring (plus one for a ring range that straddles a chunk boundary)
+        const uint32_t max_chunks = (v->S + 127u) / 128u + (v->cap + 127u) / 128u + 1u;
+        const int per_head = (uint32_t) target < max_chunks ? target : (int) max_chunks;
+        rc = sjk_tc_dense_dyn_launch(v, n_q, n_head, 0, n_kv, q, scale, part, ds, base + L.dense, per_head * n_kv, st);
+        if (rc) return rc;
+    }
+    // the CUDA-core kernel: with both tensor-core paths it only takes the partly visible record of a query over a
+    // prefix (at most one chunk per KV head); otherwise up to the target
+    const int v1_max = ((pa.tc_body || pa.tc_trellis) && pa.dense) ? 1 : target;
+    rc = launch_split(t, v1p, v1_max, n_kv, st);
+    if (rc) return rc;
+    const int max_splits = (pa.tc_body ? sjk_tc_body_max_splits(n_kv) : pa.tc_trellis ? sjk_tc_trellis_max_splits(n_kv) : 0) +
+                           2 * target;
+    return launch_merge(part, 0, &ds->splits, max_splits, n_q * n_head, v->lay.D, out, nullptr, st);
 }
 
 // Attention over a subset of the regions, as one partial (m, l, o[D]) per (query row, query head). The
@@ -466,16 +578,20 @@ extern "C" int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, ui
 extern "C" int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st) {
     if (!parts || !out || n_parts <= 0 || n_rows <= 0 || D <= 0 || n_parts > MERGE_SPLITS) return SJKVARN_ERR_ARG;
     attend_merge_kernel<<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
-        parts, n_parts, n_rows, D, out, nullptr);
+        parts, n_parts, n_rows, D, out, nullptr, nullptr);
     return sjk_check_launch();
 }
 
-// status words of every kernel with bounded waits: 1 if any wait ran out since the last call
+SJK_DESC_STATUS_READER(attend_desc_status_take)
+
+// status words of every kernel with bounded waits (SJK_DEVICE_TIMEOUT) and of the descriptor-driven calls
+// (SJK_DEVICE_DESC) since the last call
 extern "C" int sjk_device_status(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take(), c = sjk_tc_trellis_status_take();
-    if (a < 0 || b < 0 || c < 0) return -1;
-    return a | b | c;
+    const int d = attend_desc_status_take(), e = sjk_seal_desc_status_take(), f = sjk_stage_desc_status_take();
+    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0) return -1;
+    return a | b | c | d | e | f;
 }
 
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,

@@ -19,6 +19,7 @@
 
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
+#include "sjk_plan.cuh"
 #include "sjk_tc.cuh"
 
 namespace {
@@ -53,6 +54,7 @@ struct DenseParams {
     int n_q, n_head, grp, rows;
     float scale;
     float * part;                       // [slots][n_q n_head][D + 2]
+    int n_items;                        // CTAs with an item (the descriptor-driven grid may be larger)
     DenseSeq seq[MAX_SEQS];
     DenseItem item[MAX_ITEMS];          // one per CTA
 };
@@ -91,7 +93,7 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t w) {
     return __half22float2(h);
 }
 
-__global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(const __grid_constant__ DenseParams p) {
+SJK_DEV void dense_body(const DenseParams & p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int quarter = warp & 3, half = warp >> 2, tl = quarter * 32 + lane;
@@ -410,6 +412,44 @@ __global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(const __grid_con
     if (warp == 0) tc::tmem_dealloc(*tmem_slot, TM_COLS);
 }
 
+__global__ void __launch_bounds__(NT, 2) attend_dense_tc_kernel(const __grid_constant__ DenseParams p) { dense_body(p); }
+
+// the descriptor-driven form: items planned on the device (dense_dyn_plan_kernel); CTAs past them return at once
+__global__ void __launch_bounds__(NT, 2) attend_dense_tc_dyn_kernel(const DenseParams * __restrict__ pp) {
+    if ((int) blockIdx.x >= pp->n_items) return;
+    dense_body(*pp);
+}
+
+// One sequence: chunk list [0, n_chunks) (sink chunks first) of KV heads kv0 .. kv0 + n_kv - 1, `splits` items of
+// chunks_per_split chunks per head; item (head hl, split s) writes partial slot split0 + s. Runs on the host and in
+// the planner kernel of the descriptor-driven call.
+SJK_HD void fill_single(DenseParams & p, const sjk_view & v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                        int kv0, int n_kv, const float * q, float scale, float * part, int split0, int splits,
+                        uint32_t n_sink_chunks, uint32_t n_chunks, int chunks_per_split) {
+    p.v = v; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp; p.scale = scale; p.part = part;
+    p.seq[0].sink = v.sink; p.seq[0].ring = v.ring; p.seq[0].q = q; p.seq[0].B = B; p.seq[0].N = N; p.seq[0].qpos0 = qpos0;
+    p.seq[0].n_sink_chunks = n_sink_chunks;
+    int k = 0;
+    for (int hl = 0; hl < n_kv; ++hl)
+        for (int s = 0; s < splits; ++s, ++k) {
+            DenseItem & it = p.item[k];
+            it.seq_hl = (uint32_t) hl << 16;
+            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
+            it.c0 = (uint32_t) s * (uint32_t) chunks_per_split;
+            it.c1 = it.c0 + (uint32_t) chunks_per_split < n_chunks ? it.c0 + (uint32_t) chunks_per_split : n_chunks;
+        }
+    p.n_items = k;
+}
+
+// planner of the descriptor-driven call: the plan of sjk_tc_dense_launch for the counts in *ds
+__global__ void dense_dyn_plan_kernel(const sjk_dyn_state * __restrict__ ds, sjk_view v, int n_q, int n_head, int kv0, int n_kv,
+                                      const float * q, float scale, float * part, DenseParams * out) {
+    if (threadIdx.x != 0) return;
+    const sjk_dyn_state d = *ds;
+    fill_single(*out, v, d.B, d.N, d.qpos0, n_q, n_head, kv0, n_kv, q, scale, part, d.splits_tc, d.ok ? d.splits_d : 0,
+                d.n_sink_d, d.n_dense, d.cps_d);
+}
+
 }  // namespace
 
 // Whether the dense tensor-core path applies to the staged regions: D = 256, <= 16 query rows per KV head.
@@ -418,13 +458,10 @@ int sjk_tc_dense_supported(const sjk_view * v, int n_q, int grp) {
 }
 
 int sjk_tc_dense_splits(uint32_t n_chunks, int n_kv, int * chunks_per_split) {
-    if (n_chunks == 0) { *chunks_per_split = 1; return 0; }
-    const int target = (2 * 148 + n_kv - 1) / n_kv;
-    int cps = (int) ((n_chunks + (uint32_t) target - 1) / (uint32_t) target);
-    if (cps < 1) cps = 1;
-    *chunks_per_split = cps;
-    return (int) ((n_chunks + (uint32_t) cps - 1) / (uint32_t) cps);
+    return sjk_dense_split_count(n_chunks, n_kv, chunks_per_split);
 }
+
+size_t sjk_tc_dense_params_bytes(void) { return sizeof(DenseParams); }
 
 namespace {
 int dense_launch_params(const DenseParams & p, int n_items, sjk_stream st) {
@@ -443,19 +480,25 @@ int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpo
     if (splits <= 0) return 0;
     if (splits * n_kv > MAX_ITEMS || split0 + splits > 0xFFFF) return SJK_ERR_UNSUPPORTED;
     static thread_local DenseParams p;
-    p.v = *v; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp; p.scale = scale; p.part = part;
-    p.seq[0].sink = v->sink; p.seq[0].ring = v->ring; p.seq[0].q = q; p.seq[0].B = B; p.seq[0].N = N; p.seq[0].qpos0 = qpos0;
-    p.seq[0].n_sink_chunks = n_sink_chunks;
-    int k = 0;
-    for (int hl = 0; hl < n_kv; ++hl)
-        for (int s = 0; s < splits; ++s, ++k) {
-            DenseItem & it = p.item[k];
-            it.seq_hl = (uint32_t) hl << 16;
-            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
-            it.c0 = (uint32_t) s * (uint32_t) chunks_per_split;
-            it.c1 = it.c0 + (uint32_t) chunks_per_split < n_chunks ? it.c0 + (uint32_t) chunks_per_split : n_chunks;
-        }
-    return dense_launch_params(p, k, st);
+    fill_single(p, *v, B, N, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, splits, n_sink_chunks, n_chunks,
+                chunks_per_split);
+    return dense_launch_params(p, p.n_items, st);
+}
+
+// Descriptor-driven form: the counts come from *ds (written on the device by the call's planner), this function's
+// planner kernel writes the plan into `params` (sjk_tc_dense_params_bytes() bytes of device memory) and the kernel
+// reads it there. The grid covers max_items CTAs, the most items a plan of this cache can have.
+int sjk_tc_dense_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                            float * part, const sjk_dyn_state * ds, void * params, int max_items, sjk_stream st) {
+    if (max_items <= 0) return 0;
+    if (max_items > MAX_ITEMS) return SJK_ERR_UNSUPPORTED;
+    DenseParams * dp = static_cast<DenseParams *>(params);
+    dense_dyn_plan_kernel<<<1, 32, 0, st>>>(ds, *v, n_q, n_head, kv0, n_kv, q, scale, part, dp);
+    if (sjk_check_launch()) return SJK_ERR_DEVICE;
+    cudaError_t e = cudaFuncSetAttribute(attend_dense_tc_dyn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    if (e != cudaSuccess) return sjk_check(e);
+    attend_dense_tc_dyn_kernel<<<(unsigned) max_items, NT, SMEM_TOTAL, st>>>(dp);
+    return sjk_check_launch();
 }
 
 // Many sequences of one layer (same layout and formats as *v): sequence s has sink / ring pointers views[s], query
@@ -504,6 +547,7 @@ int sjk_tc_dense_batch_launch(const sjk_view * views, const uint32_t * B, const 
     }
     first[pairs] = (uint16_t) (slot0 + k);
     *n_items = k;
+    p.n_items = k;
     if (k == 0) return 0;
     return dense_launch_params(p, k, st);
 }

@@ -27,6 +27,7 @@
 // issuer drains its own copies and MMAs before the TMEM is released.
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
+#include "sjk_plan.cuh"
 #include "sjk_tc.cuh"
 
 namespace {
@@ -62,6 +63,7 @@ struct TcParams {
     float scale;
     float * part;               // [splits][n_q*n_head][D + 2]
     int split0;                 // partial slot of this kernel's first split
+    int n_splits;               // splits per KV head (the descriptor-driven grid may be wider)
     // staged rows, taken by the same CTAs before their records: the sink [0, min(S, N)) and the staging ring
     // [max(B, S), N) in chunks of 128 positions (sink chunks first); chunk u of a head goes to split u % splits
     const uint8_t * sink;
@@ -156,7 +158,7 @@ __device__ __forceinline__ uint2 codes8(const uint8_t * blk, int j0, const uint3
     return make_uint2(prmt(a, b, 0x5140u) | qh_lut[qh & 0xFFu], prmt(a, b, 0x7362u) | qh_lut[qh >> 8]);
 }
 
-__global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
+SJK_DEV void body_tc_body(const TcParams & p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hl = blockIdx.y, h = p.kv0 + hl, split = blockIdx.x;
@@ -298,7 +300,7 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
             tc::fence_after_sync();
             return got;
         };
-        for (uint32_t u = (uint32_t) split; u < p.n_dense && ok; u += gridDim.x) {
+        for (uint32_t u = (uint32_t) split; u < p.n_dense && ok; u += (uint32_t) p.n_splits) {
             const Chunk ck = chunk_of(u);
             const uint32_t p0 = ck.p0, len = ck.len, side_off = ck.side_off;
             const bool f16 = ck.f16;
@@ -913,6 +915,96 @@ __global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(TcParams p) {
     if (warp == 2 * NW) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
+__global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(const __grid_constant__ TcParams p) { body_tc_body(p); }
+
+// the descriptor-driven form: the plan was made on the device (body_tc_dyn_plan_kernel); the grid covers the most
+// splits a plan can use and the CTAs past the plan's return at once
+__global__ void __launch_bounds__(NT, 1) attend_body_tc_dyn_kernel(const TcParams * __restrict__ pp) {
+    if ((int) blockIdx.x >= pp->n_splits) return;
+    body_tc_body(*pp);
+}
+
+// fp64 steps of the record balancing, rounded as written (the device form must not contract them into fma)
+SJK_HD double d_mul(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dmul_rn(a, b);
+#else
+    return a * b;
+#endif
+}
+SJK_HD double d_add(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dadd_rn(a, b);
+#else
+    return a + b;
+#endif
+}
+SJK_HD double d_div(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __ddiv_rn(a, b);
+#else
+    return a / b;
+#endif
+}
+
+// A staged-row chunk costs about DENSE_WEIGHT sealed records of CTA time; the record ranges are balanced so that
+// the CTAs that also take a chunk get fewer records.
+constexpr double DENSE_WEIGHT = 4.5;
+
+// The plan of one call (records [0, n_rec) of KV heads kv0 .., plus the staged rows of dense_regions). Returns the
+// splits per KV head. Runs on the host (sjk_tc_body_launch) and in the descriptor-driven call's planner kernel.
+SJK_HD int fill_plan(TcParams & p, const sjk_view & v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0,
+                     int n_q, int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0,
+                     bool enabled) {
+    p.lay = v.lay; p.body = v.body; p.blocks = v.blocks; p.H = v.n_head_kv; p.kv0 = kv0; p.S = v.S;
+    p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
+    for (int r = 0; r < NR; ++r) {
+        const int iq = r < p.rows ? r / p.grp : 0, g = r < p.rows ? r % p.grp : 0;
+        p.row_iq[r] = (uint32_t) iq;
+        p.row_q[r] = iq * n_head + g;
+    }
+    p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
+    p.sink = v.sink; p.ring = v.ring; p.staging = v.staging; p.sink_type = v.sink_type; p.cap = v.cap;
+    p.stage_bytes = (uint32_t) v.stage_bytes; p.B = B; p.N = N;
+    p.n_sink_chunks = 0; p.n_dense = 0;
+    if (dense_regions) {
+        const uint32_t s_end = v.S < N ? v.S : N, t0 = B > v.S ? B : v.S;
+        p.n_sink_chunks = (dense_regions & 1) ? (s_end + 127u) / 128u : 0u;
+        p.n_dense = p.n_sink_chunks + ((dense_regions & 2) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
+    }
+    const int splits = enabled ? sjk_tcbody_split_count(n_kv, n_rec, p.n_dense) : 0;
+    p.n_splits = splits;
+    if (splits == 0) return 0;
+    // record ranges: split s takes d(s) chunks (u = s, s + splits, ..) and about target - DENSE_WEIGHT d(s) records
+    double want[MAX_SPLITS], total = 0.0;
+    const double target = d_div(d_add((double) n_rec, d_mul(DENSE_WEIGHT, (double) p.n_dense)), (double) splits);
+    for (int s = 0; s < splits; ++s) {
+        const uint32_t d = p.n_dense > (uint32_t) s ? (p.n_dense - 1u - (uint32_t) s) / (uint32_t) splits + 1u : 0u;
+        const double w = d_add(target, -d_mul(DENSE_WEIGHT, (double) d));
+        want[s] = w > 0.0 ? w : 0.0;
+        total = d_add(total, want[s]);
+    }
+    double run = 0.0;
+    p.rec_bounds[0] = 0;
+    for (int s = 0; s < splits; ++s) {
+        run = d_add(run, want[s]);
+        uint32_t b = total > 0.0 ? (uint32_t) d_add(d_mul(d_div(run, total), (double) n_rec), 0.5) : 0u;
+        if (b > n_rec) b = n_rec;
+        if (b < p.rec_bounds[s]) b = p.rec_bounds[s];
+        p.rec_bounds[s + 1] = b;
+    }
+    p.rec_bounds[splits] = n_rec;
+    return splits;
+}
+
+// planner of the descriptor-driven call: the plan of sjk_tc_body_launch for the counts in *ds
+__global__ void body_tc_dyn_plan_kernel(const sjk_dyn_state * __restrict__ ds, sjk_view v, int n_q, int n_head, int kv0, int n_kv,
+                                        const float * q, float scale, float * part, TcParams * out) {
+    if (threadIdx.x != 0) return;
+    const sjk_dyn_state d = *ds;
+    fill_plan(*out, v, d.B, d.N, d.n_tc, (int) d.dense_regions, d.qpos0, n_q, n_head, kv0, n_kv, q, scale, part, 0, d.ok != 0);
+}
+
 }  // namespace
 
 // ---- host side ---------------------------------------------------------------------------------------------
@@ -931,57 +1023,33 @@ int sjk_tc_body_max_splits(int n_kv) {
     return t < MAX_SPLITS ? t : MAX_SPLITS;
 }
 
-// A staged-row chunk costs about DENSE_WEIGHT sealed records of CTA time; the record ranges are balanced so that
-// the CTAs that also take a chunk get fewer records.
-constexpr double DENSE_WEIGHT = 4.5;
-
 int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                        sjk_stream st) {
     TcParams p;
-    p.lay = v->lay; p.body = v->body; p.blocks = v->blocks; p.H = v->n_head_kv; p.kv0 = kv0; p.S = v->S;
-    p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
-    for (int r = 0; r < NR; ++r) {
-        const int iq = r < p.rows ? r / p.grp : 0, g = r < p.rows ? r % p.grp : 0;
-        p.row_iq[r] = (uint32_t) iq;
-        p.row_q[r] = iq * n_head + g;
-    }
-    p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
-    p.sink = v->sink; p.ring = v->ring; p.staging = v->staging; p.sink_type = v->sink_type; p.cap = v->cap;
-    p.stage_bytes = (uint32_t) v->stage_bytes; p.B = B; p.N = N;
-    p.n_sink_chunks = 0; p.n_dense = 0;
-    if (dense_regions) {
-        const uint32_t s_end = v->S < N ? v->S : N, t0 = B > v->S ? B : v->S;
-        p.n_sink_chunks = (dense_regions & 1) ? (s_end + 127u) / 128u : 0u;
-        p.n_dense = p.n_sink_chunks + ((dense_regions & 2) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
-    }
-    const uint32_t items = n_rec + p.n_dense;
-    int splits = sjk_tc_body_max_splits(n_kv);
-    if ((uint32_t) splits > items) splits = (int) items;
+    const int splits = fill_plan(p, *v, B, N, n_rec, dense_regions, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, true);
     *splits_out = splits;
     if (splits == 0) return 0;
-    // record ranges: split s takes d(s) chunks (u = s, s + splits, ..) and about target - DENSE_WEIGHT d(s) records
-    double want[MAX_SPLITS], total = 0.0;
-    const double target = ((double) n_rec + DENSE_WEIGHT * p.n_dense) / splits;
-    for (int s = 0; s < splits; ++s) {
-        const uint32_t d = p.n_dense > (uint32_t) s ? (p.n_dense - 1u - (uint32_t) s) / (uint32_t) splits + 1u : 0u;
-        const double w = target - DENSE_WEIGHT * d;
-        want[s] = w > 0.0 ? w : 0.0;
-        total += want[s];
-    }
-    double run = 0.0;
-    p.rec_bounds[0] = 0;
-    for (int s = 0; s < splits; ++s) {
-        run += want[s];
-        uint32_t b = total > 0.0 ? (uint32_t) (run / total * n_rec + 0.5) : 0u;
-        if (b > n_rec) b = n_rec;
-        if (b < p.rec_bounds[s]) b = p.rec_bounds[s];
-        p.rec_bounds[s + 1] = b;
-    }
-    p.rec_bounds[splits] = n_rec;
     cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
     attend_body_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
+    return sjk_check_launch();
+}
+
+size_t sjk_tc_body_params_bytes(void) { return sizeof(TcParams); }
+
+// Descriptor-driven form: the counts come from *ds (written on the device by the call's planner), this function's
+// planner kernel writes the plan into `params` (sjk_tc_body_params_bytes() bytes of device memory) and the kernel
+// reads it there. The grid covers the most splits a plan can use.
+int sjk_tc_body_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                           float * part, const sjk_dyn_state * ds, void * params, sjk_stream st) {
+    TcParams * dp = static_cast<TcParams *>(params);
+    body_tc_dyn_plan_kernel<<<1, 32, 0, st>>>(ds, *v, n_q, n_head, kv0, n_kv, q, scale, part, dp);
+    if (sjk_check_launch()) return SJK_ERR_DEVICE;
+    const int max_splits = sjk_tc_body_max_splits(n_kv);
+    cudaError_t e = cudaFuncSetAttribute(attend_body_tc_dyn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    if (e != cudaSuccess) return sjk_check(e);
+    attend_body_tc_dyn_kernel<<<dim3((unsigned) max_splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(dp);
     return sjk_check_launch();
 }
 

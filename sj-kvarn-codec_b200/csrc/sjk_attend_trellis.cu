@@ -31,6 +31,7 @@
 
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
+#include "sjk_plan.cuh"
 #include "sjk_tc.cuh"
 
 namespace {
@@ -263,7 +264,7 @@ __device__ __forceinline__ void prefetch_l2(const void * src, uint32_t bytes) {
 
 // R: query rows per KV head the kernel computes (8 or 16, padded; the MMA N is 2 R)
 template <int BK, int BV, int R>
-__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
+SJK_DEV void trellis_ws_body(const TwParams & p) {
     constexpr int RH = R / 2;                                   // B_K rows per thread (two row halves)
     constexpr int LPR = 32 / R, LPH = 32 / RH;                  // lanes per row after a warp_rows<R> / <RH>
     extern __shared__ __align__(128) uint8_t sm[];
@@ -600,7 +601,27 @@ __global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_c
 }
 
 template <int BK, int BV, int R>
-int launch_kernel(const TwParams & p, sjk_stream st) {
+__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
+    trellis_ws_body<BK, BV, R>(p);
+}
+
+// the descriptor-driven form: the work list was planned on the device (trellis_dyn_plan_kernel); the grid covers
+// the most CTAs a plan can use and the CTAs past the plan's return at once
+template <int BK, int BV, int R>
+__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_dyn_kernel(const TwParams * __restrict__ pp) {
+    if ((int) blockIdx.x >= pp->n_cta) return;
+    trellis_ws_body<BK, BV, R>(*pp);
+}
+
+template <int BK, int BV, int R>
+int launch_kernel(const TwParams & p, const TwParams * dyn, sjk_stream st) {
+    if (dyn) {
+        auto kfn = attend_trellis_ws_dyn_kernel<BK, BV, R>;
+        const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+        if (e != cudaSuccess) return sjk_check(e);
+        kfn<<<(unsigned) p.n_cta, NT, SMEM_TOTAL, st>>>(dyn);
+        return sjk_check_launch();
+    }
     auto kfn = attend_trellis_ws_kernel<BK, BV, R>;
     const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
@@ -608,17 +629,20 @@ int launch_kernel(const TwParams & p, sjk_stream st) {
     return sjk_check_launch();
 }
 
+// p: the plan (host launches) or only its layout, rows and grid size (dyn: the plan in device memory)
 template <int R>
-int launch_rows(const TwParams & p, sjk_stream st) {
+int launch_rows(const TwParams & p, const TwParams * dyn, sjk_stream st) {
     const int bk = p.lay.bits_k, bv = p.lay.bits_v;
-    if (bk == 3) return bv == 3 ? launch_kernel<3, 3, R>(p, st) : launch_kernel<3, 2, R>(p, st);
-    return bv == 3 ? launch_kernel<2, 3, R>(p, st) : launch_kernel<2, 2, R>(p, st);
+    if (bk == 3) return bv == 3 ? launch_kernel<3, 3, R>(p, dyn, st) : launch_kernel<3, 2, R>(p, dyn, st);
+    return bv == 3 ? launch_kernel<2, 3, R>(p, dyn, st) : launch_kernel<2, 2, R>(p, dyn, st);
 }
 
 // the 8-row kernel for up to 8 query rows per KV head (decode width 1 or 2 at GQA 4), else the 16-row one
-int launch(const TwParams & p, sjk_stream st) { return p.rows <= 8 ? launch_rows<8>(p, st) : launch_rows<16>(p, st); }
+int launch(const TwParams & p, sjk_stream st, const TwParams * dyn = nullptr) {
+    return p.rows <= 8 ? launch_rows<8>(p, dyn, st) : launch_rows<16>(p, dyn, st);
+}
 
-void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
+SJK_HD void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
     p.grp = n_head / n_kv;
     p.rows = n_q * p.grp;
     p.n_rows = n_q * n_head;
@@ -627,6 +651,38 @@ void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
         p.row_iq[r] = (uint32_t) iq;
         p.row_q[r] = iq * n_head + g;
     }
+}
+
+// One sequence: records [0, n_rec) of KV heads kv0 .. kv0 + n_kv - 1, each head split into `splits` contiguous ranges;
+// item (head, split) is CTA hl * splits + split and writes partial slot split0 + split. Runs on the host (sjk_attend)
+// and in the planner kernel of the descriptor-driven call.
+SJK_HD void fill_single(TwParams & p, const sjk_view & v, uint32_t b_end, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head,
+                        int kv0, int n_kv, const float * q, float scale, float * part, int split0, int splits) {
+    p.lay = v.lay; p.n_head_kv = v.n_head_kv; p.scale = scale; p.part = part;
+    fill_rows(p, n_q, n_head, n_kv);
+    p.seq[0].body = v.body; p.seq[0].blocks = v.blocks; p.seq[0].q = q; p.seq[0].S = v.S;
+    p.seq[0].b_end = b_end; p.seq[0].qpos0 = qpos0; p.seq[0].pad = 0;
+    int k = 0;
+    for (int hl = 0; hl < n_kv; ++hl)
+        for (int s = 0; s < splits; ++s, ++k) {
+            TwItem & it = p.item[k];
+            it.seq_hl = (uint32_t) hl << 16;
+            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
+            it.r0 = (uint32_t) (((uint64_t) n_rec * (uint32_t) s) / (uint32_t) splits);
+            it.r1 = (uint32_t) (((uint64_t) n_rec * (uint32_t) (s + 1)) / (uint32_t) splits);
+            p.cta_item[k] = (uint16_t) k;
+        }
+    p.cta_item[k] = (uint16_t) k;
+    p.n_cta = k;
+}
+
+// planner of the descriptor-driven call: the plan of sjk_tc_trellis_launch for the counts in *ds
+__global__ void trellis_dyn_plan_kernel(const sjk_dyn_state * __restrict__ ds, sjk_view v, int n_q, int n_head, int kv0, int n_kv,
+                                        const float * q, float scale, float * part, TwParams * out) {
+    if (threadIdx.x != 0) return;
+    const sjk_dyn_state d = *ds;
+    const uint32_t b_end = d.B < d.N ? d.B : d.N;
+    fill_single(*out, v, b_end, d.n_tc, d.qpos0, n_q, n_head, kv0, n_kv, q, scale, part, 0, d.ok ? d.splits_tc : 0);
 }
 
 }  // namespace
@@ -649,35 +705,38 @@ int sjk_tc_trellis_max_splits(int n_kv) {
     return t < MAX_CTAS ? t : MAX_CTAS;
 }
 
+size_t sjk_tc_trellis_params_bytes(void) { return sizeof(TwParams); }
+
 // One sequence: records [0, n_rec) of KV heads kv0 .. kv0 + n_kv - 1, each head split into `splits` contiguous
 // ranges; item (head, split) is CTA hl * splits + split and writes partial slot split0 + split.
 int sjk_tc_trellis_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head,
                           int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
                           sjk_stream st) {
-    int splits = sjk_tc_trellis_max_splits(n_kv);
-    if ((uint32_t) splits > n_rec) splits = (int) n_rec;
-    while (splits * n_kv > MAX_CTAS) --splits;
+    const int splits = sjk_trellis_split_count(n_kv, n_rec);
     *splits_out = splits;
     if (splits <= 0) return 0;
     if (split0 + splits > 0xFFFF) return SJK_ERR_UNSUPPORTED;
     static thread_local TwParams p;
-    p.lay = v->lay; p.n_head_kv = v->n_head_kv; p.scale = scale; p.part = part;
-    fill_rows(p, n_q, n_head, n_kv);
-    p.seq[0].body = v->body; p.seq[0].blocks = v->blocks; p.seq[0].q = q; p.seq[0].S = v->S;
-    p.seq[0].b_end = B < N ? B : N; p.seq[0].qpos0 = qpos0; p.seq[0].pad = 0;
-    int k = 0;
-    for (int hl = 0; hl < n_kv; ++hl)
-        for (int s = 0; s < splits; ++s, ++k) {
-            TwItem & it = p.item[k];
-            it.seq_hl = (uint32_t) hl << 16;
-            it.h_slot = (uint32_t) (kv0 + hl) | ((uint32_t) (split0 + s) << 16);
-            it.r0 = (uint32_t) (((uint64_t) n_rec * (uint32_t) s) / (uint32_t) splits);
-            it.r1 = (uint32_t) (((uint64_t) n_rec * (uint32_t) (s + 1)) / (uint32_t) splits);
-            p.cta_item[k] = (uint16_t) k;
-        }
-    p.cta_item[k] = (uint16_t) k;
-    p.n_cta = k;
+    fill_single(p, *v, B < N ? B : N, n_rec, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, splits);
     return launch(p, st);
+}
+
+// Descriptor-driven form: the counts come from *ds (written on the device by the call's planner), this function's
+// planner kernel writes the plan into `params` (sjk_tc_trellis_params_bytes() bytes of device memory) and the kernel
+// reads it from there. The launch covers the most CTAs a plan can use.
+int sjk_tc_trellis_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                              float * part, const sjk_dyn_state * ds, void * params, sjk_stream st) {
+    TwParams * dp = static_cast<TwParams *>(params);
+    trellis_dyn_plan_kernel<<<1, 32, 0, st>>>(ds, *v, n_q, n_head, kv0, n_kv, q, scale, part, dp);
+    if (sjk_check_launch()) return SJK_ERR_DEVICE;
+    static thread_local TwParams shape;        // only the layout, the rows and the grid size are read
+    shape.lay = v->lay;
+    fill_rows(shape, n_q, n_head, n_kv);
+    int max_splits = sjk_tc_trellis_max_splits(n_kv);
+    while (max_splits * n_kv > MAX_CTAS) --max_splits;
+    shape.n_cta = max_splits * n_kv;
+    if (shape.n_cta <= 0) return 0;
+    return launch(shape, st, dp);
 }
 
 // Many sequences of one layer (same layout as views[0]): sequence s attends with query rows q + s n_q n_head D over its

@@ -52,3 +52,20 @@ int sjk_tc_trellis_status_take(void);
 // zeroes them. Groups with no block are skipped (op 0 writes zeros for them). One launch (sjk_decode.cu).
 int sjk_group_move(uint8_t * body, const uint32_t * blocks, uint32_t g0, uint32_t n, size_t group_bytes, uint8_t * buf, int op,
                    sjk_stream st);
+
+// ---- descriptor-driven attention (sjk_attend_dyn): the counts are planned on the device into a sjk_dyn_state
+// (sjk_plan.cuh); each kernel family's planner kernel writes its launch plan into `params` (device memory of the
+// family's *_params_bytes()) and its kernel reads it there
+struct sjk_dyn_state;
+size_t sjk_tc_body_params_bytes(void);
+size_t sjk_tc_trellis_params_bytes(void);
+size_t sjk_tc_dense_params_bytes(void);
+int sjk_tc_body_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                           float * part, const sjk_dyn_state * ds, void * params, sjk_stream st);
+int sjk_tc_trellis_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                              float * part, const sjk_dyn_state * ds, void * params, sjk_stream st);
+int sjk_tc_dense_dyn_launch(const sjk_view * v, int n_q, int n_head, int kv0, int n_kv, const float * q, float scale,
+                            float * part, const sjk_dyn_state * ds, void * params, int max_items, sjk_stream st);
+// descriptor faults of the seal and store kernels (SJK_DEVICE_DESC; read and cleared)
+int sjk_seal_desc_status_take(void);
+int sjk_stage_desc_status_take(void);

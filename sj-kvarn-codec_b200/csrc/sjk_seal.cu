@@ -16,6 +16,7 @@
 // strict-< ascending-branch Viterbi from state 0 (1021-1053), sequential double sums in column order for
 // the refit (1078-1109). Only the order of independent work differs.
 #include "sjk_common.cuh"
+#include "sjk_desc.cuh"
 
 namespace {
 
@@ -40,6 +41,10 @@ struct SealParams {
     const uint32_t * blocks;
     // output
     uint8_t * body;
+    // descriptor-driven ring seal (sjk_seal_dyn): B_from and the group count come from desc when the kernel runs
+    const int32_t * desc;
+    sjk_desc_ref dref;
+    uint32_t n_groups_max;
 };
 
 // Shared-memory carve for one side. All offsets are multiples of 16 bytes.
@@ -445,6 +450,17 @@ SJK_DEV void seal_side(const SealParams & p, uint8_t * smem) {
 template <int D>
 __global__ void __launch_bounds__(NT, 1) seal_kernel(SealParams p) {
     extern __shared__ __align__(16) uint8_t smem[];
+    if (p.desc) {
+        // groups [(B_OLD - S) / G, (B - S) / G) of the descriptor; the launch covers n_groups_max of them
+        sjk_desc_vals dv;
+        const bool ok = sjk_desc_read(p.desc, p.dref, &dv) && (dv.B - dv.B_old) / (uint32_t) G <= p.n_groups_max;
+        if (!ok) {
+            if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) sjk_desc_fault();
+            return;
+        }
+        if ((uint32_t) blockIdx.x >= (dv.B - dv.B_old) / (uint32_t) G * (uint32_t) p.H) return;
+        p.B_from = dv.B_old;
+    }
     if (blockIdx.y == 0) seal_side<D, false>(p, smem);
     else seal_side<D, true>(p, smem);
 }
@@ -495,3 +511,20 @@ extern "C" int sjk_seal_ring(const sjk_view * v, uint8_t * body, uint32_t B_from
     p.stage_bytes = (uint32_t) v->stage_bytes; p.blocks = v->blocks; p.body = body;
     return seal_dispatch(p, (int) (ng * (uint32_t) v->n_head_kv), st);
 }
+
+// Descriptor-driven ring seal (the reference's seal_dyn op, INTEGRATION_LLAMACPP.md:49): a fixed launch over
+// n_groups_max groups x n_head_kv heads whose CTAs read [B_OLD, B) from the descriptor; CTAs past the descriptor's
+// groups return at once.
+extern "C" int sjk_seal_dyn(const sjk_view * v, const int32_t * desc, uint32_t n_groups_max, int iters, sjk_stream st) {
+    if (!v || !desc || !v->body || !v->ring || iters < 0 || v->n_head_kv <= 0) return SJKVARN_ERR_ARG;
+    if (n_groups_max == 0) return 0;
+    if ((uint64_t) n_groups_max * (uint32_t) v->n_head_kv > 0x7FFFFFFFu) return SJKVARN_ERR_ARG;
+    SealParams p = {};
+    p.lay = v->lay; p.H = v->n_head_kv; p.iters = iters;
+    p.source = SRC_RING; p.staging = v->staging; p.ring = v->ring; p.S = v->S; p.cap = v->cap; p.B_from = v->S;
+    p.stage_bytes = (uint32_t) v->stage_bytes; p.blocks = v->blocks; p.body = const_cast<uint8_t *>(v->body);
+    p.desc = desc; p.dref = sjk_desc_ref_of(*v); p.n_groups_max = n_groups_max;
+    return seal_dispatch(p, (int) (n_groups_max * (uint32_t) v->n_head_kv), st);
+}
+
+SJK_DESC_STATUS_READER(sjk_seal_desc_status_take)

@@ -10,6 +10,7 @@
 // blocks of a whole position are assembled in shared memory and leave in 16-byte stores, because a
 // position's slot ([H][K row | V row], 1568 B at D=256, H=4) is contiguous and 16-byte aligned.
 #include "sjk_common.cuh"
+#include "sjk_desc.cuh"
 
 namespace {
 
@@ -27,6 +28,8 @@ struct StoreParams {
     int rotate;
     float fwht_scale;   // 1/sqrt(D), computed on the host with the reference's operations
     uint32_t stage_bytes;
+    const int32_t * desc;   // sjk_store_dyn: pos0 is the descriptor's QPOS0, read when the kernel runs
+    sjk_desc_ref dref;
 };
 
 template <int VPL>
@@ -184,7 +187,16 @@ __global__ void __launch_bounds__(256) store_batch_kernel(const __grid_constant_
 
 template <int D>
 __global__ void __launch_bounds__(256) store_kernel(StoreParams p) {
-    store_position<D>(p, p.pos0 + blockIdx.x, p.sink, p.ring, blockIdx.x);
+    uint32_t pos0 = p.pos0;
+    if (p.desc) {
+        sjk_desc_vals dv;
+        if (!sjk_desc_read(p.desc, p.dref, &dv)) {
+            if (blockIdx.x == 0 && threadIdx.x == 0) sjk_desc_fault();
+            return;
+        }
+        pos0 = dv.qpos0;
+    }
+    store_position<D>(p, pos0 + blockIdx.x, p.sink, p.ring, blockIdx.x);
 }
 
 // Position pos of one cache; its rows are row0 .. of k and v ([*][H][D]).
@@ -371,11 +383,13 @@ extern "C" int sjk_store_batch(const sjk_view * views, const uint32_t * pos, int
     return 0;
 }
 
-extern "C" int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos,
-                         const float * k, const float * vv, int rotate, sjk_stream st) {
+namespace {
+int store_launch(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos, const float * k,
+                 const float * vv, int rotate, const int32_t * desc, sjk_stream st) {
     if (!v || !k || !vv || !sink || !ring || v->n_head_kv <= 0 || v->cap == 0) return SJKVARN_ERR_ARG;
     if (n_pos == 0) return 0;
     StoreParams p;
+    p.desc = desc; p.dref = sjk_desc_ref_of(*v);
     p.k = k; p.v = vv; p.sink = sink; p.ring = ring; p.pos0 = pos0; p.S = v->S; p.cap = v->cap; p.H = v->n_head_kv;
     p.staging = v->staging; p.sink_f16 = v->sink_type == SJKVARN_SINK_F16; p.rotate = rotate;
     p.fwht_scale = host_fwht_scale(v->lay.D); p.stage_bytes = (uint32_t) v->stage_bytes;
@@ -390,3 +404,19 @@ extern "C" int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uin
     }
     return sjk_check_launch();
 }
+}  // namespace
+
+extern "C" int sjk_store(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t pos0, uint32_t n_pos,
+                         const float * k, const float * vv, int rotate, sjk_stream st) {
+    return store_launch(v, sink, ring, pos0, n_pos, k, vv, rotate, nullptr, st);
+}
+
+// Descriptor-driven store (the reference's staged set_rows, INTEGRATION_LLAMACPP.md:48): positions QPOS0 ..
+// QPOS0 + n_pos - 1 of the descriptor, read when the kernel runs.
+extern "C" int sjk_store_dyn(const sjk_view * v, const int32_t * desc, uint32_t n_pos, const float * k, const float * vv,
+                             int rotate, sjk_stream st) {
+    if (!v || !desc) return SJKVARN_ERR_ARG;
+    return store_launch(v, const_cast<uint8_t *>(v->sink), const_cast<uint8_t *>(v->ring), 0, n_pos, k, vv, rotate, desc, st);
+}
+
+SJK_DESC_STATUS_READER(sjk_stage_desc_status_take)

@@ -143,6 +143,11 @@ SIGNATURES = {
     "sjk_attend_batch_scratch_bytes": (C.c_size_t, [P(View), C.c_int, C.c_int, C.c_int]),
     "sjk_attend_batch": (C.c_int, [P(View), P(u32), P(u32), P(u32), C.c_int, C.c_int, C.c_int, vp, C.c_float, vp, vp,
                                    C.c_size_t, vp]),
+    "sjk_desc_fill": (C.c_int, [P(View), u32, u32, u32, u32, P(C.c_int32)]),
+    "sjk_seal_dyn": (C.c_int, [P(View), vp, u32, C.c_int, vp]),
+    "sjk_store_dyn": (C.c_int, [P(View), vp, u32, vp, vp, C.c_int, vp]),
+    "sjk_attend_dyn_scratch_bytes": (C.c_size_t, [P(View), C.c_int, C.c_int]),
+    "sjk_attend_dyn": (C.c_int, [P(View), vp, C.c_int, C.c_int, vp, C.c_float, vp, vp, C.c_size_t, vp]),
     "sjk_layer_store": (C.c_int, [P(Layer), u32, u32, vp, vp, C.c_int, vp]),
     "sjk_layer_seal": (C.c_int, [P(Layer), u32, u32, vp]),
     "sjk_layer_attend": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
@@ -200,6 +205,21 @@ def config(head_dim=256, n_head_kv=4, n_ctx=16384, n_ubatch=512, **kw):
     for k, v in kw.items():
         setattr(c, k, v)
     return c
+
+
+# descriptor entries of the descriptor-driven calls (include/sjk.h, the reference's ggml_sjkvarn_desc order)
+(DESC_S, DESC_CAP, DESC_B, DESC_N, DESC_QPOS0, DESC_G, DESC_D, DESC_RECBYTES, DESC_HKV, DESC_B_OLD, DESC_TYPE_K,
+ DESC_TYPE_V, DESC_BODY_TYPE, DESC_SINK_TYPE) = range(14)
+DESC_N_ENTRIES = 16
+DEVICE_TIMEOUT, DEVICE_DESC = 1, 2
+
+
+def desc_fill(view, B_old, B, N, qpos0):
+    """Host descriptor (numpy int32[16]) for view; raises SjkError when the kernels would reject the values."""
+    import numpy as np
+    d = np.zeros(DESC_N_ENTRIES, np.int32)
+    check(lib().sjk_desc_fill(C.byref(view), B_old, B, N, qpos0, d.ctypes.data_as(C.POINTER(C.c_int32))), "desc_fill")
+    return d
 
 
 # region mask of sjk_attend_partial (include/sjk.h)

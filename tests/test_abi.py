@@ -146,3 +146,25 @@ def test_state_peek_rejects_damage_without_gpu(L, oracle_lib):
     assert L.sj_kvarn_state_peek(st.tobytes(), len(st) - 1, C.byref(info)) == -103
     assert L.sj_kvarn_state_peek(st.tobytes(), 4, C.byref(info)) == -103
     s.close()
+
+
+def test_desc_fill_entries_and_checks(L):
+    """The descriptor of the descriptor-driven calls: the reference's entry order (INTEGRATION_LLAMACPP.md:54-69),
+    values from the view, and the same checks the kernels apply (host-only, no GPU)."""
+    v = sjk.View()
+    v.lay = sjk.layout(256, 3, 3, 1)
+    v.n_head_kv, v.staging, v.sink_type, v.S, v.cap, v.stage_bytes = 4, 0, 0, 128, 1152, 196
+    d = sjk.desc_fill(v, 128 + 256, 128 + 512, 900, 899)
+    assert list(d) == [128, 1152, 640, 900, 899, 128, 256, v.lay.bytes, 4, 384, 0, 0, 1, 0, 0, 0]
+    assert sjk.DESC_B_OLD == 9 and sjk.DESC_SINK_TYPE == 13 and sjk.DESC_N_ENTRIES == 16
+    # sink-only, empty ubatch seal
+    assert list(sjk.desc_fill(v, 128, 128, 50, 49))[:5] == [128, 1152, 128, 50, 49]
+    bad = [(128, 128 + 100, 900, 0),       # B off a group boundary
+           (128 + 256, 128, 900, 0),       # B_OLD > B
+           (100, 128, 900, 0),             # B_OLD inside the sink
+           (128, 64, 100, 0),              # B inside the sink
+           (128, 256, 256 + 1153, 0),      # more staged positions than the ring holds
+           (128, 256, 2 ** 31, 0)]         # not an int32
+    for args in bad:
+        with pytest.raises(sjk.SjkError):
+            sjk.desc_fill(v, *args)
