@@ -11,18 +11,21 @@
 // holds the Viterbi back-pointers and `part`'s space the trellis payload.
 //
 // Bit-exactness: every rounding follows the reference's order - the 8-chunk double reduction with the
-// fixed pairwise combine and an fma second pass (sj_kvarn.h:939-978), two IEEE divides per rescaled
-// element (980-987), the clamp/compare forms of 679-682 and 1000-1008, ties-to-even rint (1014-1019),
+// fixed pairwise combine and an fma second pass (sj_kvarn.h:939-978), two correctly rounded divides per
+// rescaled element (980-987; each from the scale's reciprocal and one residual correction, which yields
+// the IEEE quotient), the clamp/compare forms of 679-682 and 1000-1008, ties-to-even rint (1014-1019),
 // strict-< ascending-branch Viterbi from state 0 (1021-1053), sequential double sums in column order for
 // the refit (1078-1109). Only the order of independent work differs.
+#include <cuda_fp16.h>
+
 #include "sjk_common.cuh"
 #include "sjk_desc.cuh"
 
 namespace {
 
 constexpr int G = 128;
-constexpr int NT = 512;                 // threads per CTA
-constexpr int NW = NT / 32;
+constexpr int NT = 1024;                // threads per CTA (64 registers each: the whole register file)
+constexpr int VNW = 16;                 // warps running the Viterbi (its per-warp tables fill M's and part's space)
 constexpr unsigned FULL = 0xFFFFFFFFu;
 
 enum SealSource { SRC_F16_ROWS = 0, SRC_RING = 1 };
@@ -86,11 +89,12 @@ SJK_DEV double tree8(const double * p, int stride) {
                      __dadd_rn(__dadd_rn(p[4 * stride], p[5 * stride]), __dadd_rn(p[6 * stride], p[7 * stride])));
 }
 
-// ---- phase 0: the seal input -> M (fp16 bits) -------------------------------------------------------------
+// ---- phase 0: the seal input -> M (fp16 bits); returns whether this thread stored an Inf or NaN ------------
 template <int D, bool IS_V>
-SJK_DEV void load_input(const SealParams & p, int rec_local, uint16_t * M, const float * cent) {
+SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const float * cent) {
     using CV = Carve<D, IS_V>;
     const int g = rec_local / p.H, h = rec_local % p.H;
+    bool nonfinite = false;
     for (int e = threadIdx.x; e < G * D; e += NT) {
         const int t = e / D, d = e % D;                               // token-major walk: coalesced reads
         uint16_t hv;
@@ -113,23 +117,49 @@ SJK_DEV void load_input(const SealParams & p, int rec_local, uint16_t * M, const
         }
         const int r = IS_V ? t : d, c = IS_V ? d : t;
         M[r * CV::C + c] = hv;
+        nonfinite |= (hv & 0x7C00u) == 0x7C00u;
     }
+    return nonfinite;
 }
 
-// cur = (M / s_col) / s_row, two IEEE divides per element (sj_kvarn.h:980-987)
+// RN(a / b) given y = RN(1 / b). q = RN(a y) lies within one ulp of a / b, so the residual b q - a is exact in one
+// fma, and one correction step RN(q - (b q - a) y) is the correctly rounded quotient (Markstein's theorem; the
+// residual is formed as b q - a so that a = -0 keeps its sign). It holds while the quotient and the residual stay
+// in the normal range, which the balancing guarantees for finite inputs: a is 0 or at least 2^-24 / s in magnitude
+// with every scale s = exp(clamp(., -0.3, 10)) in [0.74, 22027], so every quotient is 0 or between 1e-16 and 1.2e5.
+SJK_DEV float div_by_rcp(float a, float b, float y) {
+    const float q = __fmul_rn(a, y);
+    const float t = __fmaf_rn(q, b, -a);
+    return __fmaf_rn(t, -y, q);
+}
+
+// cur = (M / s_col) / s_row, two IEEE divides per element (sj_kvarn.h:980-987). Finite inputs divide through
+// rrow / rcol = RN(1 / s) of every scale (div_by_rcp); a tile holding an Inf or NaN uses the IEEE divides
+// themselves. A thread keeps one column (C divides the CTA size), so its column scale stays in registers.
 template <int D, bool IS_V>
-SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const float * scol) {
+SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const float * scol, const float * rrow,
+                     const float * rcol, bool finite) {
     using CV = Carve<D, IS_V>;
-    for (int e = threadIdx.x; e < CV::R * CV::C; e += NT) {
-        const int r = e / CV::C, c = e % CV::C;
-        cur[r * CV::LD + c] = __fdiv_rn(__fdiv_rn(sjk_h2f(M[e]), scol[c]), srow[r]);
+    constexpr int R = CV::R, C = CV::C, RSTEP = NT / C;
+    static_assert(NT % C == 0, "a thread keeps one column");
+    const int c = threadIdx.x % C;
+    if (finite) {
+        const float sc = scol[c], rc = rcol[c];
+#pragma unroll 4
+        for (int r = threadIdx.x / C; r < R; r += RSTEP) {
+            const float m = __half2float(__ushort_as_half(M[r * C + c]));
+            cur[r * CV::LD + c] = div_by_rcp(div_by_rcp(m, sc, rc), srow[r], rrow[r]);
+        }
+    } else {
+        for (int r = threadIdx.x / C; r < R; r += RSTEP)
+            cur[r * CV::LD + c] = __fdiv_rn(__fdiv_rn(sjk_h2f(M[r * C + c]), scol[c]), srow[r]);
     }
 }
 
 // One balancing half-step over columns (COLS = true: std of each column over the R rows) or rows.
 // Chunked double sums (8 contiguous chunks), fixed pairwise combine, fma second pass (sj_kvarn.h:939-978).
 template <int D, bool IS_V, bool COLS>
-SJK_DEV void balance_half(const float * cur, double * part, double * mean, double * lacc, float * sacc) {
+SJK_DEV void balance_half(const float * cur, double * part, double * mean, double * lacc, float * sacc, float * racc) {
     using CV = Carve<D, IS_V>;
     constexpr int N = COLS ? CV::C : CV::R;        // number of vectors
     constexpr int L = COLS ? CV::R : CV::C;        // length of each vector
@@ -167,7 +197,9 @@ SJK_DEV void balance_half(const float * cur, double * part, double * mean, doubl
         const float sd = lesser_f(greater_f(sdv, 1e-3f), 1e3f);
         const double lg = lesser_d(greater_d(__dadd_rn(lacc[v], log((double) sd)), -0.3), 10.0);
         lacc[v] = lg;
-        sacc[v] = (float) exp(lg);
+        const float sv = (float) exp(lg);
+        sacc[v] = sv;
+        racc[v] = __frcp_rn(sv);
     }
     __syncthreads();
 }
@@ -234,6 +266,7 @@ SJK_DEV void viterbi_side(const float * cur, const float * lo, const float * ste
     constexpr int NB = 1 << BITS;
     constexpr int NA = 64 / NB;                 // distinct history groups
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp >= VNW) return;
     uint8_t * bp = bp_all + warp * (G * 32);
     float * mt = mt_all + warp * 64;
     const int s0 = 2 * lane, s1 = 2 * lane + 1;
@@ -243,7 +276,7 @@ SJK_DEV void viterbi_side(const float * cur, const float * lo, const float * ste
     float cA[NB], cB[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) { cA[j] = sjk_h2f(cb16[s0 + 64 * j]); cB[j] = sjk_h2f(cb16[s1 + 64 * j]); }
-    for (int d = warp; d < D; d += NW) {
+    for (int d = warp; d < D; d += VNW) {
         // targets y[t] = (bal - lo) / step of this channel, lane holds t = lane + 32 k
         float y[4];
 #pragma unroll
@@ -365,21 +398,21 @@ SJK_DEV void seal_side(const SealParams & p, uint8_t * smem) {
     uint8_t * rec = p.body + ((size_t) blk * p.H + h) * l.bytes;
 
     if (threadIdx.x < 64) cent[threadIdx.x] = sjk_tq6_cent[threadIdx.x];
-    for (int c = threadIdx.x; c < C; c += NT) { scol[c] = 1.0f; lcol[c] = 0.0; }
-    for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; lrow[r] = 0.0; }
+    float * rrow = lo, * rcol = step;                            // reciprocals of the scales while balancing
+    for (int c = threadIdx.x; c < C; c += NT) { scol[c] = 1.0f; rcol[c] = 1.0f; lcol[c] = 0.0; }
+    for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; rrow[r] = 1.0f; lrow[r] = 0.0; }
     __syncthreads();
-    load_input<D, IS_V>(p, rec_local, M, cent);
-    __syncthreads();
-    rescale<D, IS_V>(cur, M, srow, scol);
+    const bool finite = !__syncthreads_or(load_input<D, IS_V>(p, rec_local, M, cent));
+    rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
     __syncthreads();
 
     // ---- log-domain variance balancing, exactly `iters` column-then-row passes (sj_kvarn.h:989-1012) ----
     for (int it = 0; it < p.iters; ++it) {
-        balance_half<D, IS_V, true>(cur, part, mean, lcol, scol);
-        rescale<D, IS_V>(cur, M, srow, scol);
+        balance_half<D, IS_V, true>(cur, part, mean, lcol, scol, rcol);
+        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
         __syncthreads();
-        balance_half<D, IS_V, false>(cur, part, mean, lrow, srow);
-        rescale<D, IS_V>(cur, M, srow, scol);
+        balance_half<D, IS_V, false>(cur, part, mean, lrow, srow, rrow);
+        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
         __syncthreads();
     }
 

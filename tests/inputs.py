@@ -101,3 +101,33 @@ def seq_row(seed, variant, pos, n, side):
     g = (h & np.uint64(1023)).astype(np.int64) + ((h >> np.uint64(10)) & np.uint64(1023)).astype(np.int64) - 1024
     scale = np.where((i % np.uint64(41)) == 0, 24, 1 + ((h >> np.uint64(20)) & np.uint64(3)).astype(np.int64))
     return (g * scale).astype(np.float32) * np.float32(1.0 / 4096.0)
+
+
+def edge_tiles(D, G=128, seed=7):
+    """Seal inputs (K, V as fp16 bits [G][D]) at the edges of the balancing arithmetic: signed zeros, fp16
+    subnormals, values near the fp16 maximum, constant and all-zero rows and columns. Every value is finite
+    (the reference's quantiser casts rint() of the balanced value to an integer, so an Inf or NaN input has no
+    platform-independent result)."""
+    rng = np.random.default_rng(seed)
+    sub = np.array([1, 2, 3, 0x1FF, 0x3FF], np.uint16)             # fp16 subnormal encodings
+    out = []
+    # 1: zeros of both signs with a few subnormals and normals
+    k = np.where(rng.random((G, D)) < 0.5, 0x8000, 0x0000).astype(np.uint16)
+    m = rng.random((G, D)) < 0.1
+    k[m] = rng.choice(sub, m.sum()) | np.where(rng.random(m.sum()) < 0.5, 0x8000, 0).astype(np.uint16)
+    v = _f16(rng.standard_normal((G, D)))
+    v[:, 3] = 0x8000                                                  # a column of -0
+    v[5] = 0                                                          # a row of +0
+    out.append(("zeros+subnormals", k, v))
+    # 2: a wide dynamic range: values near 65504 next to subnormals
+    x = rng.standard_normal((G, D)) * np.exp(rng.uniform(-16, 10, (G, D)))
+    k = _f16(np.clip(x, -65504, 65504))
+    k[0, 0], k[1, 1], k[2, 2] = 0x7BFF, 0xFBFF, 0x0001
+    v = _f16(np.clip(rng.standard_normal((G, D)) * 3e4, -65504, 65504))
+    out.append(("wide range", k, v))
+    # 3: constant rows and columns (zero standard deviation: the 1e-3 clamp) and an all-zero tile
+    k = np.tile(_f16(rng.standard_normal(D)), (G, 1))
+    v = np.tile(_f16(rng.standard_normal((G, 1))), (1, D))
+    out.append(("constant rows / columns", k, v))
+    out.append(("all zero", np.zeros((G, D), np.uint16), np.full((G, D), 0x8000, np.uint16)))
+    return out

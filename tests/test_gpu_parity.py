@@ -70,6 +70,19 @@ def test_seal_and_decode_golden(L, oracle_lib, D, bk, bv, body, nbytes, erec, ed
     assert oracle_lib.fnv(np.stack([k, v], axis=1)) == edec
 
 
+@pytest.mark.parametrize("bk,bv,body", [(4, 4, 0), (3, 2, 1), (3, 3, 1), (2, 2, 1), (4, 2, 0)])
+def test_seal_edge_values(L, oracle_lib, bk, bv, body):
+    """Seal records bit-exact with the oracle on edge tiles: signed zeros, fp16 subnormals, values near the fp16
+    maximum, constant rows and columns, an all-zero tile (the balancing's divides, clamps and degenerate refits)."""
+    lay = sjk.layout(256, bk, bv, body)
+    ol = oracle_lib.layout(256, bk, bv, body == 1)
+    rec = gu.dev_zeros(lay.bytes)
+    for name, k, v in inputs.edge_tiles(256):
+        dk, dv = gu.dev(k), gu.dev(v)
+        sjk.check(L.sjk_seal(C.byref(lay), gu.ptr(dk), gu.ptr(dv), 256, 1, 1, 16, gu.ptr(rec), None, None), "seal")
+        assert np.array_equal(gu.host(rec), oracle_lib.seal(ol, k, v)), name
+
+
 def test_tq6_golden(L, oracle_lib):
     for ln in open(os.path.join(GOLDEN, "expected_vectors.txt")):
         m = re.match(r"tq6 rows=(\d+) n=(\d+) enc=([0-9a-f]+) dec=([0-9a-f]+)", ln)

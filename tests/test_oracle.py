@@ -125,3 +125,30 @@ def test_window_and_layout_offsets(oracle_lib):
     assert o.layout(256, 3, 3, 1).bytes == 26880
     assert o.layout(256, 3, 2, 1).bytes == 22784
     assert o.layout(256, 2, 2, 1).bytes == 18688
+
+
+EDGE_BODIES = [(4, 4, 0), (3, 2, 1), (3, 3, 1), (2, 2, 1), (4, 2, 0)]
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref", "libsjref.so")),
+                    reason="reference not compiled here")
+@pytest.mark.parametrize("bk,bv,body", EDGE_BODIES)
+def test_oracle_seal_edges_match_compiled_reference(oracle_lib, bk, bv, body):
+    """Oracle seal == the compiled reference's sj_kvarn_seal_group on edge tiles (signed zeros, fp16 subnormals,
+    values near the fp16 maximum, constant and all-zero tiles): pins the oracle where no golden vector reaches."""
+    import ctypes as C
+    import inputs
+    import oracle
+    import sjk
+    r = oracle.ref()
+    lay = sjk.Layout()
+    assert r.sj_kvarn_layout_init(C.byref(lay), 256, 128, bk, bv, body) == 0
+    r.sjref_seal_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_int]
+    ol = oracle_lib.layout(256, bk, bv, body == 1)
+    assert ol.bytes == lay.bytes
+    for name, k, v in inputs.edge_tiles(256):
+        want = np.zeros(lay.bytes, np.uint8)
+        r.sjref_seal_batch(C.byref(lay), k.ctypes.data, v.ctypes.data, 256, 1, 1, 16, want.ctypes.data, 1)
+        got = oracle_lib.seal(ol, k, v)
+        assert np.array_equal(got, want), name
