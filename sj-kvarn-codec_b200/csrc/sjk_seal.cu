@@ -134,11 +134,12 @@ SJK_DEV float div_by_rcp(float a, float b, float y) {
 }
 
 // cur = (M / s_col) / s_row, two IEEE divides per element (sj_kvarn.h:980-987). Finite inputs divide through
-// rrow / rcol = RN(1 / s) of every scale (div_by_rcp); a tile holding an Inf or NaN uses the IEEE divides
-// themselves. A thread keeps one column (C divides the CTA size), so its column scale stays in registers.
+// rrow / rcol = RN(1 / s) of every scale (div_by_rcp; the row pairs also sit interleaved in sr2); a tile holding
+// an Inf or NaN uses the IEEE divides themselves. A thread keeps one column (C divides the CTA size), so its
+// column scale stays in registers.
 template <int D, bool IS_V>
 SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const float * scol, const float * rrow,
-                     const float * rcol, bool finite) {
+                     const float * rcol, const float2 * sr2, bool finite) {
     using CV = Carve<D, IS_V>;
     constexpr int R = CV::R, C = CV::C, RSTEP = NT / C;
     static_assert(NT % C == 0, "a thread keeps one column");
@@ -148,7 +149,8 @@ SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const 
 #pragma unroll 4
         for (int r = threadIdx.x / C; r < R; r += RSTEP) {
             const float m = __half2float(__ushort_as_half(M[r * C + c]));
-            cur[r * CV::LD + c] = div_by_rcp(div_by_rcp(m, sc, rc), srow[r], rrow[r]);
+            const float2 rs = sr2[r];                                 // (s_row, 1 / s_row): one broadcast load
+            cur[r * CV::LD + c] = div_by_rcp(div_by_rcp(m, sc, rc), rs.x, rs.y);
         }
     } else {
         for (int r = threadIdx.x / C; r < R; r += RSTEP)
@@ -159,7 +161,8 @@ SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const 
 // One balancing half-step over columns (COLS = true: std of each column over the R rows) or rows.
 // Chunked double sums (8 contiguous chunks), fixed pairwise combine, fma second pass (sj_kvarn.h:939-978).
 template <int D, bool IS_V, bool COLS>
-SJK_DEV void balance_half(const float * cur, double * part, double * mean, double * lacc, float * sacc, float * racc) {
+SJK_DEV void balance_half(const float * cur, double * part, double * mean, double * lacc, float * sacc, float * racc,
+                          float2 * sr2) {
     using CV = Carve<D, IS_V>;
     constexpr int N = COLS ? CV::C : CV::R;        // number of vectors
     constexpr int L = COLS ? CV::R : CV::C;        // length of each vector
@@ -198,8 +201,10 @@ SJK_DEV void balance_half(const float * cur, double * part, double * mean, doubl
         const double lg = lesser_d(greater_d(__dadd_rn(lacc[v], log((double) sd)), -0.3), 10.0);
         lacc[v] = lg;
         const float sv = (float) exp(lg);
+        const float rv = __frcp_rn(sv);
         sacc[v] = sv;
-        racc[v] = __frcp_rn(sv);
+        racc[v] = rv;
+        if (!COLS) sr2[v] = make_float2(sv, rv);
     }
     __syncthreads();
 }
@@ -399,20 +404,21 @@ SJK_DEV void seal_side(const SealParams & p, uint8_t * smem) {
 
     if (threadIdx.x < 64) cent[threadIdx.x] = sjk_tq6_cent[threadIdx.x];
     float * rrow = lo, * rcol = step;                            // reciprocals of the scales while balancing
+    float2 * sr2 = reinterpret_cast<float2 *>(fit);              // (srow, rrow) pairs while balancing
     for (int c = threadIdx.x; c < C; c += NT) { scol[c] = 1.0f; rcol[c] = 1.0f; lcol[c] = 0.0; }
-    for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; rrow[r] = 1.0f; lrow[r] = 0.0; }
+    for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; rrow[r] = 1.0f; sr2[r] = make_float2(1.0f, 1.0f); lrow[r] = 0.0; }
     __syncthreads();
     const bool finite = !__syncthreads_or(load_input<D, IS_V>(p, rec_local, M, cent));
-    rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
+    rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
     __syncthreads();
 
     // ---- log-domain variance balancing, exactly `iters` column-then-row passes (sj_kvarn.h:989-1012) ----
     for (int it = 0; it < p.iters; ++it) {
-        balance_half<D, IS_V, true>(cur, part, mean, lcol, scol, rcol);
-        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
+        balance_half<D, IS_V, true>(cur, part, mean, lcol, scol, rcol, sr2);
+        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
         __syncthreads();
-        balance_half<D, IS_V, false>(cur, part, mean, lrow, srow, rrow);
-        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, finite);
+        balance_half<D, IS_V, false>(cur, part, mean, lrow, srow, rrow, sr2);
+        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
         __syncthreads();
     }
 
