@@ -166,6 +166,10 @@ SJK_DEV void copy_out(uint8_t * dst, const uint8_t * src, uint32_t n, int tid, i
 // Batched cache write (sjk_store_batch): one position per item, each in its own cache (sink and ring of one layer of
 // one sequence); the rows of item i are k, v + i H D.
 constexpr int STORE_BATCH_MAX = 1024;
+// The store is latency-bound (two sequential 128-value norm sums per tq6_0 block): six resident CTAs per SM
+// (40 registers a thread) hide more of it than three at the unconstrained 72 registers (8,320 positions:
+// 76 against 107 us).
+constexpr int STORE_MIN_CTAS = 6;
 struct StoreBatchParams {
     StoreParams c;                          // shared fields (k, v, formats, S, cap, H); sink / ring / pos0 per item
     uint8_t * sink[STORE_BATCH_MAX];
@@ -175,18 +179,18 @@ struct StoreBatchParams {
 
 // One CTA per position: its 2H rows (head-major, K then V) are rotated, staged and written.
 template <int D>
-__global__ void __launch_bounds__(256) store_kernel(StoreParams p);
+__global__ void __launch_bounds__(256, STORE_MIN_CTAS) store_kernel(StoreParams p);
 template <int D>
 __device__ __forceinline__ void store_position(const StoreParams & p, uint32_t pos, uint8_t * sink, uint8_t * ring,
                                                size_t row0);
 
 template <int D>
-__global__ void __launch_bounds__(256) store_batch_kernel(const __grid_constant__ StoreBatchParams b) {
+__global__ void __launch_bounds__(256, STORE_MIN_CTAS) store_batch_kernel(const __grid_constant__ StoreBatchParams b) {
     store_position<D>(b.c, b.pos[blockIdx.x], b.sink[blockIdx.x], b.ring[blockIdx.x], blockIdx.x);
 }
 
 template <int D>
-__global__ void __launch_bounds__(256) store_kernel(StoreParams p) {
+__global__ void __launch_bounds__(256, STORE_MIN_CTAS) store_kernel(StoreParams p) {
     uint32_t pos0 = p.pos0;
     if (p.desc) {
         sjk_desc_vals dv;
