@@ -91,7 +91,7 @@ SJK_DEV double tree8(const double * p, int stride) {
 
 // ---- phase 0: the seal input -> M (fp16 bits); returns whether this thread stored an Inf or NaN ------------
 template <int D, bool IS_V>
-SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const float * cent) {
+SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const float * cent, const size_t * rowoff) {
     using CV = Carve<D, IS_V>;
     const int g = rec_local / p.H, h = rec_local % p.H;
     bool nonfinite = false;
@@ -102,9 +102,7 @@ SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const
             const uint16_t * src = (IS_V ? p.v : p.k) + ((size_t) g * G + t) * p.row_stride + (size_t) h * D;
             hv = src[d];
         } else {
-            const uint32_t pos = p.B_from + (uint32_t) (g * G + t);
-            const uint8_t * row = p.ring + ((size_t) sjk_ring_slot(p.S, p.cap, pos) * p.H + h) * 2 * p.stage_bytes +
-                                  (IS_V ? p.stage_bytes : 0);
+            const uint8_t * row = p.ring + rowoff[t];
             if (p.staging == SJKVARN_STAGING_F16) {
                 hv = sjk_ld_u16(row + 2 * d);
                 hv = sjk_f2h(sjk_h2f(hv));                              // widen + round back, as the reference
@@ -112,7 +110,11 @@ SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const
                 const uint8_t * b = row + (d >> 7) * SJKVARN_TQ6_BLOCK_BYTES;
                 const int j = d & 127;
                 const int code = ((b[2 + (j >> 1)] >> (4 * (j & 1))) & 15) | (((b[66 + (j >> 2)] >> (2 * (j & 3))) & 3) << 4);
-                hv = sjk_f2h(__fmul_rn(cent[code], sjk_h2f(sjk_ld_u16(b))));
+                // hardware conversions (exact, and round-to-nearest-even like the reference's) except for Inf / NaN
+                const uint16_t nb = sjk_ld_u16(b);
+                const float nf = (nb & 0x7C00u) == 0x7C00u ? sjk_h2f(nb) : __half2float(__ushort_as_half(nb));
+                const float xv = __fmul_rn(cent[code], nf);
+                hv = xv != xv ? sjk_f2h(xv) : __half_as_ushort(__float2half_rn(xv));
             }
         }
         const int r = IS_V ? t : d, c = IS_V ? d : t;
@@ -403,12 +405,18 @@ SJK_DEV void seal_side(const SealParams & p, uint8_t * smem) {
     uint8_t * rec = p.body + ((size_t) blk * p.H + h) * l.bytes;
 
     if (threadIdx.x < 64) cent[threadIdx.x] = sjk_tq6_cent[threadIdx.x];
+    // byte offset of each token's K or V row in the ring, one ring-slot division per token (only during the load)
+    size_t * rowoff = reinterpret_cast<size_t *>(smem + CV::regB + 256);
+    if (p.source == SRC_RING && threadIdx.x < G) {
+        const uint32_t pos = p.B_from + (uint32_t) (g_local * G + threadIdx.x);
+        rowoff[threadIdx.x] = ((size_t) sjk_ring_slot(p.S, p.cap, pos) * p.H + h) * 2 * p.stage_bytes + (IS_V ? p.stage_bytes : 0);
+    }
     float * rrow = lo, * rcol = step;                            // reciprocals of the scales while balancing
     float2 * sr2 = reinterpret_cast<float2 *>(fit);              // (srow, rrow) pairs while balancing
     for (int c = threadIdx.x; c < C; c += NT) { scol[c] = 1.0f; rcol[c] = 1.0f; lcol[c] = 0.0; }
     for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; rrow[r] = 1.0f; sr2[r] = make_float2(1.0f, 1.0f); lrow[r] = 0.0; }
     __syncthreads();
-    const bool finite = !__syncthreads_or(load_input<D, IS_V>(p, rec_local, M, cent));
+    const bool finite = !__syncthreads_or(load_input<D, IS_V>(p, rec_local, M, cent, rowoff));
     rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
     __syncthreads();
 
