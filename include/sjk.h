@@ -111,6 +111,12 @@ size_t sj_kvarn_stage_row_bytes(int staging, int D);
 void   sj_kvarn_stage_row(int staging, const float * x_rot, void * dst, int D);
 void   sj_kvarn_unstage_row(int staging, const void * src, float * x_rot, int D);
 
+/* ---- reference attention helpers (rotated basis; sj_kvarn.h:218-222, 1288-1311); DEVICE pointers ---- */
+/* scores[t] = dot(q, K[t]) for the first n tokens of a record: each a sequential fp32 sum over the channels */
+void   sj_kvarn_record_scores(const sj_kvarn_layout * l, const uint8_t * rec, const float * q, int n, float * scores);
+/* acc[d] += sum_t w[t] * V[t, d] for the first n tokens of a record, added in token order */
+void   sj_kvarn_record_accum_v(const sj_kvarn_layout * l, const uint8_t * rec, const float * w, int n, float * acc);
+
 /* ---- adaptive tail / journal policy (host; sj_kvarn.h:224-274) ---- */
 typedef struct sj_kvarn_policy {
     uint32_t sink, tail, tail_max, group, flush_chunk;
@@ -433,6 +439,27 @@ int sjk_seq_store(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_pos, const float *
                   int rotate, sjk_stream st);
 /* copy record (g, h) to host memory (synchronous) */
 int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * host_dst);
+
+/* ---- seeded synthetic inputs of the benchmark configurations (DEVICE outputs) ----
+ * Input generation for benchmarks and parity tests; no counterpart in the reference. K = X * s with X ~ N(0, 1)
+ * (Student-t(4) when heavy) and s ~ LogNormal(0, 1) channel scales with 4 outlier channels x 8 per (layer, head);
+ * V ~ N(0, 1); Q ~ N(0, 1) rounded to fp16. SplitMix64 draws and Box-Muller normals computed with correctly rounded
+ * double operations only, so a host build of the same arithmetic (csrc/sjk_synth.h) produces identical bits; every
+ * value is a function of (seed, layer, position, head, channel), so any position range can be generated alone. */
+/* scale: DEVICE [n_layers][H][D] channel scales of layers layer0 .. layer0 + n_layers - 1 */
+int sjk_synth_scales(uint64_t seed, int layer0, int n_layers, int H, int D, float * scale, sjk_stream st);
+/* k, v: DEVICE [n][H][D] model-basis rows of positions pos0 .. pos0 + n - 1 of one layer; scale: DEVICE [H][D] of that
+ * layer (sjk_synth_scales); H * D even, k and v 8-byte aligned */
+int sjk_synth_kv(uint64_t seed, int layer, int H, int D, int heavy, const float * scale, uint32_t pos0, uint32_t n,
+                 float * k, float * v, sjk_stream st);
+/* q: DEVICE [n_rows][D] query rows of one layer (row = query row * n_head + query head), fp16-rounded floats */
+int sjk_synth_q(uint64_t seed, int layer, uint32_t n_rows, int D, float * q, sjk_stream st);
+
+/* Self-check of the seal's math library: lg[i] = log(x[i]) and ex[i] = exp(x[i]) with the device's double log and
+ * exp, the two calls the balancing makes per scale update (sj_kvarn.h:1001-1008). Record bytes equal the
+ * reference's only where these equal the host libm's results on the arguments the balancing reaches. x, lg, ex:
+ * DEVICE arrays of n doubles. No counterpart in the reference. */
+int sjk_seal_libm_probe(const double * x, size_t n, double * lg, double * ex, sjk_stream st);
 
 #ifdef __cplusplus
 }

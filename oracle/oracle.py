@@ -32,10 +32,19 @@ class Cache(C.Structure):
                 ("sink", C.c_void_p), ("ring", C.c_void_p), ("body", C.c_void_p), ("blocks", C.c_void_p)]
 
 
+def reference_dir():
+    """The reference checkout: SJK_REF_DIR, else a `reference` directory beside this repository (None if absent)."""
+    for d in (os.environ.get("SJK_REF_DIR"), os.path.join(HERE, "..", "..", "reference")):
+        if d and os.path.isfile(os.path.join(d, "sj_kvarn.h")):
+            return os.path.abspath(d)
+    return None
+
+
 def build():
     """Compile liboracle.so (and _ref/libsjref.so when the reference sources exist)."""
     import subprocess
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref_dir = reference_dir()
+    subprocess.run(["make", "-s", "-C", HERE] + ([f"SJK_REF_DIR={ref_dir}"] if ref_dir else []), check=True)
 
 
 _lib = None
@@ -82,6 +91,9 @@ def lib():
                                      [C.c_uint32] * 3 + [C.c_void_p]
         L.ora_state_write.restype = C.c_size_t
         L.ora_fnv.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]; L.ora_fnv.restype = C.c_uint64
+        L.ora_trace_balance.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+        L.ora_trace_counts.argtypes = [C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+        L.ora_libm_log_exp.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
         _lib = L
     return _lib
 

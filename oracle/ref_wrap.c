@@ -189,3 +189,19 @@ void sjref_layer_seal_mt(sj_kvarn_layer * L, uint32_t B_from, uint32_t B_to, int
 }
 
 int sjref_nthreads(int n) { return ref_threads(n); }
+
+/* ---- buffers of a reference layer, for byte comparisons with the device caches ---- */
+const uint8_t * sjref_layer_ring(const sj_kvarn_layer * L, size_t * bytes) {
+    *bytes = (size_t) L->cap * (size_t) L->cfg.n_head_kv * 2 * L->stage_bytes;
+    return L->ring;
+}
+
+const uint8_t * sjref_layer_sink(const sj_kvarn_layer * L, size_t * bytes) {
+    const size_t per = L->cfg.sink_type == SJKVARN_SINK_F16 ? (size_t) L->cfg.head_dim * 4 : 2 * L->stage_bytes;
+    *bytes = (size_t) L->cfg.sink * (size_t) L->cfg.n_head_kv * per;
+    return L->sink;
+}
+
+uint32_t sjref_layer_cap(const sj_kvarn_layer * L) { return L->cap; }
+uint32_t sjref_layer_record_bytes(const sj_kvarn_layer * L) { return L->lay.bytes; }
+const sj_kvarn_layout * sjref_layer_layout(const sj_kvarn_layer * L) { return &L->lay; }

@@ -277,6 +277,44 @@ static void rescale(const float * M, int R, int C, const float * srow, const flo
         for (c = 0; c < C; ++c) cur[(size_t) r * C + c] = (M[(size_t) r * C + c] / scol[c]) / srow[r];
 }
 
+/* Optional trace of every argument the balancing passes to log() and exp() (for the check of the device's double
+ * log/exp against this host's libm): slots are claimed atomically, so tracing works under the threaded seals. */
+static double * g_trace_log, * g_trace_exp;
+static size_t g_trace_cap, g_trace_n_log, g_trace_n_exp;
+
+void ora_trace_balance(double * log_args, double * exp_args, size_t cap) {
+    g_trace_log = log_args; g_trace_exp = exp_args; g_trace_cap = cap;
+    __atomic_store_n(&g_trace_n_log, 0, __ATOMIC_SEQ_CST);
+    __atomic_store_n(&g_trace_n_exp, 0, __ATOMIC_SEQ_CST);
+}
+
+void ora_trace_counts(size_t * n_log, size_t * n_exp) {
+    *n_log = __atomic_load_n(&g_trace_n_log, __ATOMIC_SEQ_CST);
+    *n_exp = __atomic_load_n(&g_trace_n_exp, __ATOMIC_SEQ_CST);
+}
+
+static double traced_log(double x) {
+    if (g_trace_log) {
+        const size_t i = __atomic_fetch_add(&g_trace_n_log, 1, __ATOMIC_RELAXED);
+        if (i < g_trace_cap) g_trace_log[i] = x;
+    }
+    return log(x);
+}
+
+static double traced_exp(double x) {
+    if (g_trace_exp) {
+        const size_t i = __atomic_fetch_add(&g_trace_n_exp, 1, __ATOMIC_RELAXED);
+        if (i < g_trace_cap) g_trace_exp[i] = x;
+    }
+    return exp(x);
+}
+
+/* this host's libm log and exp of n doubles (the functions the reference's balancing calls) */
+void ora_libm_log_exp(const double * x, size_t n, double * lg, double * ex) {
+    size_t i;
+    for (i = 0; i < n; ++i) { lg[i] = log(x[i]); ex[i] = exp(x[i]); }
+}
+
 /* log-domain variance balancing, exactly `iters` column-then-row passes (sj_kvarn.h:989-1012) */
 static void balance(const float * M, int R, int C, int iters, float * srow, float * scol, float * cur,
                     double * lrow, double * lcol) {
@@ -287,14 +325,14 @@ static void balance(const float * M, int R, int C, int iters, float * srow, floa
     for (it = 0; it < iters; ++it) {
         for (c = 0; c < C; ++c) {
             const float sd = lesser_f(greater_f(chunked_std(cur + c, R, (size_t) C), 1e-3f), 1e3f);
-            lcol[c] = lesser_d(greater_d(lcol[c] + log((double) sd), -0.3), 10.0);
-            scol[c] = (float) exp(lcol[c]);
+            lcol[c] = lesser_d(greater_d(lcol[c] + traced_log((double) sd), -0.3), 10.0);
+            scol[c] = (float) traced_exp(lcol[c]);
         }
         rescale(M, R, C, srow, scol, cur);
         for (r = 0; r < R; ++r) {
             const float sd = lesser_f(greater_f(chunked_std(cur + (size_t) r * C, C, 1), 1e-3f), 1e3f);
-            lrow[r] = lesser_d(greater_d(lrow[r] + log((double) sd), -0.3), 10.0);
-            srow[r] = (float) exp(lrow[r]);
+            lrow[r] = lesser_d(greater_d(lrow[r] + traced_log((double) sd), -0.3), 10.0);
+            srow[r] = (float) traced_exp(lrow[r]);
         }
         rescale(M, R, C, srow, scol, cur);
     }

@@ -159,6 +159,41 @@ __global__ void kv_row_kernel(sjk_view v, uint32_t B, uint32_t pos, int h, float
 
 }  // namespace
 
+namespace {
+// The reference's attention helpers on one record (sj_kvarn.h:1288-1311), with its arithmetic order: each score is
+// the sequential fp32 sum over channels of q[d] * K[t, d] (one rounding per multiply and per add; one thread per
+// token), and each output channel adds w[t] * V[t, d] in token order (one thread per channel).
+__global__ void record_scores_kernel(sj_kvarn_layout l, const uint8_t * rec, const float * q, int n, float * scores) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    float s = 0.0f;
+    for (int d = 0; d < l.D; ++d) s = __fadd_rn(s, __fmul_rn(q[d], decode_value(l, rec, t, d, 0)));
+    scores[t] = s;
+}
+
+__global__ void record_accum_v_kernel(sj_kvarn_layout l, const uint8_t * rec, const float * w, int n, float * acc) {
+    const int d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= l.D) return;
+    float a = acc[d];
+    for (int t = 0; t < n; ++t) a = __fadd_rn(a, __fmul_rn(w[t], decode_value(l, rec, t, d, 1)));
+    acc[d] = a;
+}
+}  // namespace
+
+int sjk_record_scores(const sj_kvarn_layout * lay, const uint8_t * rec, const float * q, int n, float * scores, sjk_stream st) {
+    if (!lay || !rec || !q || !scores || n < 0 || n > lay->G) return SJKVARN_ERR_ARG;
+    if (n == 0) return 0;
+    record_scores_kernel<<<(n + 127) / 128, 128, 0, st>>>(*lay, rec, q, n, scores);
+    return sjk_check_launch();
+}
+
+int sjk_record_accum_v(const sj_kvarn_layout * lay, const uint8_t * rec, const float * w, int n, float * acc, sjk_stream st) {
+    if (!lay || !rec || !w || !acc || n < 0 || n > lay->G) return SJKVARN_ERR_ARG;
+    if (n == 0) return 0;
+    record_accum_v_kernel<<<(lay->D + 127) / 128, 128, 0, st>>>(*lay, rec, w, n, acc);
+    return sjk_check_launch();
+}
+
 int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st) {
     if (!lay || !rec || !out || t < 0 || t >= lay->G) return SJKVARN_ERR_ARG;
     decode_row_kernel<<<1, 256, 0, st>>>(*lay, rec, t, is_v, out);

@@ -270,6 +270,12 @@ extern "C" void sj_kvarn_decode_k_row(const sj_kvarn_layout * l, const uint8_t *
 extern "C" void sj_kvarn_decode_v_row(const sj_kvarn_layout * l, const uint8_t * rec, int t, float * out) {
     sticky(sjk_decode_row(l, rec, t, 1, out, 0));
 }
+extern "C" void sj_kvarn_record_scores(const sj_kvarn_layout * l, const uint8_t * rec, const float * q, int n, float * scores) {
+    sticky(sjk_record_scores(l, rec, q, n, scores, 0));
+}
+extern "C" void sj_kvarn_record_accum_v(const sj_kvarn_layout * l, const uint8_t * rec, const float * w, int n, float * acc) {
+    sticky(sjk_record_accum_v(l, rec, w, n, acc, 0));
+}
 extern "C" void sj_kvarn_tq6_quantize_row(const float * x, sj_kvarn_tq6_block * y, int n) {
     sticky(sjk_stage_rows(SJKVARN_STAGING_TQ6_0, x, (uint8_t *) y, (size_t) n / 128 * SJKVARN_TQ6_BLOCK_BYTES, n, 1, 0));
 }

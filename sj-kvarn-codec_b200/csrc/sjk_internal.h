@@ -18,6 +18,9 @@ size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, i
 int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, float * vo, sjk_stream st);
 // decode row t of one record (is_v selects V) to out[D] (device)
 int sjk_decode_row(const sj_kvarn_layout * lay, const uint8_t * rec, int t, int is_v, float * out, sjk_stream st);
+// the reference's record attention helpers on device pointers (sjk_decode.cu)
+int sjk_record_scores(const sj_kvarn_layout * lay, const uint8_t * rec, const float * q, int n, float * scores, sjk_stream st);
+int sjk_record_accum_v(const sj_kvarn_layout * lay, const uint8_t * rec, const float * w, int n, float * acc, sjk_stream st);
 
 // tensor-core attention over the sealed body of a 4-bit scalar layer (sjk_attend_tc.cu); dense_regions: the same
 // CTAs also take the staged rows (bit 0 the sink, bit 1 the staging ring; formats of sjk_tc_dense_supported). *splits_out gets the

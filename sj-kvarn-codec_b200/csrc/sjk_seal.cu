@@ -575,3 +575,22 @@ extern "C" int sjk_seal_dyn(const sjk_view * v, const int32_t * desc, uint32_t n
 }
 
 SJK_DESC_STATUS_READER(sjk_seal_desc_status_take)
+
+namespace {
+// the double log and exp of the balancing (the calls of seal_kernel's scale updates), on a list of arguments
+__global__ void libm_probe_kernel(const double * x, size_t n, double * lg, double * ex) {
+    for (size_t i = (size_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const double a = x[i];
+        lg[i] = log(a);
+        ex[i] = exp(a);
+    }
+}
+}  // namespace
+
+extern "C" int sjk_seal_libm_probe(const double * x, size_t n, double * lg, double * ex, sjk_stream st) {
+    if (n == 0) return 0;
+    if (!x || !lg || !ex) return SJKVARN_ERR_ARG;
+    const size_t blocks = (n + 255) / 256;
+    libm_probe_kernel<<<(unsigned) (blocks < 4096 ? blocks : 4096), 256, 0, st>>>(x, n, lg, ex);
+    return sjk_check_launch();
+}

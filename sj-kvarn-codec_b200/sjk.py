@@ -77,6 +77,8 @@ SIGNATURES = {
     "sj_kvarn_seal_group": (None, [P(Layout), vp, vp, C.c_size_t, C.c_int, vp, vp]),
     "sj_kvarn_decode_k_row": (None, [P(Layout), vp, C.c_int, vp]),
     "sj_kvarn_decode_v_row": (None, [P(Layout), vp, C.c_int, vp]),
+    "sj_kvarn_record_scores": (None, [P(Layout), vp, vp, C.c_int, vp]),
+    "sj_kvarn_record_accum_v": (None, [P(Layout), vp, vp, C.c_int, vp]),
     "sj_kvarn_tq6_quantize_row": (None, [vp, vp, C.c_int]),
     "sj_kvarn_tq6_dequantize_row": (None, [vp, vp, C.c_int]),
     "sj_kvarn_stage_row": (None, [C.c_int, vp, vp, C.c_int]),
@@ -153,6 +155,11 @@ SIGNATURES = {
     "sjk_layer_attend": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sjk_layer_view": (None, [P(Layer), P(View)]),
     "sjk_layer_record_copy": (C.c_int, [P(Layer), u32, C.c_int, vp]),
+    # seeded synthetic inputs
+    "sjk_synth_scales": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]),
+    "sjk_synth_kv": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, u32, u32, vp, vp, vp]),
+    "sjk_synth_q": (C.c_int, [C.c_uint64, C.c_int, u32, C.c_int, vp, vp]),
+    "sjk_seal_libm_probe": (C.c_int, [vp, C.c_size_t, vp, vp, vp]),
 }
 
 _lib = None

@@ -1,6 +1,7 @@
-"""Regenerates the golden fixtures in this folder from the reference checkout
-(SJK_REF_DIR, default /root/reference). Run in a container that has the reference;
-the fixtures are committed so the GPU box never needs the reference at run time.
+"""Regenerates the golden fixtures in this folder from a checkout of the reference
+(JakeATX/sj-kvarn-codec): the directory named by SJK_REF_DIR, else a `reference` checkout
+beside this repository. The fixtures are committed, so running the tests never needs the
+reference.
 
   expected_vectors.txt  the reference's 21 FNV-1a 64 hashes of seal records, decoded
                         rows and tq6_0 staging bytes (its tests/expected_vectors.txt)
@@ -11,7 +12,7 @@ import os
 import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SJK_REF_DIR", "/root/reference")
+REF = os.environ.get("SJK_REF_DIR") or os.path.join(HERE, "..", "..", "..", "reference")
 
 
 def copy_hashes(name, pattern):

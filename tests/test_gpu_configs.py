@@ -1,0 +1,335 @@
+"""Parity at the benchmark configurations' own shapes and seeds: each cache is built twice from the same seeded rows,
+on the GPU through the product API (sj-kvarn-codec_b200/configs.py: the device generator, sjk_layer_store with the
+rotation inside, sjk_layer_seal / the bulk seal) and on the host through the reference compiled from its own source
+(oracle/_ref: sj_kvarn_hadamard, sj_kvarn_layer_store, sj_kvarn_layer_seal or the threaded harness over the same
+public per-record calls, sj_kvarn_layer_attend_row), then compared.
+
+Bit-exact: sink, staging ring and record bytes, decoded rows, kv rows; the seeded rows themselves (device generator
+against the host generator). Attention: max relative L2 error per (row, head) <= 1e-3 against
+sj_kvarn_layer_attend_row (the contract); the measured error is printed and also held to 1e-4.
+Also: the device's double log / exp against this host's libm on every argument the balancing reaches in configs 0
+and 2 (record bytes can only match where these agree)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import configs
+import gpu_util as gu
+import oracle
+import refcache
+import sjk
+
+pytestmark = pytest.mark.gpu
+
+D, H, HQ = configs.D, configs.H, configs.HQ
+ATTN_TOL = 1e-3           # north-star contract (fp32 accumulate)
+ATTN_TOL_TIGHT = 1e-4     # internal bound
+
+
+@pytest.fixture(scope="module")
+def L():
+    import build
+    build.build()
+    import torch
+    assert torch.cuda.is_available()
+    return sjk.lib()
+
+
+@pytest.fixture(scope="module")
+def R():
+    assert refcache.available(), "oracle/_ref/libsjref.so (the compiled reference) is needed for configuration parity"
+    return refcache.ref()
+
+
+def _sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+def _body(layer, n_groups):
+    return gu.d2h_ptr(layer.body, n_groups * H * layer.lay.bytes)
+
+
+def _ring(layer):
+    return gu.d2h_ptr(layer.ring, layer.cap * H * 2 * layer.stage_bytes)
+
+
+def _sink(layer):
+    return gu.d2h_ptr(layer.sink, configs.SINK * H * D * 4)
+
+
+def _ref_grow(rl, seed, heavy, scale, frm, to, n_ub=512, threaded=True):
+    """The engine loop on the reference: begin_ubatch (seal what is due, commit), then store the ubatch's rows."""
+    pos = frm
+    while pos < to:
+        n = min(n_ub, to - pos)
+        rl.begin_ubatch(pos, n, threaded)
+        k, v = refcache.synth_kv(seed, 0, H, D, heavy, scale, pos, n, lib=rl.R)
+        rl.store(pos, k, v)
+        pos += n
+
+
+def _rotated_queries(L, syn, n_q):
+    q = syn.queries(0, n_q)
+    sjk.check(L.sjk_hadamard(gu.ptr(q), n_q * HQ, D, None), "hadamard")
+    return q
+
+
+def _attend_dev(L, layer, B, N, q, n_q):
+    out = gu.torch().empty_like(q)
+    sjk.check(L.sjk_layer_attend(C.byref(layer), B, N, N - n_q, n_q, HQ, gu.ptr(q), configs.SCALE, gu.ptr(out), None),
+              "attend")
+    return gu.host(out, np.float32).reshape(n_q, HQ, D)
+
+
+def _attn_err(rl, B, N, q_host_rot, out, pairs):
+    ref = rl.attend_pairs(B, N, N - out.shape[0], q_host_rot, pairs, configs.SCALE)
+    got = np.stack([out[p] for p in pairs])
+    want = np.stack([ref[p] for p in pairs])
+    return gu.rel_err_rows(got, want)
+
+
+def test_device_generator_matches_host(L, R):
+    """The device generator draws the same fp32 bits as the host build of the same arithmetic (and so as the rows the
+    reference is fed), at small and large positions, for both K distributions, and for the queries."""
+    T = gu.torch()
+    sc = T.empty((2, H, D), dtype=T.float32, device="cuda")
+    sjk.check(L.sjk_synth_scales(2, 3, 2, H, D, gu.ptr(sc), None))
+    want = refcache.synth_scales(2, 3, 2, H, D, lib=R)
+    assert np.array_equal(gu.host(sc, np.uint32), want.view(np.uint32).ravel())
+    for seed, layer, heavy, pos0, n in ((0, 0, False, 0, 300), (2, 1, True, 1_000_000, 77), (4, 15, False, 8191 * 128, 256),
+                                        (1, 7, False, 99_999, 1)):
+        dsc = T.empty((1, H, D), dtype=T.float32, device="cuda")
+        sjk.check(L.sjk_synth_scales(seed, layer, 1, H, D, gu.ptr(dsc), None))
+        k = T.empty((n, H, D), dtype=T.float32, device="cuda")
+        v = T.empty_like(k)
+        sjk.check(L.sjk_synth_kv(seed, layer, H, D, int(heavy), gu.ptr(dsc), pos0, n, gu.ptr(k), gu.ptr(v), None))
+        hsc = refcache.synth_scales(seed, layer, 1, H, D, lib=R)[0]
+        hk, hv = refcache.synth_kv(seed, layer, H, D, heavy, hsc, pos0, n, lib=R)
+        assert np.array_equal(gu.host(k, np.uint32), hk.view(np.uint32).ravel()), (seed, layer, pos0)
+        assert np.array_equal(gu.host(v, np.uint32), hv.view(np.uint32).ravel()), (seed, layer, pos0)
+    q = T.empty((4, HQ, D), dtype=T.float32, device="cuda")
+    sjk.check(L.sjk_synth_q(1, 5, 4 * HQ, D, gu.ptr(q), None))
+    assert np.array_equal(gu.host(q, np.uint32), refcache.synth_q(1, 5, 4, HQ, D, lib=R).view(np.uint32).ravel())
+
+
+def test_config0_bytes(L, R):
+    """Config 0 (H 4, D 256, 4/4, tail 4096 -> 8192, ubatch 512, seed 0): 8,320 positions through the policy, then the
+    4096-token commit. Sink, ring, all 128 records (against the reference's own sj_kvarn_layer_seal), every decoded
+    row of them and kv rows across the regions are bit-exact."""
+    c = configs.CFG0
+    m, B0, B1 = configs.build_config0()
+    lay = m.layers[0]
+    sjk.check(L.sjk_layer_seal(C.byref(lay), B0, B1, None), "seal")
+    L.sj_kvarn_policy_commit(C.byref(m.pol))
+    _sync()
+    rl = refcache.RefLayer(D, H, c["n_ctx"], c["n_ub"], tail=c["tail"], tail_max=c["tail_max"])
+    scale = refcache.synth_scales(c["seed"], 0, 1, H, D, lib=R)[0]
+    _ref_grow(rl, c["seed"], False, scale, 0, c["npos"])
+    rl.begin_ubatch(c["npos"], c["n_ub"], threaded=False)          # the reference's own layer_seal
+    assert (rl.pol.B, m.pol.B) == (B1, B1)
+    assert np.array_equal(_sink(lay), rl.sink_bytes()), "sink bytes"
+    assert np.array_equal(_ring(lay), rl.ring_bytes()), "ring bytes"
+    ng = (B1 - B0) // 128
+    body = _body(lay, ng)
+    assert np.array_equal(body, rl.records(0, ng)), "record bytes"
+    T = gu.torch()
+    ok = T.empty((ng * H, 128, D), dtype=T.float32, device="cuda")
+    ov = T.empty_like(ok)
+    sjk.check(L.sjk_decode(C.byref(lay.lay), C.c_void_p(lay.body), ng * H, gu.ptr(ok), gu.ptr(ov), None), "decode")
+    k_all, v_all = gu.host(ok, np.float32).reshape(ng, H, 128, D), gu.host(ov, np.float32).reshape(ng, H, 128, D)
+    for g in range(ng):
+        for h in range(H):
+            rk, rv = rl.decode(g, h)
+            assert np.array_equal(k_all[g, h].view(np.uint32), rk.view(np.uint32)), (g, h)
+            assert np.array_equal(v_all[g, h].view(np.uint32), rv.view(np.uint32)), (g, h)
+    dk, dv = T.empty(D, dtype=T.float32, device="cuda"), T.empty(D, dtype=T.float32, device="cuda")
+    R.sj_kvarn_layer_kv_row.argtypes = [C.c_void_p, C.c_uint32, C.c_uint32, C.c_int, C.c_void_p, C.c_void_p]
+    for pos in (0, 127, 128, 129, 2000, 4223, 4224, 6000, 8319):
+        for h in range(H):
+            L.sj_kvarn_layer_kv_row(C.byref(lay), B1, pos, h, gu.ptr(dk), gu.ptr(dv))
+            rk, rv = np.zeros(D, np.float32), np.zeros(D, np.float32)
+            R.sj_kvarn_layer_kv_row(rl.L, B1, pos, h, rk.ctypes.data, rv.ctypes.data)
+            assert np.array_equal(gu.host(dk, np.uint32), rk.view(np.uint32)), (pos, h)
+            assert np.array_equal(gu.host(dv, np.uint32), rv.view(np.uint32)), (pos, h)
+    rl.close()
+    m.free()
+
+
+def test_config2_seal_bytes(L, R):
+    """Config 2's seal (3/2 trellis, K Student-t(4) before the channel scales, seed 2): the 4096-token commit of the
+    config-0 schedule, all 128 records bit-exact."""
+    c = configs.CFG0
+    m, B0, B1 = configs.build_config0(bits=(3, 2), heavy=True, seed=2)
+    lay = m.layers[0]
+    assert lay.lay.body == 1 and lay.lay.bytes == 22784
+    sjk.check(L.sjk_layer_seal(C.byref(lay), B0, B1, None), "seal")
+    _sync()
+    rl = refcache.RefLayer(D, H, c["n_ctx"], c["n_ub"], bits_k=3, bits_v=2, tail=c["tail"], tail_max=c["tail_max"])
+    scale = refcache.synth_scales(2, 0, 1, H, D, lib=R)[0]
+    _ref_grow(rl, 2, True, scale, 0, c["npos"])
+    rl.begin_ubatch(c["npos"], c["n_ub"])
+    ng = (B1 - B0) // 128
+    assert np.array_equal(_body(lay, ng), rl.records(0, ng)), "3/2t record bytes"
+    assert np.array_equal(_ring(lay), rl.ring_bytes()), "ring bytes"
+    rl.close()
+    m.free()
+
+
+def test_config2_attention_32k(L, R):
+    """Config 2's attention at 32K (3/2t, idled at 32,768: B = 28,672, tail 4,096): every record and ring byte
+    bit-exact, and all 64 (row, head) outputs within tolerance of sj_kvarn_layer_attend_row."""
+    c = configs.CFG2
+    m = configs.build_config2()
+    lay = m.layers[0]
+    B, N = m.pol.B, c["N"]
+    q = _rotated_queries(L, m.syn, c["n_q"])
+    out = _attend_dev(L, lay, B, N, q, c["n_q"])
+    rl = refcache.RefLayer(D, H, N + 1024, c["n_ub"], bits_k=3, bits_v=2, tail=c["tail"], tail_max=c["tail_max"])
+    scale = refcache.synth_scales(2, 0, 1, H, D, lib=R)[0]
+    _ref_grow(rl, 2, True, scale, 0, N)
+    rl.idle(0)
+    assert rl.pol.B == B
+    ng = (B - 128) // 128
+    assert np.array_equal(_body(lay, ng), rl.records(0, ng)), "record bytes"
+    assert np.array_equal(_ring(lay), rl.ring_bytes()), "ring bytes"
+    qh = rl.rotate(refcache.synth_q(2, 0, c["n_q"], HQ, D, lib=R))
+    assert np.array_equal(qh.view(np.uint32).ravel(), gu.host(q, np.uint32))
+    pairs = [(iq, hq) for hq in range(HQ) for iq in range(c["n_q"])]
+    err = _attn_err(rl, B, N, qh, out, pairs)
+    print(f"config 2 attention (32K, 3/2t, 64 pairs): max rel err {err:.2e}")
+    assert err <= ATTN_TOL and err <= ATTN_TOL_TIGHT
+    rl.close()
+    m.free()
+
+
+def test_config1_attention_100k(L, R):
+    """Config 1 at its full context (one layer of the 16: N = 100,000, B = 93,824, tail 6,176, seed 1): all 2,928
+    records and the ring bit-exact; 16 (row, head) pairs covering every KV head within tolerance of
+    sj_kvarn_layer_attend_row."""
+    c = configs.CFG1
+    m = configs.build_config1(layers=1)
+    lay = m.layers[0]
+    B, N = m.pol.B, c["N"]
+    q = _rotated_queries(L, m.syn, c["n_q"])
+    out = _attend_dev(L, lay, B, N, q, c["n_q"])
+    rl = refcache.RefLayer(D, H, N, c["n_ub"], tail=c["tail"], tail_max=c["tail_max"])
+    scale = refcache.synth_scales(1, 0, 1, H, D, lib=R)[0]
+    _ref_grow(rl, 1, False, scale, 0, c["idle_at"])
+    rl.idle(0)
+    _ref_grow(rl, 1, False, scale, c["idle_at"], N)
+    assert rl.pol.B == B == 93824
+    ng = (B - 128) // 128
+    assert np.array_equal(_body(lay, ng), rl.records(0, ng)), "record bytes"
+    assert np.array_equal(_ring(lay), rl.ring_bytes()), "ring bytes"
+    qh = rl.rotate(refcache.synth_q(1, 0, c["n_q"], HQ, D, lib=R))
+    pairs = [(hq % c["n_q"], hq) for hq in range(HQ)]
+    err = _attn_err(rl, B, N, qh, out, pairs)
+    print(f"config 1 attention (100K, 4/4, 16 pairs over the 4 KV heads): max rel err {err:.2e}")
+    assert err <= ATTN_TOL and err <= ATTN_TOL_TIGHT
+    rl.close()
+    m.free()
+
+
+CFG4_SAMPLE = (0, 1, 2, 511, 1024, 2047, 2048, 3001, 4095, 4096, 5555, 6143, 7000, 8000, 8190, 8191)
+
+
+def test_config4_sampled_records(L, R):
+    """Config 4 (one sequence of 8,192 groups per KV head, bulk-sealed from a staging buffer in the ring layout,
+    seed 4): 16 groups spread over [0, 8192) x 4 heads bit-exact against sj_kvarn_layer_seal of the same positions."""
+    sm = configs.SliceModel(0, configs.CFG4["groups"], sink=True, tail=configs.CFG4["tail"], n_layers=1)
+    sm.build()
+    _sync()
+    lay = sm.layers[0]
+    rl = refcache.RefLayer(D, H, sm.N + 1024, 512)
+    scale = refcache.synth_scales(4, 0, 1, H, D, lib=R)[0]
+    rec = lay.lay.bytes
+    for g in CFG4_SAMPLE:
+        p0 = 128 + 128 * g
+        k, v = refcache.synth_kv(4, 0, H, D, False, scale, p0, 128, lib=R)
+        rl.store(p0, k, v)
+        rl.seal(p0, p0 + 128, threaded=False)
+        got = gu.d2h_ptr(lay.body + g * H * rec, H * rec)
+        assert np.array_equal(got, rl.records(g, g + 1)), g
+    rl.close()
+    sm.free()
+
+
+def test_config4_slices_merge(L):
+    """Config 4's multi-GPU data path emulated on one GPU: 8 context slices of the seeded sequence (rank r: groups
+    [8192 r / 8, 8192 (r + 1) / 8), rank 0 with the sink, rank 7 with the tail), a partial triple per slice and the
+    merge in rank order, against one attention call over the whole cache."""
+    import slices
+    T = gu.torch()
+    c4 = configs.CFG4
+    whole = configs.SliceModel(0, c4["groups"], sink=True, tail=c4["tail"], n_layers=1)
+    whole.build()
+    syn = configs.DeviceSynth(4, 1)
+    q = _rotated_queries(L, syn, c4["n_q"])
+    ref = _attend_dev(L, whole.layers[0], whole.B, whole.N, q, c4["n_q"])
+    whole.free()
+    W, rows = 8, c4["n_q"] * HQ
+    parts = T.empty((W, rows, D + 2), dtype=T.float32, device="cuda")
+    for r in range(W):
+        g0, g1 = slices.group_range(r, W, c4["groups"])
+        sm = configs.SliceModel(g0, g1, sink=(r == 0), tail=c4["tail"] if r == W - 1 else 0, n_layers=1)
+        sm.build()
+        v = sjk.view_of(sm.layers[0])
+        qpos0 = sm.N - c4["n_q"] if r == W - 1 else sm.N
+        need = L.sjk_attend_scratch_bytes(C.byref(v), sm.N, c4["n_q"], HQ)
+        scratch = T.empty(int(need), dtype=T.uint8, device="cuda")
+        sjk.check(L.sjk_attend_partial(C.byref(v), sm.B, sm.N, qpos0, c4["n_q"], HQ, slices.regions(r, W), gu.ptr(q),
+                                       configs.SCALE, C.c_void_p(parts[r].data_ptr()), gu.ptr(scratch), need, None),
+                  "attend_partial")
+        _sync()
+        sm.free()
+    out = T.empty((c4["n_q"], HQ, D), dtype=T.float32, device="cuda")
+    sjk.check(L.sjk_attend_merge(gu.ptr(parts), W, rows, D, gu.ptr(out), None), "merge")
+    err = gu.rel_err_rows(gu.host(out, np.float32).reshape(rows, D), ref.reshape(rows, D))
+    print(f"config 4 (8 slices merged vs one call over 1,052,928 positions): max rel err {err:.2e}")
+    assert err <= ATTN_TOL_TIGHT
+
+
+def test_libm_log_exp_on_balancing_arguments(L, oracle_lib):
+    """The seal's double log and exp (the device's) against this host's libm (the reference's) on every argument the
+    balancing reaches while sealing config 0's and config 2's commits: bit-for-bit equal results."""
+    T = gu.torch()
+    O = oracle_lib.lib()
+    args_log, args_exp = [], []
+    for seed, bits, heavy in ((0, (4, 4), False), (2, (3, 2), True)):
+        c = configs.CFG0
+        oc = oracle_lib.OracleCache(D, H, bits[0], bits[1], bits != (4, 4), 16, 0, True, 128, c["tail"], c["tail_max"],
+                                    c["n_ub"], c["n_ctx"])
+        scale = refcache.synth_scales(seed, 0, 1, H, D, lib=O)[0]
+        for pos in range(0, c["npos"], 512):
+            n = min(512, c["npos"] - pos)
+            k, v = refcache.synth_kv(seed, 0, H, D, heavy, scale, pos, n, lib=O)
+            kr, vr = oracle_lib.fwht_rows(k), oracle_lib.fwht_rows(v)
+            for i in range(n):
+                oc.store(pos + i, kr[i], vr[i])
+        cap = 4_000_000
+        bl, be = np.zeros(cap), np.zeros(cap)
+        O.ora_trace_balance(bl.ctypes.data, be.ctypes.data, cap)
+        oc.seal(128, 4224)
+        nl, ne = C.c_size_t(), C.c_size_t()
+        O.ora_trace_counts(C.byref(nl), C.byref(ne))
+        O.ora_trace_balance(None, None, 0)
+        assert 0 < nl.value <= cap and 0 < ne.value <= cap
+        args_log.append(bl[:nl.value])
+        args_exp.append(be[:ne.value])
+        oc.close()
+    x = np.unique(np.concatenate(args_log + args_exp))
+    lg, ex = np.zeros_like(x), np.zeros_like(x)
+    O.ora_libm_log_exp(x.ctypes.data, x.size, lg.ctypes.data, ex.ctypes.data)
+    dx = T.from_numpy(x).cuda()
+    dlg, dex = T.empty_like(dx), T.empty_like(dx)
+    sjk.check(L.sjk_seal_libm_probe(gu.ptr(dx), x.size, gu.ptr(dlg), gu.ptr(dex), None), "libm probe")
+    is_log = np.isin(x, np.concatenate(args_log))
+    is_exp = np.isin(x, np.concatenate(args_exp))
+    glg, gex = gu.host(dlg, np.float64), gu.host(dex, np.float64)
+    bad_log = int((glg.view(np.uint64) != lg.view(np.uint64))[is_log].sum())
+    bad_exp = int((gex.view(np.uint64) != ex.view(np.uint64))[is_exp].sum())
+    print(f"balancing arguments: {int(is_log.sum())} distinct log, {int(is_exp.sum())} distinct exp; "
+          f"differing results: log {bad_log}, exp {bad_exp}")
+    assert bad_log == 0 and bad_exp == 0

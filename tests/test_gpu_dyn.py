@@ -212,3 +212,59 @@ def test_bad_descriptor_writes_nothing(L):
         T.cuda.synchronize()
     finally:
         s.close()
+
+
+@pytest.mark.parametrize("bk,bv,body", [(3, 2, 1), (4, 4, 0)])
+def test_dyn_calls_against_oracle(L, oracle_lib, bk, bv, body):
+    """The descriptor-driven calls checked directly against the oracle (not only against the host-planned product
+    path): a cache written by sjk_store_dyn and sealed by sjk_seal_dyn, one descriptor per ubatch, holds the oracle's
+    sink, ring and record bytes, and sjk_attend_dyn matches the oracle's attention loop (sj_kvarn.h:1535-1564)."""
+    import refcache
+    D, n_ub, npos, n_q, n_head = 256, 64, 1700, 2, 8
+    cfg = sjk.config(D, H, 2048, n_ub, bits_k=bk, bits_v=bv, body=body, tail=TAIL, tail_max=TAIL_MAX)
+    layer = sjk.Layer()
+    sjk.check(L.sj_kvarn_layer_init(C.byref(layer), C.byref(cfg)), "layer_init")
+    trellis = L.sj_kvarn_body_resolve(body, bk, bv) == 1
+    oc = oracle_lib.OracleCache(D, H, bk, bv, trellis, 16, 0, True, 128, TAIL, TAIL_MAX, n_ub, 2048)
+    pol = sjk.Policy()
+    L.sj_kvarn_policy_init(C.byref(pol), 128, TAIL, TAIL_MAX, 128, 0)
+    view = sjk.View()
+    L.sjk_layer_view(C.byref(layer), C.byref(view))
+    O = oracle_lib.lib()
+    scale_kv = refcache.synth_scales(21, 0, 1, H, D, lib=O)[0]
+    try:
+        for pos in range(0, npos, n_ub):
+            n = min(n_ub, npos - pos)
+            L.sj_kvarn_policy_begin_ubatch(C.byref(pol), pos, n)
+            desc = gu.dev(sjk.desc_fill(view, pol.B, pol.B_pending, pos + n, pos))
+            sjk.check(L.sjk_seal_dyn(C.byref(view), gu.ptr(desc), 16, 16, None), "seal_dyn")
+            if pol.B_pending > pol.B:
+                oc.seal(pol.B, pol.B_pending)
+            L.sj_kvarn_policy_commit(C.byref(pol))
+            k, v = refcache.synth_kv(21, 0, H, D, False, scale_kv, pos, n, lib=O)
+            dk, dv = gu.dev(k), gu.dev(v)
+            sjk.check(L.sjk_store_dyn(C.byref(view), gu.ptr(desc), n, gu.ptr(dk), gu.ptr(dv), 1, None), "store_dyn")
+            kr, vr = oracle_lib.fwht_rows(k), oracle_lib.fwht_rows(v)
+            for i in range(n):
+                oc.store(pos + i, kr[i].ravel(), vr[i].ravel())
+            gu.torch().cuda.synchronize()
+        B = pol.B
+        ng = (B - 128) // 128
+        assert ng >= 8
+        assert np.array_equal(gu.d2h_ptr(layer.body, ng * H * layer.lay.bytes), oc.body_bytes(ng)), "records"
+        assert np.array_equal(gu.d2h_ptr(layer.ring, layer.cap * H * 2 * layer.stage_bytes), oc.ring_bytes()), "ring"
+        q = oracle_lib.fwht_rows(np.random.default_rng(22).standard_normal((n_q, n_head, D)).astype(np.float32))
+        dq = gu.dev(q)
+        out = gu.dev_zeros(q.nbytes)
+        need = L.sjk_attend_dyn_scratch_bytes(C.byref(view), n_q, n_head)
+        scratch = gu.dev_zeros(need)
+        desc = gu.dev(sjk.desc_fill(view, B, B, npos, npos - n_q))
+        sjk.check(L.sjk_attend_dyn(C.byref(view), gu.ptr(desc), n_q, n_head, gu.ptr(dq), np.float32(1 / 16), gu.ptr(out),
+                                   gu.ptr(scratch), need, None), "attend_dyn")
+        ref = oc.attend(B, npos, npos - n_q, q, 1.0 / 16)
+        err = gu.rel_err_rows(gu.host(out, np.float32, q.shape), ref)
+        assert err <= 1e-4, err
+        assert L.sjk_device_status() == 0
+    finally:
+        L.sj_kvarn_layer_free(C.byref(layer))
+        oc.close()

@@ -326,3 +326,37 @@ def test_state_roundtrip_pool_and_truncate(L, oracle_lib):
         q.close()
     assert pool.n_free == pool.n_blocks - 1
     L.sj_kvarn_pool_free(C.byref(pool))
+
+
+@pytest.mark.parametrize("bk,bv,body", [(4, 4, 0), (3, 2, 1), (3, 3, 1), (4, 2, 0)])
+def test_record_scores_and_accum_v_match_reference(L, oracle_lib, bk, bv, body):
+    """sj_kvarn_record_scores / sj_kvarn_record_accum_v on device pointers equal the compiled reference's
+    (sj_kvarn.h:1288-1311: sequential fp32 dots and token-ordered accumulation) bit for bit, for full and partial
+    token counts."""
+    import refcache
+    if not refcache.available():
+        pytest.skip("oracle/_ref not built")
+    R = refcache.ref()
+    R.sj_kvarn_record_scores.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+    R.sj_kvarn_record_accum_v.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]
+    K, V = _group(256)
+    lay = sjk.layout(256, bk, bv, body)
+    rec = oracle_lib.seal(oracle_lib.layout(256, bk, bv, body == 1), K, V)
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal(256).astype(np.float32)
+    w = rng.random(128).astype(np.float32)
+    acc0 = rng.standard_normal(256).astype(np.float32)
+    drec, dq, dw = gu.dev(rec), gu.dev(q), gu.dev(w)
+    for n in (128, 77, 1):
+        dsc = gu.dev_zeros(128 * 4)
+        L.sj_kvarn_record_scores(C.byref(lay), gu.ptr(drec), gu.ptr(dq), n, gu.ptr(dsc))
+        sjk.check_sticky("record_scores")
+        want = np.zeros(128, np.float32)
+        R.sj_kvarn_record_scores(C.byref(lay), rec.ctypes.data, q.ctypes.data, n, want.ctypes.data)
+        assert np.array_equal(gu.host(dsc, np.uint32)[:n], want.view(np.uint32)[:n]), n
+        dacc = gu.dev(acc0)
+        L.sj_kvarn_record_accum_v(C.byref(lay), gu.ptr(drec), gu.ptr(dw), n, gu.ptr(dacc))
+        sjk.check_sticky("record_accum_v")
+        acc = acc0.copy()
+        R.sj_kvarn_record_accum_v(C.byref(lay), rec.ctypes.data, w.ctypes.data, n, acc.ctypes.data)
+        assert np.array_equal(gu.host(dacc, np.uint32), acc.view(np.uint32)), n

@@ -152,3 +152,81 @@ def test_oracle_seal_edges_match_compiled_reference(oracle_lib, bk, bv, body):
         r.sjref_seal_batch(C.byref(lay), k.ctypes.data, v.ctypes.data, 256, 1, 1, 16, want.ctypes.data, 1)
         got = oracle_lib.seal(ol, k, v)
         assert np.array_equal(got, want), name
+
+
+REF_BUILT = os.path.exists(os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref", "libsjref.so"))
+
+
+def _small_builds(oracle_lib, bits=(4, 4), heavy=False, npos=1500, seed=9, H=2):
+    """The same small cache (D 256, sink 128, tail 256 -> 512, ubatch 128) built through the policy in the oracle and
+    in the compiled reference, from the seeded generator's rows."""
+    import refcache
+    D, tail, tail_max, n_ub = 256, 256, 512, 128
+    trellis = bits != (4, 4) and bits != (4, 2)
+    oc = oracle_lib.OracleCache(D, H, bits[0], bits[1], trellis, 16, 0, True, 128, tail, tail_max, n_ub, npos + 256)
+    rl = refcache.RefLayer(D, H, npos + 256, n_ub, bits_k=bits[0], bits_v=bits[1], tail=tail, tail_max=tail_max)
+    O = oracle_lib.lib()
+    pol = oracle_lib.Policy()
+    O.ora_policy_init(pol, 128, tail, tail_max, 128, 0)
+    scale = refcache.synth_scales(seed, 0, 1, H, D)[0]
+    for pos in range(0, npos, n_ub):
+        n = min(n_ub, npos - pos)
+        O.ora_policy_begin(pol, pos, n)
+        if pol.B_pending > pol.B:
+            oc.seal(pol.B, pol.B_pending)
+        O.ora_policy_commit(pol)
+        rl.begin_ubatch(pos, n, threaded=False)
+        k, v = refcache.synth_kv(seed, 0, H, D, heavy, scale, pos, n)
+        rl.store(pos, k, v)
+        kr, vr = oracle_lib.fwht_rows(k), oracle_lib.fwht_rows(v)
+        for i in range(n):
+            oc.store(pos + i, kr[i], vr[i])
+    assert pol.B == rl.pol.B
+    return oc, rl, pol.B
+
+
+@pytest.mark.skipif(not REF_BUILT, reason="reference not compiled here")
+@pytest.mark.parametrize("bits,heavy", [((4, 4), False), ((3, 2), True)])
+def test_oracle_cache_and_attend_row_match_compiled_reference(oracle_lib, bits, heavy):
+    """A policy-driven build in the oracle equals one through the compiled reference (sink, ring, records), and the
+    oracle's attention loop ora_attend_row equals sj_kvarn_layer_attend_row bit for bit over every region."""
+    import ctypes as C
+    import refcache
+    oc, rl, B = _small_builds(oracle_lib, bits, heavy)
+    N = 1500
+    ng = (B - 128) // 128
+    assert np.array_equal(oc.body_bytes(ng), rl.records(0, ng))
+    assert np.array_equal(oc.ring_bytes(), rl.ring_bytes())
+    assert np.array_equal(oc.sink_bytes(), rl.sink_bytes())
+    q = rl.rotate(refcache.synth_q(9, 0, 3, 4, 256))
+    out = np.zeros(256, np.float32)
+    for iq in range(3):
+        for hq in range(4):
+            for qpos in (N - 3 + iq, 200, B + 5):
+                want = rl.attend_row(B, N, q[iq, hq], hq // 2, qpos, 1.0 / 16)
+                oracle_lib.lib().ora_attend_row(C.byref(oc.c), B, N, np.ascontiguousarray(q[iq, hq]), hq // 2, qpos,
+                                                1.0 / 16, out)
+                assert np.array_equal(out.view(np.uint32), want.view(np.uint32)), (iq, hq, qpos)
+    oc.close()
+    rl.close()
+
+
+@pytest.mark.skipif(not REF_BUILT, reason="reference not compiled here")
+def test_reference_seal_harness_matches_layer_seal():
+    """The threaded harness that the CPU baselines and the configuration tests use (sjref_layer_seal_mt: per record,
+    unstage the ring rows, round to fp16, sj_kvarn_seal_group with a per-thread workspace) writes exactly the records
+    of the reference's own sj_kvarn_layer_seal."""
+    import refcache
+    D, H = 256, 4
+    for bits, heavy in (((4, 4), False), ((3, 2), True)):
+        a = refcache.RefLayer(D, H, 2048, 512, bits_k=bits[0], bits_v=bits[1], tail=512, tail_max=1024)
+        b = refcache.RefLayer(D, H, 2048, 512, bits_k=bits[0], bits_v=bits[1], tail=512, tail_max=1024)
+        scale = refcache.synth_scales(5, 0, 1, H, D)[0]
+        k, v = refcache.synth_kv(5, 0, H, D, heavy, scale, 0, 128 + 3 * 128)
+        a.store(0, k, v)
+        b.store(0, k, v)
+        a.seal(128, 512, threaded=True)
+        b.seal(128, 512, threaded=False)
+        assert np.array_equal(a.records(0, 3), b.records(0, 3)), bits
+        a.close()
+        b.close()
