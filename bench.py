@@ -16,7 +16,8 @@ host). The BASELINE configurations (sj-kvarn-codec_b200/configs.py):
   config3   64-sequence paged pool, 3/3 trellis, decode width 1: tokens/s over a window of decode steps that holds
             policy-triggered seals; sequences split over the ranks by LPT (no collective)
   config4   one 1,048,576-token sequence sliced by context over the ranks: bulk seal (Mtok/s per GPU) and attention
-            (partial per rank, NCCL all-gather of the (m, l, o) triples, merge), with per-phase times
+            (partial per rank, the (m, l, o) triples exchanged over peer memory and merged), with per-phase times and
+            the NCCL all-gather + merge path beside it
   parity    the GPU's config-0 records and config-1 / config-2 attention against the reference's, computed in the
             cpu_baseline leg from the same seeded rows (or against the committed golden hashes without that leg)
   cpu_baseline  the reference (oracle/_ref: sj_kvarn.h compiled from its own source) on the host cores: config-1
@@ -342,8 +343,9 @@ def run_config4(args, torch, dist, rank, world):
     """Config 4: one 1,048,576-token sequence (8,192 groups per KV head and layer + 128 sink + 4,096 tail, seed 4)
     sliced by context: rank r holds groups [8192 r / W, 8192 (r + 1) / W) of every layer (rank 0 also the sink, the
     last rank the tail). Bulk seal: each layer's slice is staged into one staging buffer in the ring layout and
-    sealed in one launch (timed: Mtok/s per GPU). Attention per layer call: sjk_attend_partial on every rank, an NCCL
-    all-gather of the (m, l, o) triples, sjk_attend_merge in rank order; the phases are timed separately too. With
+    sealed in one launch (timed: Mtok/s per GPU). Attention per layer call: sjk_attend_partial on every rank, then the
+    (m, l, o) triples go to every rank over peer memory (slices.PeerExchange: NVLink stores, local merge in rank order);
+    the NCCL all-gather + sjk_attend_merge path is timed beside it, and the phases separately. With
     several ranks, rank 0 also rebuilds layer 0 whole and checks the merged output against one call over it."""
     import configs
     import sjk
@@ -405,7 +407,18 @@ def run_config4(args, torch, dist, rank, world):
         if rc:
             raise sjk.SjkError(rc, "attend_merge")
 
-    def step():
+    xch = slices.PeerExchange(dist, rank, world, rows, D)
+
+    def p2p(il):
+        xch.exchange(part, out[il], st)
+
+    def step():                                                  # the product path: partial + peer exchange
+        with torch.cuda.stream(s):
+            for il in range(nl):
+                partial(il)
+                p2p(il)
+
+    def step_nccl():                                             # the same through NCCL all-gather + merge
         with torch.cuda.stream(s):
             for il in range(nl):
                 partial(il)
@@ -413,13 +426,21 @@ def run_config4(args, torch, dist, rank, world):
                 merge(il)
 
     ms = time_events(torch, s, step, max(3, args.steps), args.warmup, barrier)
+    ms_nccl = time_events(torch, s, step_nccl, max(3, args.steps), args.warmup, barrier)
     # per-phase device times over the same number of layer calls
     with torch.cuda.stream(s):
         ms_partial = time_events(torch, s, lambda: [partial(il) for il in range(nl)], max(3, args.steps), 1, barrier)
+        ms_p2p = time_events(torch, s, lambda: [p2p(il) for il in range(nl)], max(3, args.steps), 1, barrier)
         ms_exchange = time_events(torch, s, lambda: [exchange() for _ in range(nl)], max(3, args.steps), 1, barrier)
         ms_merge = time_events(torch, s, lambda: [merge(il) for il in range(nl)], max(3, args.steps), 1, barrier)
+    # the peer exchange's output against the NCCL path's (same triples, same merge order: identical bits)
     step()
     torch.cuda.synchronize()
+    out_p2p = out.clone()
+    step_nccl()
+    torch.cuda.synchronize()
+    p2p_equal = bool(torch.equal(out_p2p.view(torch.int32), out.view(torch.int32)))
+    xch.close()
     check_err = None
     if world > 1 and rank == 0:
         whole = configs.SliceModel(0, c4["groups"], sink=True, tail=c4["tail"], n_layers=1, stream=st)
@@ -432,14 +453,16 @@ def run_config4(args, torch, dist, rank, world):
         a, b = out[0].cpu().numpy().reshape(rows, D).astype(np.float64), wout.cpu().numpy().reshape(rows, D).astype(np.float64)
         check_err = float((np.linalg.norm(a - b, axis=1) / np.linalg.norm(b, axis=1)).max())
         whole.free()
-    t = torch.tensor([ms, ms_partial, ms_exchange, ms_merge, ms_seal], device="cuda")
+    t = torch.tensor([ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, 0.0 if p2p_equal else 1.0],
+                     device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_partial, ms_exchange, ms_merge, ms_seal = [float(x) for x in t]
+    ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, p2p_diff = [float(x) for x in t]
     sm.free()
     B_global = SINK + c4["groups"] * G
     n_global = B_global + c4["tail"]
     return dict(ms=ms / nl, ms_partial=ms_partial / nl, ms_exchange=ms_exchange / nl, ms_merge=ms_merge / nl,
+                ms_nccl=ms_nccl / nl, ms_p2p=ms_p2p / nl, p2p_equals_nccl=p2p_diff == 0.0,
                 bytes=attn_bytes_per_call(B_global, n_global), n_ctx=n_global, layers=nl, exchange=rows * (D + 2) * 4,
                 groups_per_rank=g1 - g0, write_s=write_s, seal_ms=ms_seal, tokens_sealed=tokens_sealed,
                 merged_vs_whole=check_err)
@@ -968,12 +991,15 @@ def main():
         "config4": None if cfg4 is None else {
             "workload": f"config 4: one 1,048,576-token sequence (+ 128 sink, 4,096 tail), 4/4, seed 4, {cfg4['layers']} "
                         f"layers, split by context slice over {world} rank(s); bulk seal of each rank's slice; per layer "
-                        "call: partial attention per rank + NCCL all-gather of (m, l, o) + merge",
+                        "call: partial attention per rank + exchange of the (m, l, o) triples over peer memory + merge",
             "attn_us_per_call": cfg4["ms"] * 1e3, "attn_bytes_per_call": cfg4["bytes"], "n_ctx": cfg4["n_ctx"],
             "attn_gbs": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9,
             "attn_frac_of_all_ranks": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9 / (peak * world),
-            "phases_us_per_call": {"partial": cfg4["ms_partial"] * 1e3, "all_gather": cfg4["ms_exchange"] * 1e3,
-                                   "merge": cfg4["ms_merge"] * 1e3},
+            "phases_us_per_call": {"partial": cfg4["ms_partial"] * 1e3, "peer_exchange": cfg4["ms_p2p"] * 1e3,
+                                   "nccl_all_gather": cfg4["ms_exchange"] * 1e3, "nccl_merge": cfg4["ms_merge"] * 1e3},
+            "nccl_path_us_per_call": cfg4["ms_nccl"] * 1e3, "peer_exchange_equals_nccl_path": cfg4["p2p_equals_nccl"],
+            "exchange": "per layer call: each rank stores its (m, l, o) triples into every peer's exchange buffer over "
+                        "NVLink (CUDA IPC mappings, plain stores) and merges all ranks' triples locally in rank order",
             "bulk_seal": {"mtoks_per_gpu": cfg4["tokens_sealed"] / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "mtoks_all_gpus": cfg4["tokens_sealed"] * world / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "ms": cfg4["seal_ms"], "tokens_per_gpu": cfg4["tokens_sealed"],

@@ -440,6 +440,30 @@ int sjk_seq_store(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_pos, const float *
 /* copy record (g, h) to host memory (synchronous) */
 int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * host_dst);
 
+/* ---- exchange of attention partials between GPUs over peer memory ----
+ * For a sequence split by context slice over `world` GPUs (one process per GPU), sjk_attend_partial gives each rank
+ * one (m, l, o[D]) triple per (query row, query head); these calls replace an all-gather of the triples plus
+ * sjk_attend_merge by NVLink P2P stores into the other ranks' exchange buffers and a local merge. Each rank allocates
+ * one exchange buffer (sjk_xchg_alloc, zeroed; its CUDA IPC handle, SJK_XCHG_HANDLE_BYTES, goes to the other ranks,
+ * which map it with sjk_xchg_open). Per layer call, with an epoch the ranks count up alike from 1:
+ * sjk_xchg_publish writes this rank's triples into slot `rank` of every rank's buffer (peers: HOST array of world
+ * device addresses as this process sees them, peers[rank] = its own buffer) and raises its flags there;
+ * sjk_xchg_merge waits (bounded by about 1 s) for every rank's flags in the local buffer and merges the slots in
+ * rank order with sjk_attend_merge's kernel, so the output equals all-gather + sjk_attend_merge bit for bit. A wait
+ * that runs out yields zeros and SJK_DEVICE_TIMEOUT in sjk_device_status(). Calls of consecutive epochs alternate
+ * between two slot sets, so a rank may publish epoch e + 1 while others still merge epoch e. No TMA, no multicast:
+ * plain stores and loads. No counterpart in the reference, whose attention runs on one device. */
+#define SJK_XCHG_MAX_WORLD   16
+#define SJK_XCHG_HANDLE_BYTES 64
+size_t sjk_xchg_bytes(int world, int n_rows, int D);
+int    sjk_xchg_alloc(size_t bytes, void ** buf, void * ipc_handle);
+int    sjk_xchg_free(void * buf);
+int    sjk_xchg_open(const void * ipc_handle, void ** peer_buf);
+int    sjk_xchg_close(void * peer_buf);
+int    sjk_xchg_publish(void * const * peers, int world, int rank, const float * part, int n_rows, int D, uint32_t epoch,
+                        sjk_stream st);
+int    sjk_xchg_merge(void * local_buf, int world, int n_rows, int D, uint32_t epoch, float * out, sjk_stream st);
+
 /* ---- seeded synthetic inputs of the benchmark configurations (DEVICE outputs) ----
  * Input generation for benchmarks and parity tests; no counterpart in the reference. K = X * s with X ~ N(0, 1)
  * (Student-t(4) when heavy) and s ~ LogNormal(0, 1) channel scales with 4 outlier channels x 8 per (layer, head);

@@ -91,7 +91,8 @@ def lib():
                                      [C.c_uint32] * 3 + [C.c_void_p]
         L.ora_state_write.restype = C.c_size_t
         L.ora_fnv.argtypes = [C.c_void_p, C.c_size_t, C.c_uint64]; L.ora_fnv.restype = C.c_uint64
-        L.ora_trace_balance.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t]
+        L.ora_trace_balance.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]
+        L.ora_balance_step.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
         L.ora_trace_counts.argtypes = [C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
         L.ora_libm_log_exp.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
         _lib = L

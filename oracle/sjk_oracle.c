@@ -279,11 +279,11 @@ static void rescale(const float * M, int R, int C, const float * srow, const flo
 
 /* Optional trace of every argument the balancing passes to log() and exp() (for the check of the device's double
  * log/exp against this host's libm): slots are claimed atomically, so tracing works under the threaded seals. */
-static double * g_trace_log, * g_trace_exp;
+static double * g_trace_log, * g_trace_prev, * g_trace_exp;
 static size_t g_trace_cap, g_trace_n_log, g_trace_n_exp;
 
-void ora_trace_balance(double * log_args, double * exp_args, size_t cap) {
-    g_trace_log = log_args; g_trace_exp = exp_args; g_trace_cap = cap;
+void ora_trace_balance(double * log_args, double * log_prev, double * exp_args, size_t cap) {
+    g_trace_log = log_args; g_trace_prev = log_prev; g_trace_exp = exp_args; g_trace_cap = cap;
     __atomic_store_n(&g_trace_n_log, 0, __ATOMIC_SEQ_CST);
     __atomic_store_n(&g_trace_n_exp, 0, __ATOMIC_SEQ_CST);
 }
@@ -293,10 +293,11 @@ void ora_trace_counts(size_t * n_log, size_t * n_exp) {
     *n_exp = __atomic_load_n(&g_trace_n_exp, __ATOMIC_SEQ_CST);
 }
 
-static double traced_log(double x) {
+/* log(x) of a scale update whose running log-scale before the update is `prev` (both traced) */
+static double traced_log(double prev, double x) {
     if (g_trace_log) {
         const size_t i = __atomic_fetch_add(&g_trace_n_log, 1, __ATOMIC_RELAXED);
-        if (i < g_trace_cap) g_trace_log[i] = x;
+        if (i < g_trace_cap) { g_trace_log[i] = x; g_trace_prev[i] = prev; }
     }
     return log(x);
 }
@@ -310,6 +311,12 @@ static double traced_exp(double x) {
 }
 
 /* this host's libm log and exp of n doubles (the functions the reference's balancing calls) */
+/* next running log-scale of a scale update, as the balancing forms it (sj_kvarn.h:1001-1008) */
+void ora_balance_step(const double * prev, const double * lg, size_t n, double * out) {
+    size_t i;
+    for (i = 0; i < n; ++i) out[i] = lesser_d(greater_d(prev[i] + lg[i], -0.3), 10.0);
+}
+
 void ora_libm_log_exp(const double * x, size_t n, double * lg, double * ex) {
     size_t i;
     for (i = 0; i < n; ++i) { lg[i] = log(x[i]); ex[i] = exp(x[i]); }
@@ -325,13 +332,13 @@ static void balance(const float * M, int R, int C, int iters, float * srow, floa
     for (it = 0; it < iters; ++it) {
         for (c = 0; c < C; ++c) {
             const float sd = lesser_f(greater_f(chunked_std(cur + c, R, (size_t) C), 1e-3f), 1e3f);
-            lcol[c] = lesser_d(greater_d(lcol[c] + traced_log((double) sd), -0.3), 10.0);
+            lcol[c] = lesser_d(greater_d(lcol[c] + traced_log(lcol[c], (double) sd), -0.3), 10.0);
             scol[c] = (float) traced_exp(lcol[c]);
         }
         rescale(M, R, C, srow, scol, cur);
         for (r = 0; r < R; ++r) {
             const float sd = lesser_f(greater_f(chunked_std(cur + (size_t) r * C, C, 1), 1e-3f), 1e3f);
-            lrow[r] = lesser_d(greater_d(lrow[r] + traced_log((double) sd), -0.3), 10.0);
+            lrow[r] = lesser_d(greater_d(lrow[r] + traced_log(lrow[r], (double) sd), -0.3), 10.0);
             srow[r] = (float) traced_exp(lrow[r]);
         }
         rescale(M, R, C, srow, scol, cur);

@@ -101,9 +101,11 @@ size_t ora_state_write(const ora_cache * layers, int nl, const ora_policy * p, u
                        int trellis, int iters, int staging, int sink_f16, uint32_t tail, uint32_t tail_max,
                        uint32_t flush_chunk, uint8_t * dst);
 
-/* trace every log()/exp() argument of the balancing into the given arrays (NULL stops tracing); counts of the
- * arguments seen since (they may exceed cap: only the first cap are kept) */
-void ora_trace_balance(double * log_args, double * exp_args, size_t cap);
+/* trace every log()/exp() argument of the balancing (and the running log-scale each log result is added to) into
+ * the given arrays (NULL stops tracing); counts of the arguments seen since (only the first cap are kept) */
+void ora_trace_balance(double * log_args, double * log_prev, double * exp_args, size_t cap);
+/* out[i] = clamp(prev[i] + lg[i], -0.3, 10): the balancing's update of a running log-scale */
+void ora_balance_step(const double * prev, const double * lg, size_t n, double * out);
 void ora_trace_counts(size_t * n_log, size_t * n_exp);
 /* this host's libm log and exp of n doubles */
 void ora_libm_log_exp(const double * x, size_t n, double * lg, double * ex);

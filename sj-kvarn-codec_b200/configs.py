@@ -211,7 +211,7 @@ class SliceModel:
         for off in range(0, self.n_body, self.chunk):
             n = min(self.chunk, self.n_body - off)
             self.syn.rows_into(il, SINK + self.g0 * G + off, n, k, v)
-            sjk.check(L.sjk_store(C.byref(sv), None, C.c_void_p(self.staging.data_ptr()), SINK + off, n,
+            sjk.check(L.sjk_store(C.byref(sv), C.c_void_p(lay.sink), C.c_void_p(self.staging.data_ptr()), SINK + off, n,
                                   C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), 1, self.st), "store staging")
         if self.tail:
             for off in range(0, self.tail, self.chunk):

@@ -590,8 +590,9 @@ extern "C" int sjk_device_status(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take(), c = sjk_tc_trellis_status_take();
     const int d = attend_desc_status_take(), e = sjk_seal_desc_status_take(), f = sjk_stage_desc_status_take();
-    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0) return -1;
-    return a | b | c | d | e | f;
+    const int x = sjk_xchg_status_take();
+    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0 || x < 0) return -1;
+    return a | b | c | d | e | f | x;
 }
 
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,

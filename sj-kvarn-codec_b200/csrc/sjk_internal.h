@@ -49,6 +49,7 @@ int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpo
 int sjk_tc_body_status_take(void);
 int sjk_tc_dense_status_take(void);
 int sjk_tc_trellis_status_take(void);
+int sjk_xchg_status_take(void);
 
 // Move the record groups [g0, g0 + n) of one layer (group_bytes = n_head_kv x record bytes) through
 // an optional device block table: op 0 gathers them into buf (group order), op 1 scatters buf into them, op 2

@@ -155,6 +155,14 @@ SIGNATURES = {
     "sjk_layer_attend": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sjk_layer_view": (None, [P(Layer), P(View)]),
     "sjk_layer_record_copy": (C.c_int, [P(Layer), u32, C.c_int, vp]),
+    # exchange of partials over peer memory
+    "sjk_xchg_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
+    "sjk_xchg_alloc": (C.c_int, [C.c_size_t, P(vp), vp]),
+    "sjk_xchg_free": (C.c_int, [vp]),
+    "sjk_xchg_open": (C.c_int, [vp, P(vp)]),
+    "sjk_xchg_close": (C.c_int, [vp]),
+    "sjk_xchg_publish": (C.c_int, [P(vp), C.c_int, C.c_int, vp, C.c_int, C.c_int, u32, vp]),
+    "sjk_xchg_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, u32, vp, vp]),
     # seeded synthetic inputs
     "sjk_synth_scales": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]),
     "sjk_synth_kv": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, u32, u32, vp, vp, vp]),

@@ -81,3 +81,62 @@ def lpt_assign(costs, world):
         owner[i] = r
         load[r] += float(costs[i])
     return owner
+
+
+class PeerExchange:
+    """The per-layer exchange of config 4's partial triples over peer memory (sjk_xchg_*): every rank allocates one
+    exchange buffer, the ranks swap its CUDA IPC handle once through the process group, and each layer call publishes
+    the rank's triples into every peer's buffer with NVLink stores and merges the ranks' triples locally in rank
+    order. The output equals an all-gather + sjk_attend_merge of the same triples bit for bit."""
+
+    def __init__(self, dist, rank, world, n_rows, D):
+        import ctypes as C
+
+        import sjk
+        self.C, self.sjk, self.L = C, sjk, sjk.lib()
+        self.rank, self.world, self.n_rows, self.D = rank, world, n_rows, D
+        nbytes = self.L.sjk_xchg_bytes(world, n_rows, D)
+        if nbytes == 0:
+            raise ValueError("exchange shape out of range")
+        self.buf = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        sjk.check(self.L.sjk_xchg_alloc(nbytes, C.byref(self.buf), handle), "xchg_alloc")
+        handles = [bytes(handle)] * world
+        if dist is not None and world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle))
+        self.peers = (C.c_void_p * world)()
+        self.opened = []
+        for r in range(world):
+            if r == rank:
+                self.peers[r] = self.buf.value
+            else:
+                p = C.c_void_p()
+                hb = (C.c_uint8 * 64).from_buffer_copy(handles[r])
+                sjk.check(self.L.sjk_xchg_open(hb, C.byref(p)), "xchg_open")
+                self.peers[r] = p.value
+                self.opened.append(p)
+        self.dist = dist
+        self.epoch = 0
+
+    def exchange(self, part, out, stream):
+        """part: this rank's [n_rows][D + 2] triples (device); out: [n_rows][D] merged output (device)."""
+        C = self.C
+        self.epoch += 1
+        self.sjk.check(self.L.sjk_xchg_publish(self.peers, self.world, self.rank, C.c_void_p(part.data_ptr()), self.n_rows,
+                                               self.D, self.epoch, stream), "xchg_publish")
+        self.sjk.check(self.L.sjk_xchg_merge(self.buf, self.world, self.n_rows, self.D, self.epoch,
+                                             C.c_void_p(out.data_ptr()), stream), "xchg_merge")
+
+    def close(self):
+        """Collective: every rank calls it once all its exchanges have completed on the device."""
+        import torch
+        torch.cuda.synchronize()
+        if self.dist is not None and self.world > 1:
+            self.dist.barrier()
+        for p in self.opened:
+            self.L.sjk_xchg_close(p)
+        self.opened = []
+        if self.buf:
+            self.L.sjk_xchg_free(self.buf)
+            self.buf = self.C.c_void_p()
