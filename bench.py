@@ -359,21 +359,22 @@ def run_config4(args, torch, dist, rank, world):
     sm = configs.SliceModel(g0, g1, sink=(rank == 0), tail=c4["tail"] if rank == world - 1 else 0,
                             n_layers=args.config4_layers, stream=st)
     nl = len(sm.layers)
+    # every layer: its slice's rows staged (the staging buffer is shared by the layers), then its bulk seal; the seal
+    # launches alone are timed with events (max over ranks)
+    barrier = (lambda: dist.barrier()) if dist else None
+    ms_seal = 0.0
     for il in range(nl):
         sm.write_layer(il)
-    torch.cuda.synchronize()
-    write_s = time.time() - t0
-    # bulk seal of every layer's slice, timed with events (max over ranks)
-    barrier = (lambda: dist.barrier()) if dist else None
-    if barrier:
-        barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for il in range(nl):
+        if barrier and il == 0:
+            torch.cuda.synchronize()
+            barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
         sm.seal_layer(il)
-    e1.record(s)
-    torch.cuda.synchronize()
-    ms_seal = e0.elapsed_time(e1)
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms_seal += e0.elapsed_time(e1)
+    write_s = time.time() - t0
     tokens_sealed = sm.n_body * nl
     n_q, rows = c4["n_q"], c4["n_q"] * HQ
     q = torch.stack([sm.syn.queries(il, n_q) for il in range(nl)]).contiguous()
@@ -412,7 +413,16 @@ def run_config4(args, torch, dist, rank, world):
     def p2p(il):
         xch.exchange(part, out[il], st)
 
-    def step():                                                  # the product path: partial + peer exchange
+    def fused(il):
+        xch.attend(views[il], sm.B, sm.N, qpos0, n_q, HQ, reg, C.c_void_p(q.data_ptr() + il * per * 4), SCALE, scratch,
+                   need, C.c_void_p(out.data_ptr() + il * per * 4), st)
+
+    def step():                                                  # the product path: partial + exchange in one call
+        with torch.cuda.stream(s):
+            for il in range(nl):
+                fused(il)
+
+    def step_split():                                            # partial, then the stand-alone exchange
         with torch.cuda.stream(s):
             for il in range(nl):
                 partial(il)
@@ -426,6 +436,7 @@ def run_config4(args, torch, dist, rank, world):
                 merge(il)
 
     ms = time_events(torch, s, step, max(3, args.steps), args.warmup, barrier)
+    ms_split = time_events(torch, s, step_split, max(3, args.steps), args.warmup, barrier)
     ms_nccl = time_events(torch, s, step_nccl, max(3, args.steps), args.warmup, barrier)
     # per-phase device times over the same number of layer calls
     with torch.cuda.stream(s):
@@ -453,16 +464,16 @@ def run_config4(args, torch, dist, rank, world):
         a, b = out[0].cpu().numpy().reshape(rows, D).astype(np.float64), wout.cpu().numpy().reshape(rows, D).astype(np.float64)
         check_err = float((np.linalg.norm(a - b, axis=1) / np.linalg.norm(b, axis=1)).max())
         whole.free()
-    t = torch.tensor([ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, 0.0 if p2p_equal else 1.0],
+    t = torch.tensor([ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, 0.0 if p2p_equal else 1.0, ms_split],
                      device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, p2p_diff = [float(x) for x in t]
+    ms, ms_partial, ms_exchange, ms_merge, ms_seal, ms_nccl, ms_p2p, p2p_diff, ms_split = [float(x) for x in t]
     sm.free()
     B_global = SINK + c4["groups"] * G
     n_global = B_global + c4["tail"]
     return dict(ms=ms / nl, ms_partial=ms_partial / nl, ms_exchange=ms_exchange / nl, ms_merge=ms_merge / nl,
-                ms_nccl=ms_nccl / nl, ms_p2p=ms_p2p / nl, p2p_equals_nccl=p2p_diff == 0.0,
+                ms_nccl=ms_nccl / nl, ms_p2p=ms_p2p / nl, p2p_equals_nccl=p2p_diff == 0.0, ms_split=ms_split / nl,
                 bytes=attn_bytes_per_call(B_global, n_global), n_ctx=n_global, layers=nl, exchange=rows * (D + 2) * 4,
                 groups_per_rank=g1 - g0, write_s=write_s, seal_ms=ms_seal, tokens_sealed=tokens_sealed,
                 merged_vs_whole=check_err)
@@ -997,9 +1008,11 @@ def main():
             "attn_frac_of_all_ranks": cfg4["bytes"] / (cfg4["ms"] * 1e-3) / 1e9 / (peak * world),
             "phases_us_per_call": {"partial": cfg4["ms_partial"] * 1e3, "peer_exchange": cfg4["ms_p2p"] * 1e3,
                                    "nccl_all_gather": cfg4["ms_exchange"] * 1e3, "nccl_merge": cfg4["ms_merge"] * 1e3},
-            "nccl_path_us_per_call": cfg4["ms_nccl"] * 1e3, "peer_exchange_equals_nccl_path": cfg4["p2p_equals_nccl"],
-            "exchange": "per layer call: each rank stores its (m, l, o) triples into every peer's exchange buffer over "
-                        "NVLink (CUDA IPC mappings, plain stores) and merges all ranks' triples locally in rank order",
+            "nccl_path_us_per_call": cfg4["ms_nccl"] * 1e3, "split_exchange_path_us_per_call": cfg4["ms_split"] * 1e3,
+            "peer_exchange_equals_nccl_path": cfg4["p2p_equals_nccl"],
+            "exchange": "per layer call, one sjk_attend_partial_xchg: the call's merge kernel stores the rank's (m, l, o) "
+                        "triples into every rank's exchange buffer over NVLink (CUDA IPC mappings, plain stores), waits "
+                        "for the other ranks' and merges all of them in rank order",
             "bulk_seal": {"mtoks_per_gpu": cfg4["tokens_sealed"] / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "mtoks_all_gpus": cfg4["tokens_sealed"] * world / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "ms": cfg4["seal_ms"], "tokens_per_gpu": cfg4["tokens_sealed"],

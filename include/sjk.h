@@ -441,28 +441,40 @@ int sjk_seq_store(sj_kvarn_seq * s, uint32_t pos0, uint32_t n_pos, const float *
 int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * host_dst);
 
 /* ---- exchange of attention partials between GPUs over peer memory ----
- * For a sequence split by context slice over `world` GPUs (one process per GPU), sjk_attend_partial gives each rank
- * one (m, l, o[D]) triple per (query row, query head); these calls replace an all-gather of the triples plus
- * sjk_attend_merge by NVLink P2P stores into the other ranks' exchange buffers and a local merge. Each rank allocates
- * one exchange buffer (sjk_xchg_alloc, zeroed; its CUDA IPC handle, SJK_XCHG_HANDLE_BYTES, goes to the other ranks,
- * which map it with sjk_xchg_open). Per layer call, with an epoch the ranks count up alike from 1:
- * sjk_xchg_publish writes this rank's triples into slot `rank` of every rank's buffer (peers: HOST array of world
- * device addresses as this process sees them, peers[rank] = its own buffer) and raises its flags there;
- * sjk_xchg_merge waits (bounded by about 1 s) for every rank's flags in the local buffer and merges the slots in
- * rank order with sjk_attend_merge's kernel, so the output equals all-gather + sjk_attend_merge bit for bit. A wait
- * that runs out yields zeros and SJK_DEVICE_TIMEOUT in sjk_device_status(). Calls of consecutive epochs alternate
- * between two slot sets, so a rank may publish epoch e + 1 while others still merge epoch e. No TMA, no multicast:
- * plain stores and loads. No counterpart in the reference, whose attention runs on one device. */
+ * For a sequence split by context slice over `world` GPUs (one process per GPU), every rank attends over its own
+ * slice (one (m, l, o[D]) triple per (query row, query head)) and needs the merge of all ranks' triples. These calls
+ * replace an all-gather + sjk_attend_merge by NVLink stores into the other ranks' exchange buffers and a local merge,
+ * with the same arithmetic in the same rank order, so the output is the same bit for bit. No counterpart in the
+ * reference, whose attention runs on one device.
+ * Set-up: each rank allocates one exchange buffer of sjk_xchg_bytes(world, n_rows, D) bytes (sjk_xchg_alloc, zeroed),
+ * sends its CUDA IPC handle (SJK_XCHG_HANDLE_BYTES) to the other ranks and maps theirs (sjk_xchg_open); the
+ * sjk_xchg_peers it passes holds every rank's buffer as this process sees it (buf[rank] = its own). Every call carries
+ * an epoch that all ranks count up alike from 1, one per exchange; consecutive epochs use alternate slot sets, so a
+ * rank may publish epoch e + 1 while others still merge epoch e. A rank's wait for the others is bounded (about 1 s):
+ * a rank that never publishes makes the others write zeros and raise SJK_DEVICE_TIMEOUT in sjk_device_status().
+ * Plain stores and loads only: no TMA, no multicast. Buffers are freed (sjk_xchg_close, sjk_xchg_free) only after
+ * every rank's last exchange completed. */
 #define SJK_XCHG_MAX_WORLD   16
 #define SJK_XCHG_HANDLE_BYTES 64
+typedef struct sjk_xchg_peers {
+    void * buf[SJK_XCHG_MAX_WORLD];
+    int    world, rank;
+} sjk_xchg_peers;
 size_t sjk_xchg_bytes(int world, int n_rows, int D);
 int    sjk_xchg_alloc(size_t bytes, void ** buf, void * ipc_handle);
 int    sjk_xchg_free(void * buf);
 int    sjk_xchg_open(const void * ipc_handle, void ** peer_buf);
 int    sjk_xchg_close(void * peer_buf);
-int    sjk_xchg_publish(void * const * peers, int world, int rank, const float * part, int n_rows, int D, uint32_t epoch,
-                        sjk_stream st);
-int    sjk_xchg_merge(void * local_buf, int world, int n_rows, int D, uint32_t epoch, float * out, sjk_stream st);
+/* This rank's triples part[n_rows][D + 2] (DEVICE, e.g. from sjk_attend_partial) go to every rank; out[n_rows][D]
+ * (DEVICE) gets the merge of all ranks' triples in rank order. One launch. */
+int    sjk_xchg_exchange(const sjk_xchg_peers * x, const float * part, int n_rows, int D, uint32_t epoch, float * out,
+                         sjk_stream st);
+/* sjk_attend_partial with the exchange folded into the call's last kernel: the merge kernel that forms this rank's
+ * triples stores them into every rank's buffer, waits for the others' and writes the merged output out[n_q * n_head][D]
+ * (the exchange shape: n_rows = n_q * n_head, D = head_dim). */
+int    sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, unsigned regions,
+                               const float * q, float scale, void * scratch, size_t scratch_bytes, const sjk_xchg_peers * x,
+                               uint32_t epoch, float * out, sjk_stream st);
 
 /* ---- seeded synthetic inputs of the benchmark configurations (DEVICE outputs) ----
  * Input generation for benchmarks and parity tests; no counterpart in the reference. K = X * s with X ~ N(0, 1)

@@ -221,6 +221,8 @@ class SliceModel:
                                             C.c_void_p(v.data_ptr()), 1, self.st), "store tail")
 
     def seal_layer(self, il):
+        """Seal layer il's body from the staging buffer; call it after write_layer(il) and before the next layer's
+        write_layer, which reuses the buffer."""
         lay = self.layers[il]
         sv = self.stage_view(il)
         sjk.check(self.L.sjk_seal_ring(C.byref(sv), C.c_void_p(lay.body), SINK, self.B, lay.cfg.iters, self.st),

@@ -14,6 +14,7 @@
 
 #include "sjk_common.cuh"
 #include "sjk_internal.h"
+#include "sjk_merge.cuh"
 #include "sjk_plan.cuh"
 
 namespace {
@@ -239,86 +240,46 @@ __global__ void __launch_bounds__(NT) attend_split_dyn_kernel(const AttnParams *
     split_body<D>(*pp);
 }
 
-// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m). Grid (query row x head, channel tiles of
-// 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
-constexpr int MERGE_SPLITS = 768;                     // >= the most splits a call can make (148 + 296 + 296)
-constexpr int MERGE_PRE = 24;                         // outputs per thread loaded ahead of the weights
+// out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m) (sjk_merge.cuh). Grid (query row x head, channel tiles
+// of 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
+using sjkm::MERGE_SPLITS;
+__device__ int sjk_xchg_dev_status;                   // SJK_DEVICE_TIMEOUT when an exchange wait ran out
 
 // part_out (optional): instead of out, write the combined partial (m, l, o[D]) of each row (o not normalized), the
 // form sjk_attend_partial returns
 // splits_dev (optional): read the split count from device memory (the descriptor-driven call's plan)
+// xchg (world > 0): the row's partial goes to every rank over peer memory instead, and out gets the merge of all
+// ranks' partials (sjk_attend_partial_xchg)
+template <bool XCHG>
 __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out,
-                                                           float * part_out, const int * splits_dev) {
-    extern __shared__ float wts[];                     // [splits] weights, then [4][64] partial sums
+                                                           float * part_out, const int * splits_dev,
+                                                           const __grid_constant__ sjkm::XchgArgs xchg) {
+    extern __shared__ float wts[];                     // [max(splits, ranks)] weights, then [4][64] partial sums
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     // launched as a programmatic dependent of the kernels that write the partials: wait until they completed
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (splits_dev) splits = *splits_dev;
-    // the outputs of the first MERGE_PRE splits of this thread's group go in flight with the (m, l) loads
-    const int dl = tid & 63, grp4 = tid >> 6;
-    const bool live = d0 + dl < D;
-    const float * src = part + (size_t) row * (D + 2) + 2 + d0 + (live ? dl : 0);
-    const size_t step = (size_t) n_rows * (D + 2);
-    float xo[MERGE_PRE];
-#pragma unroll
-    for (int k = 0; k < MERGE_PRE; ++k) {
-        const int i = grp4 + 4 * k;
-        xo[k] = i < splits ? src[(size_t) i * step] : 0.0f;
-    }
-    // one pass over (m, l) of the splits this thread owns (at most MERGE_SPLITS / 256)
-    float mi[MERGE_SPLITS / 256], li[MERGE_SPLITS / 256];
-#pragma unroll
-    for (int k = 0; k < MERGE_SPLITS / 256; ++k) {
-        const int i = tid + 256 * k;
-        mi[k] = -INFINITY; li[k] = 0.0f;
-        if (i < splits) {
-            const float2 ml = *reinterpret_cast<const float2 *>(part + ((size_t) i * n_rows + row) * (D + 2));
-            mi[k] = ml.x; li[k] = ml.y;
+    float m, t;
+    sjkm::merge_tile(part, splits, n_rows, D, row, d0, wts, s_red, m, t);
+    const float * acc = wts + splits;
+    if (XCHG) {
+        const float my_o = tid < 64 ? sjkm::acc_o(acc, tid) : 0.0f;
+        const bool ok = sjkm::xchg_publish_wait(xchg, n_rows, D, row, (int) blockIdx.y, m, t, my_o);
+        if (!ok) {
+            if (tid < 64 && d0 + tid < D) out[(size_t) row * D + d0 + tid] = 0.0f;
+            if (tid == 0) atomicOr(&sjk_xchg_dev_status, (int) SJK_DEVICE_TIMEOUT);
+            return;
         }
-    }
-    float m = fmaxf(fmaxf(mi[0], mi[1]), mi[2]);
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    if (lane == 0) s_red[warp] = m;
-    __syncthreads();
-    m = s_red[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, s_red[w]);
-    float den = 0.0f;
-#pragma unroll
-    for (int k = 0; k < MERGE_SPLITS / 256; ++k) {
-        const int i = tid + 256 * k;
-        if (i < splits) {
-            const float w = mi[k] == -INFINITY ? 0.0f : expf(mi[k] - m);
-            wts[i] = w;
-            den += li[k] * w;
-        }
-    }
-    for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
-    if (lane == 0) s_red[8 + warp] = den;
-    __syncthreads();
-    float t = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) t += s_red[8 + w];
-    const float s_inv = t == 0.0f ? 0.0f : 1.0f / t;
-    // 4 groups of 64 threads walk the splits in strides of 4; failed or empty splits carry weight 0 and zero
-    // outputs. The first MERGE_PRE splits of each group were loaded together with (m, l), before the barriers.
-    float o = 0.0f;
-#pragma unroll
-    for (int k = 0; k < MERGE_PRE; ++k) {
-        const int i = grp4 + 4 * k;
-        if (i < splits) o = fmaf(xo[k], wts[i], o);
-    }
-    for (int i = grp4 + 4 * MERGE_PRE; i < splits; i += 4) o = fmaf(src[(size_t) i * step], wts[i], o);
-    float * acc = wts + splits;
-    acc[grp4 * 64 + dl] = o;
-    __syncthreads();
-    if (part_out) {
-        if (tid < 64 && d0 + tid < D) part_out[(size_t) row * (D + 2) + 2 + d0 + tid] = (acc[tid] + acc[64 + tid]) + (acc[128 + tid] + acc[192 + tid]);
+        float m2, t2;
+        sjkm::merge_tile<true>(sjkm::xchg_slots(xchg, n_rows, D), xchg.world, n_rows, D, row, d0, wts, s_red, m2, t2);
+        sjkm::store_out(wts + xchg.world, t2, D, row, d0, out);
+    } else if (part_out) {
+        if (tid < 64 && d0 + tid < D) part_out[(size_t) row * (D + 2) + 2 + d0 + tid] = sjkm::acc_o(acc, tid);
         if (blockIdx.y == 0 && tid == 0) { part_out[(size_t) row * (D + 2)] = m; part_out[(size_t) row * (D + 2) + 1] = t; }
-    } else if (tid < 64 && d0 + tid < D) {
-        out[(size_t) row * D + d0 + tid] = ((acc[tid] + acc[64 + tid]) + (acc[128 + tid] + acc[192 + tid])) * s_inv;
+    } else {
+        sjkm::store_out(acc, t, D, row, d0, out);
     }
 }
 
@@ -388,19 +349,25 @@ int launch_split(const AttnParams & p, const AttnParams * dyn, int splits, int n
 // Programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them on the
 // device (griddepcontrol.wait), so the launch gap between the two kernels disappears. splits_dev: the split count
 // is read from device memory (shared memory sized for max_splits).
+// xchg (optional): exchange the rows' partials with the other ranks and write the merge of all of them to out.
 int launch_merge(const float * part, int splits, const int * splits_dev, int max_splits, int n_rows, int D, float * out,
-                 float * part_out, sjk_stream st) {
+                 float * part_out, sjk_stream st, const sjkm::XchgArgs * xchg = nullptr) {
+    sjkm::XchgArgs xa = {};
+    if (xchg) xa = *xchg;
+    const int n_w = splits_dev ? max_splits : splits;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64));
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t) ((splits_dev ? max_splits : splits) + 256) * sizeof(float);
+    cfg.dynamicSmemBytes = (size_t) ((n_w > xa.world ? n_w : xa.world) + 256) * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_merge_kernel, part, splits, n_rows, D, out, part_out, splits_dev)))
+    const cudaError_t e = xa.world > 0 ? cudaLaunchKernelEx(&cfg, attend_merge_kernel<true>, part, splits, n_rows, D, out, part_out, splits_dev, xa)
+                                       : cudaLaunchKernelEx(&cfg, attend_merge_kernel<false>, part, splits, n_rows, D, out, part_out, splits_dev, xa);
+    if (sjk_check(e))
         return SJK_ERR_DEVICE;
     return sjk_check_launch();
 }
@@ -409,7 +376,7 @@ int launch_merge(const float * part, int splits, const int * splits_dev, int max
 
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
                      const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
-                     unsigned regions, float * part_out) {
+                     unsigned regions, float * part_out, const sjk_xchg_peers * xchg, uint32_t epoch) {
     if (!v || !q || !(out || part_out) || n_q <= 0 || n_head <= 0 || n_kv <= 0 || kv_head0 < 0 || kv_head0 + n_kv > v->n_head_kv ||
         n_head % n_kv)
         return SJKVARN_ERR_ARG;
@@ -453,6 +420,12 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (d.splits_v1) {
         const int rc = launch_split(p, nullptr, d.splits_v1, n_kv, st);
         if (rc) return rc;
+    }
+    if (xchg) {
+        sjkm::XchgArgs xa = {};
+        xa.world = xchg->world; xa.rank = xchg->rank; xa.epoch = epoch;
+        for (int i = 0; i < xchg->world; ++i) xa.buf[i] = reinterpret_cast<uint8_t *>(xchg->buf[i]);
+        return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, nullptr, st, &xa);
     }
     return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, part_out, st);
 }
@@ -574,15 +547,39 @@ extern "C" int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, ui
                             regions, part_out);
 }
 
+// sjk_attend_partial whose partials go straight to every rank over peer memory: the merge kernel of the call stores
+// its rows' triples into every rank's exchange buffer, waits for every rank's and writes the merge of all of them to
+// out[n_q * n_head][D] - the all-gather + sjk_attend_merge of the same triples, in the call's own last kernel.
+extern "C" int sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                                       unsigned regions, const float * q, float scale, void * scratch, size_t scratch_bytes,
+                                       const sjk_xchg_peers * x, uint32_t epoch, float * out, sjk_stream st) {
+    if (!v || !out || !x || (regions & ~(unsigned) SJK_REGION_ALL) || epoch == 0 || x->world <= 0 ||
+        x->world > SJK_XCHG_MAX_WORLD || x->rank < 0 || x->rank >= x->world)
+        return SJKVARN_ERR_ARG;
+    for (int i = 0; i < x->world; ++i)
+        if (!x->buf[i] || ((uintptr_t) x->buf[i] & 255)) return SJKVARN_ERR_ARG;
+    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st,
+                            regions, nullptr, x, epoch);
+}
+
 // out[n_rows][D] from n_parts partial sets parts[n_parts][n_rows][D + 2], combined in index order
 extern "C" int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st) {
     if (!parts || !out || n_parts <= 0 || n_rows <= 0 || D <= 0 || n_parts > MERGE_SPLITS) return SJKVARN_ERR_ARG;
-    attend_merge_kernel<<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
-        parts, n_parts, n_rows, D, out, nullptr, nullptr);
+    attend_merge_kernel<false><<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
+        parts, n_parts, n_rows, D, out, nullptr, nullptr, sjkm::XchgArgs{});
     return sjk_check_launch();
 }
 
 SJK_DESC_STATUS_READER(attend_desc_status_take)
+
+namespace {
+int attend_xchg_status_take(void) {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, sjk_xchg_dev_status, sizeof v) != cudaSuccess) return -1;
+    if (cudaMemcpyToSymbol(sjk_xchg_dev_status, &zero, sizeof zero) != cudaSuccess) return -1;
+    return v;
+}
+}  // namespace
 
 // status words of every kernel with bounded waits (SJK_DEVICE_TIMEOUT) and of the descriptor-driven calls
 // (SJK_DEVICE_DESC) since the last call
@@ -590,9 +587,9 @@ extern "C" int sjk_device_status(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take(), c = sjk_tc_trellis_status_take();
     const int d = attend_desc_status_take(), e = sjk_seal_desc_status_take(), f = sjk_stage_desc_status_take();
-    const int x = sjk_xchg_status_take();
-    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0 || x < 0) return -1;
-    return a | b | c | d | e | f | x;
+    const int x = sjk_xchg_status_take(), y = attend_xchg_status_take();
+    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0 || x < 0 || y < 0) return -1;
+    return a | b | c | d | e | f | x | y;
 }
 
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,

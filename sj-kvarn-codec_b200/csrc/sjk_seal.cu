@@ -56,11 +56,12 @@ struct Carve {
     static constexpr int R = IS_V ? G : D;
     static constexpr int C = IS_V ? D : G;
     static constexpr int LD = C + 1;                                 // padded row stride of cur
+    static constexpr int LM = C + 2;                                 // padded row stride of M (fp16): rows 1 bank apart
     static constexpr int MX = R > C ? R : C;
     static constexpr size_t cur = 0;
     static constexpr size_t cur_bytes = ((size_t) R * LD * 4 + 15) / 16 * 16;
     static constexpr size_t regA = cur + cur_bytes;                  // M fp16 / Viterbi back-pointers
-    static constexpr size_t regA_bytes = (size_t) R * C * 2 > 65536 ? (size_t) R * C * 2 : 65536;
+    static constexpr size_t regA_bytes = ((size_t) R * LM * 2 > 65536 ? (size_t) R * LM * 2 : 65536) + 15 & ~(size_t) 15;
     static constexpr size_t regB = regA + regA_bytes;                // partials / trellis payload + M rows
     static constexpr size_t regB_bytes = 16384;
     static constexpr size_t srow = regB + regB_bytes;                // float[R]
@@ -118,7 +119,7 @@ SJK_DEV bool load_input(const SealParams & p, int rec_local, uint16_t * M, const
             }
         }
         const int r = IS_V ? t : d, c = IS_V ? d : t;
-        M[r * CV::C + c] = hv;
+        M[r * CV::LM + c] = hv;
         nonfinite |= (hv & 0x7C00u) == 0x7C00u;
     }
     return nonfinite;
@@ -150,42 +151,79 @@ SJK_DEV void rescale(float * cur, const uint16_t * M, const float * srow, const 
         const float sc = scol[c], rc = rcol[c];
 #pragma unroll 4
         for (int r = threadIdx.x / C; r < R; r += RSTEP) {
-            const float m = __half2float(__ushort_as_half(M[r * C + c]));
+            const float m = __half2float(__ushort_as_half(M[r * CV::LM + c]));
             const float2 rs = sr2[r];                                 // (s_row, 1 / s_row): one broadcast load
             cur[r * CV::LD + c] = div_by_rcp(div_by_rcp(m, sc, rc), rs.x, rs.y);
         }
     } else {
         for (int r = threadIdx.x / C; r < R; r += RSTEP)
-            cur[r * CV::LD + c] = __fdiv_rn(__fdiv_rn(sjk_h2f(M[r * C + c]), scol[c]), srow[r]);
+            cur[r * CV::LD + c] = __fdiv_rn(__fdiv_rn(sjk_h2f(M[r * CV::LM + c]), scol[c]), srow[r]);
     }
 }
 
 // One balancing half-step over columns (COLS = true: std of each column over the R rows) or rows.
 // Chunked double sums (8 contiguous chunks), fixed pairwise combine, fma second pass (sj_kvarn.h:939-978).
-template <int D, bool IS_V, bool COLS>
-SJK_DEV void balance_half(const float * cur, double * part, double * mean, double * lacc, float * sacc, float * racc,
-                          float2 * sr2) {
+// The half-step with the rescale fused into its first pass: each thread forms the balanced values of its
+// chunk(s), cur = (M / s_col) / s_row with the current scales (the rescale's own divides, in its order), sums them as
+// it stores them, and its second pass reads back only the values it stored itself (no barrier between the two). The
+// next half-step forms its values from M again with the updated scales, so the separate rescale sweeps, their reads
+// of the tile and their barriers disappear. Same arithmetic, same order, same results.
+template <int D, bool IS_V, bool COLS, bool FIN>
+SJK_DEV void balance_half_m(float * cur, const uint16_t * M, const float * srow, const float * scol, const float * rcol,
+                            const float2 * srr, double * part, double * mean, double * lacc, float * sacc, float * racc,
+                            float2 * sr2) {
     using CV = Carve<D, IS_V>;
     constexpr int N = COLS ? CV::C : CV::R;        // number of vectors
     constexpr int L = COLS ? CV::R : CV::C;        // length of each vector
     constexpr int CH = L / 8;                      // chunk length
-    constexpr int STR = COLS ? CV::LD : 1;         // element stride inside a vector
-    constexpr int VSTR = COLS ? 1 : CV::LD;        // stride between vectors
-    // pass 1: chunk sums
-    for (int task = threadIdx.x; task < N * 8; task += NT) {
-        const int v = task % N, ch = task / N;
-        const float * x = cur + v * VSTR + ch * CH * STR;
+    constexpr int TPT = N * 8 / NT;                // chunks per thread
+    static_assert(N * 8 % NT == 0 && TPT * CH * NT == CV::R * CV::C, "every thread takes its share of the tile");
+#pragma unroll
+    for (int k = 0; k < TPT; ++k) {
+        const int task = threadIdx.x + k * NT, v = task % N, ch = task / N;
         double s = 0.0;
+        if (COLS) {
+            const int c = v;
+            const float sc = scol[c], rc = rcol[c];
 #pragma unroll 8
-        for (int i = 0; i < CH; ++i) s = __dadd_rn(s, (double) x[i * STR]);
+            for (int i = 0; i < CH; ++i) {
+                const int r = ch * CH + i;
+                const float m = __half2float(__ushort_as_half(M[r * CV::LM + c]));
+                const float2 rs = srr[r];
+                const float x = FIN ? div_by_rcp(div_by_rcp(m, sc, rc), rs.x, rs.y) : __fdiv_rn(__fdiv_rn(m, sc), rs.x);
+                cur[r * CV::LD + c] = x;
+                s = __dadd_rn(s, (double) x);
+            }
+        } else {
+            const int r = v;
+            const float2 rs = srr[r];
+            const uint32_t * mrow = reinterpret_cast<const uint32_t *>(M + r * CV::LM + ch * CH);   // 4-byte aligned
+#pragma unroll 4
+            for (int i = 0; i < CH; i += 2) {
+                const uint32_t w = mrow[i / 2];
+                const float m0 = __half2float(__ushort_as_half((unsigned short) (w & 0xFFFFu)));
+                const float m1 = __half2float(__ushort_as_half((unsigned short) (w >> 16)));
+                const int c0 = ch * CH + i, c1 = c0 + 1;
+                const float x0 = FIN ? div_by_rcp(div_by_rcp(m0, scol[c0], rcol[c0]), rs.x, rs.y)
+                                     : __fdiv_rn(__fdiv_rn(m0, scol[c0]), rs.x);
+                const float x1 = FIN ? div_by_rcp(div_by_rcp(m1, scol[c1], rcol[c1]), rs.x, rs.y)
+                                     : __fdiv_rn(__fdiv_rn(m1, scol[c1]), rs.x);
+                cur[r * CV::LD + c0] = x0;
+                cur[r * CV::LD + c1] = x1;
+                s = __dadd_rn(s, (double) x0);
+                s = __dadd_rn(s, (double) x1);
+            }
+        }
         part[ch * N + v] = s;
     }
     __syncthreads();
     for (int v = threadIdx.x; v < N; v += NT) mean[v] = __ddiv_rn(tree8(part + v, N), (double) L);
     __syncthreads();
-    // pass 2: chunk sums of squared deviations with an explicit fma
-    for (int task = threadIdx.x; task < N * 8; task += NT) {
-        const int v = task % N, ch = task / N;
+    constexpr int STR = COLS ? CV::LD : 1;         // element stride inside a vector
+    constexpr int VSTR = COLS ? 1 : CV::LD;        // stride between vectors
+#pragma unroll
+    for (int k = 0; k < TPT; ++k) {
+        const int task = threadIdx.x + k * NT, v = task % N, ch = task / N;
         const float * x = cur + v * VSTR + ch * CH * STR;
         const double mu = mean[v];
         double s = 0.0;
@@ -417,18 +455,21 @@ SJK_DEV void seal_side(const SealParams & p, uint8_t * smem) {
     for (int r = threadIdx.x; r < R; r += NT) { srow[r] = 1.0f; rrow[r] = 1.0f; sr2[r] = make_float2(1.0f, 1.0f); lrow[r] = 0.0; }
     __syncthreads();
     const bool finite = !__syncthreads_or(load_input<D, IS_V>(p, rec_local, M, cent, rowoff));
+
+    // ---- log-domain variance balancing, exactly `iters` column-then-row passes (sj_kvarn.h:989-1012); every
+    // half-step forms the balanced tile from M with the current scales (the reference's rescale after each
+    // half-step), and the tile itself is stored once, after the last one ----
+    for (int it = 0; it < p.iters; ++it) {
+        if (finite) {
+            balance_half_m<D, IS_V, true, true>(cur, M, srow, scol, rcol, sr2, part, mean, lcol, scol, rcol, sr2);
+            balance_half_m<D, IS_V, false, true>(cur, M, srow, scol, rcol, sr2, part, mean, lrow, srow, rrow, sr2);
+        } else {
+            balance_half_m<D, IS_V, true, false>(cur, M, srow, scol, rcol, sr2, part, mean, lcol, scol, rcol, sr2);
+            balance_half_m<D, IS_V, false, false>(cur, M, srow, scol, rcol, sr2, part, mean, lrow, srow, rrow, sr2);
+        }
+    }
     rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
     __syncthreads();
-
-    // ---- log-domain variance balancing, exactly `iters` column-then-row passes (sj_kvarn.h:989-1012) ----
-    for (int it = 0; it < p.iters; ++it) {
-        balance_half<D, IS_V, true>(cur, part, mean, lcol, scol, rcol, sr2);
-        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
-        __syncthreads();
-        balance_half<D, IS_V, false>(cur, part, mean, lrow, srow, rrow, sr2);
-        rescale<D, IS_V>(cur, M, srow, scol, rrow, rcol, sr2, finite);
-        __syncthreads();
-    }
 
     // ---- per-row asymmetric range (sj_kvarn.h:1120-1128) ----
     const int bits = IS_V ? l.bits_v : l.bits_k;

@@ -51,6 +51,13 @@ class View(C.Structure):
                 ("cap", u32), ("stage_bytes", C.c_size_t), ("sink", vp), ("ring", vp), ("body", vp), ("blocks", vp)]
 
 
+XCHG_MAX_WORLD = 16
+
+
+class XchgPeers(C.Structure):
+    _fields_ = [("buf", vp * XCHG_MAX_WORLD), ("world", C.c_int), ("rank", C.c_int)]
+
+
 class StateInfo(C.Structure):
     _fields_ = [("state_version", u32), ("format_version", u32), ("cfg", Config), ("rotation", u32),
                 ("rotation_n", u32), ("codebook_id", C.c_uint64), ("n_layers", C.c_int), ("n", u32), ("B", u32),
@@ -161,8 +168,9 @@ SIGNATURES = {
     "sjk_xchg_free": (C.c_int, [vp]),
     "sjk_xchg_open": (C.c_int, [vp, P(vp)]),
     "sjk_xchg_close": (C.c_int, [vp]),
-    "sjk_xchg_publish": (C.c_int, [P(vp), C.c_int, C.c_int, vp, C.c_int, C.c_int, u32, vp]),
-    "sjk_xchg_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, u32, vp, vp]),
+    "sjk_xchg_exchange": (C.c_int, [P(XchgPeers), vp, C.c_int, C.c_int, u32, vp, vp]),
+    "sjk_attend_partial_xchg": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, C.c_uint, vp, C.c_float, vp, C.c_size_t,
+                                          P(XchgPeers), u32, vp, vp]),
     # seeded synthetic inputs
     "sjk_synth_scales": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp]),
     "sjk_synth_kv": (C.c_int, [C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_int, vp, u32, u32, vp, vp, vp]),

@@ -85,9 +85,9 @@ def lpt_assign(costs, world):
 
 class PeerExchange:
     """The per-layer exchange of config 4's partial triples over peer memory (sjk_xchg_*): every rank allocates one
-    exchange buffer, the ranks swap its CUDA IPC handle once through the process group, and each layer call publishes
-    the rank's triples into every peer's buffer with NVLink stores and merges the ranks' triples locally in rank
-    order. The output equals an all-gather + sjk_attend_merge of the same triples bit for bit."""
+    exchange buffer, the ranks swap its CUDA IPC handle once through the process group, and each layer call stores the
+    rank's triples into every rank's buffer with NVLink stores and merges all ranks' triples locally in rank order.
+    The output equals an all-gather + sjk_attend_merge of the same triples bit for bit."""
 
     def __init__(self, dist, rank, world, n_rows, D):
         import ctypes as C
@@ -105,16 +105,17 @@ class PeerExchange:
         if dist is not None and world > 1:
             handles = [None] * world
             dist.all_gather_object(handles, bytes(handle))
-        self.peers = (C.c_void_p * world)()
+        self.peers = sjk.XchgPeers()
+        self.peers.world, self.peers.rank = world, rank
         self.opened = []
         for r in range(world):
             if r == rank:
-                self.peers[r] = self.buf.value
+                self.peers.buf[r] = self.buf.value
             else:
                 p = C.c_void_p()
                 hb = (C.c_uint8 * 64).from_buffer_copy(handles[r])
                 sjk.check(self.L.sjk_xchg_open(hb, C.byref(p)), "xchg_open")
-                self.peers[r] = p.value
+                self.peers.buf[r] = p.value
                 self.opened.append(p)
         self.dist = dist
         self.epoch = 0
@@ -123,10 +124,16 @@ class PeerExchange:
         """part: this rank's [n_rows][D + 2] triples (device); out: [n_rows][D] merged output (device)."""
         C = self.C
         self.epoch += 1
-        self.sjk.check(self.L.sjk_xchg_publish(self.peers, self.world, self.rank, C.c_void_p(part.data_ptr()), self.n_rows,
-                                               self.D, self.epoch, stream), "xchg_publish")
-        self.sjk.check(self.L.sjk_xchg_merge(self.buf, self.world, self.n_rows, self.D, self.epoch,
-                                             C.c_void_p(out.data_ptr()), stream), "xchg_merge")
+        self.sjk.check(self.L.sjk_xchg_exchange(C.byref(self.peers), C.c_void_p(part.data_ptr()), self.n_rows, self.D,
+                                                self.epoch, C.c_void_p(out.data_ptr()), stream), "xchg_exchange")
+
+    def attend(self, view, B, N, qpos0, n_q, n_head, regions, q_ptr, scale, scratch, need, out_ptr, stream):
+        """sjk_attend_partial_xchg: this rank's partial attention with the exchange and merge in its last kernel."""
+        C = self.C
+        self.epoch += 1
+        self.sjk.check(self.L.sjk_attend_partial_xchg(C.byref(view), B, N, qpos0, n_q, n_head, regions, q_ptr, scale,
+                                                      C.c_void_p(scratch.data_ptr()), need, C.byref(self.peers), self.epoch,
+                                                      out_ptr, stream), "attend_partial_xchg")
 
     def close(self):
         """Collective: every rank calls it once all its exchanges have completed on the device."""

@@ -111,3 +111,36 @@ def test_two_rank_exchange_matches_all_gather(L):
             if p.is_alive():
                 p.kill()
     assert res == {0: ([], 0), 1: ([], 0)}, res
+
+
+def test_single_rank_fused_partial_exchange(L):
+    """sjk_attend_partial_xchg (the exchange folded into the call's merge kernel) equals sjk_attend_partial followed by
+    sjk_attend_merge of the one partial, bit for bit, on a 4/4 cache (tensor-core body with the staged rows)."""
+    import slices
+    T = gu.torch()
+    import configs
+    sm = configs.SliceModel(0, 64, sink=True, tail=700, n_layers=1)
+    sm.build()
+    v = sjk.view_of(sm.layers[0])
+    n_q, n_head = 4, 16
+    syn = configs.DeviceSynth(4, 1)
+    q = syn.queries(0, n_q)
+    sjk.check(L.sjk_hadamard(gu.ptr(q), n_q * n_head, 256, None))
+    need = L.sjk_attend_scratch_bytes(C.byref(v), sm.N, n_q, n_head)
+    scratch = T.empty(int(need), dtype=T.uint8, device="cuda")
+    part = T.empty((n_q * n_head, 258), dtype=T.float32, device="cuda")
+    ref = T.empty((n_q * n_head, 256), dtype=T.float32, device="cuda")
+    ex = slices.PeerExchange(None, 0, 1, n_q * n_head, 256)
+    try:
+        for call in range(3):
+            qpos0 = sm.N - n_q - call
+            sjk.check(L.sjk_attend_partial(C.byref(v), sm.B, sm.N, qpos0, n_q, n_head, 7, gu.ptr(q), np.float32(1 / 16),
+                                           gu.ptr(part), gu.ptr(scratch), need, None))
+            sjk.check(L.sjk_attend_merge(gu.ptr(part), 1, n_q * n_head, 256, gu.ptr(ref), None))
+            out = T.empty_like(ref)
+            ex.attend(v, sm.B, sm.N, qpos0, n_q, n_head, 7, gu.ptr(q), np.float32(1 / 16), scratch, need, gu.ptr(out), None)
+            assert np.array_equal(gu.host(out, np.uint32), gu.host(ref, np.uint32)), call
+        assert L.sjk_device_status() == 0
+    finally:
+        ex.close()
+        sm.free()
