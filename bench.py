@@ -886,6 +886,8 @@ def main():
                     help="sequences of the config-3 pool (the first N of its 64; fewer only for small profiling runs)")
     ap.add_argument("--config3-steps", type=int, default=128, help="timed decode steps of config 3 (at least --steps)")
     ap.add_argument("--config4-layers", type=int, default=16, help="layers of the config-4 sequence")
+    ap.add_argument("--only", choices=["seal", "seal2", "config2", "config3"], default=None,
+                    help="run one section alone on one GPU and print its numbers (for profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -910,6 +912,20 @@ def main():
         import torch.distributed as td
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
         dist = td
+    if args.only:
+        # one section alone (profiling): config 0's or config 2's seal, config 2's attention, or a config-3 pool
+        if args.only == "seal":
+            r = run_seal0(args, torch)
+        elif args.only == "seal2":
+            r = run_seal0(args, torch, bits=(3, 2), heavy=True, seed=2)
+        elif args.only == "config2":
+            r = run_config2(args, torch)
+            r.pop("out0", None)
+            r["seal"] = {k: r["seal"][k] for k in ("ms", "records")}
+        else:
+            r = run_config3(args, torch, None, 0, 1)
+        print(json.dumps({"only": args.only, **{k: v for k, v in r.items() if not hasattr(v, "shape")}}), flush=True)
+        return
     res = run_config1(args, torch, dist, local_rank)
     cfg4 = None if args.no_config4 else run_config4(args, torch, dist, rank, world)
     cfg3 = None if args.no_config3 else run_config3(args, torch, dist, rank, world)
