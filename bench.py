@@ -321,7 +321,7 @@ def run_config2(args, torch):
     s = torch.cuda.Stream()
     st = C.c_void_p(s.cuda_stream)
     t0 = time.time()
-    m = configs.build_config2(stream=st, layers=configs.CFG1["layers"])
+    m = configs.build_config2(stream=st, layers=args.config2_layers)
     torch.cuda.synchronize()
     build_s = time.time() - t0
     a = AttnStep(torch, m, configs.CFG2["n_q"], s, st)
@@ -886,6 +886,7 @@ def main():
                     help="sequences of the config-3 pool (the first N of its 64; fewer only for small profiling runs)")
     ap.add_argument("--config3-steps", type=int, default=128, help="timed decode steps of config 3 (at least --steps)")
     ap.add_argument("--config4-layers", type=int, default=16, help="layers of the config-4 sequence")
+    ap.add_argument("--config2-layers", type=int, default=16, help="layers of the config-2 model (fewer only for profiling)")
     ap.add_argument("--only", choices=["seal", "seal2", "config2", "config3"], default=None,
                     help="run one section alone on one GPU and print its numbers (for profiling captures)")
     args = ap.parse_args()
