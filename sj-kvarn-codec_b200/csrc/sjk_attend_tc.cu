@@ -100,7 +100,8 @@ enum : uint32_t {                                             // offsets in floa
     F_RZ = 544,        // [3][2][4][8]  row sums of p Vzero (slot g % 3)
     F_LSUM = 736,      // [16]          running sums of p
     F_OK = 752,        // [4]           per role: all its waits completed (unpack, softmax, issuer)
-    F_END = 768
+    F_BC = 768,        // [8][16]       per softmax warp: mnew and 2^ev of its 8 rows
+    F_END = 896
 };
 constexpr uint32_t OFF_BAR = OFF_F + F_END * 4;
 enum : uint32_t {                                             // mbarrier indices
@@ -769,11 +770,12 @@ SJK_DEV void body_tc_body(const TcParams & p) {
                         F[F_ALPHA + 16 * s3 + r] = mn == -INFINITY ? 1.0f : ex2(mold - mn);
                         F[F_VINV + 16 * s3 + r] = pow2f(-ev);
                     }
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        mnew[k] = __shfl_sync(0xFFFFFFFFu, mn, k);
-                        vscl[k] = __shfl_sync(0xFFFFFFFFu, vs, k);
-                    }
+                    float * bc = F + F_BC + 16 * sw;
+                    __syncwarp();
+                    if (lane < 8) { bc[lane] = mn; bc[8 + lane] = vs; }
+                    __syncwarp();
+                    ld8(bc, mnew);
+                    ld8(bc + 8, vscl);
                 }
                 // ---- weights, B_V = three s8 digits of round(P' 2^ev), row sums ----
                 {

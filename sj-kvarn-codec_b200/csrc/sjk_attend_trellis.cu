@@ -257,10 +257,6 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u));
 }
-// global -> L2 prefetch of `bytes` (multiple of 16) at a 16-byte aligned address
-__device__ __forceinline__ void prefetch_l2(const void * src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 
 // R: query rows per KV head the kernel computes (8 or 16, padded; the MMA N is 2 R)
 template <int BK, int BV, int R>
@@ -541,7 +537,7 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
         int last_commit = -1;                                   // barrier index and parity of the last commit
         uint32_t last_parity = 0;
         auto prefetch_to = [&](uint32_t upto) {
-            for (; np < n && np < upto; ++np, pc.next(p)) prefetch_l2(rec_ptr(p, pc, blk_of(p, pc)), rb);
+            for (; np < n && np < upto; ++np, pc.next(p)) tc::prefetch_l2(rec_ptr(p, pc, blk_of(p, pc)), rb);
         };
         auto mma_v = [&](uint32_t e) -> bool {
             if (!wait_bar(&bars[B_AZFULL + (e & 1u)], (e >> 1) & 1u, abort)) return false;

@@ -194,6 +194,16 @@ __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t 
                  : "memory");
 }
 
+// global -> L2 prefetch of `bytes` (a multiple of 16) at a 16-byte aligned address
+__device__ __forceinline__ void prefetch_l2(const void * src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// the same for any byte range: widened to 16-byte boundaries
+__device__ __forceinline__ void prefetch_l2_span(const void * src, uint32_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(src), a0 = a & ~(uintptr_t) 15, a1 = (a + bytes + 15) & ~(uintptr_t) 15;
+    prefetch_l2(reinterpret_cast<const void *>(a0), (uint32_t) (a1 - a0));
+}
+
 // asynchronous global -> shared copies of 4 / 16 bytes; src_bytes = 0 writes zeros (src is not read)
 __device__ __forceinline__ void cp_async4(void * dst, const void * src, uint32_t src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
