@@ -341,8 +341,8 @@ def run_config2(args, torch):
 
 def run_config4(args, torch, dist, rank, world):
     """Config 4: one 1,048,576-token sequence (8,192 groups per KV head and layer + 128 sink + 4,096 tail, seed 4)
-    sliced by context: rank r holds groups [8192 r / W, 8192 (r + 1) / W) of every layer (rank 0 also the sink, the
-    last rank the tail). Bulk seal: each layer's slice is staged into one staging buffer in the ring layout and
+    sliced by context: rank r holds a contiguous range of the 8,192 groups of every layer (rank 0 also the sink, the
+    last rank the tail), balanced by attention cost (slices.group_range: a chunk of staged rows weighs 4.5 groups). Bulk seal: each layer's slice is staged into one staging buffer in the ring layout and
     sealed in one launch (timed: Mtok/s per GPU). Attention per layer call: sjk_attend_partial on every rank, then the
     (m, l, o) triples go to every rank over peer memory (slices.PeerExchange: NVLink stores, local merge in rank order);
     the NCCL all-gather + sjk_attend_merge path is timed beside it, and the phases separately. With
@@ -354,7 +354,7 @@ def run_config4(args, torch, dist, rank, world):
     c4 = configs.CFG4
     s = torch.cuda.Stream()
     st = C.c_void_p(s.cuda_stream)
-    g0, g1 = slices.group_range(rank, world, c4["groups"])
+    g0, g1 = slices.group_range(rank, world, c4["groups"], sink_chunks=(SINK + G - 1) // G, tail_chunks=c4["tail"] // G)
     t0 = time.time()
     sm = configs.SliceModel(g0, g1, sink=(rank == 0), tail=c4["tail"] if rank == world - 1 else 0,
                             n_layers=args.config4_layers, stream=st)

@@ -8,9 +8,10 @@
 //
 // Exchange over peer memory: rank r's CTA (row, tile) stores its tile of the rank's triple (m, l, o[64]) into slot
 // [parity][r][row] of every rank's exchange buffer (plain stores through CUDA IPC mappings of the other GPUs'
-// buffers; no TMA, no multicast), fences at system scope, raises flag [parity][r][row][tile] = epoch in each buffer,
-// then waits (bounded) until the flags [parity][src][row][tile] of its own buffer all hold the epoch and merges the
-// world slots of its (row, tile) in rank order - the all-gather + merge of the same triples, in one kernel.
+// buffers; no TMA, no multicast), raises flag [parity][r][row][tile] = epoch in each buffer with a release store at
+// system scope, then waits (bounded) until the flags [parity][src][row][tile] of its own buffer all hold the epoch
+// and merges the world slots of its (row, tile) in rank order - the all-gather + merge of the same triples, in one
+// kernel.
 // Exchange buffer: flags u32 [2][SJK_XCHG_MAX_WORLD][n_rows][tiles] (rounded up to 256 bytes), then slots
 // float [2][world][n_rows][D + 2]. Consecutive epochs alternate parities; a rank publishes epoch e + 2 only after its
 // merge of e + 1 saw every rank's flags of e + 1, raised after those ranks' merges of e completed (stream order), so
@@ -145,7 +146,8 @@ __device__ __forceinline__ bool xchg_publish_wait(const XchgArgs & x, int n_rows
         if (tid < 64 && d0 + tid < D) slot[2 + d0 + tid] = my_o;
         if (tid == 64) { slot[0] = m; slot[1] = t; }          // every tile's CTA writes the row's (m, l): same values
     }
-    __threadfence_system();
+    // the CTA barrier orders every thread's slot stores before the flag stores below, and a release at system scope
+    // is cumulative: it makes the stores it is ordered after visible to a peer that acquires the flag
     __syncthreads();
     const size_t fidx_src = (((size_t) par * SJK_XCHG_MAX_WORLD + x.rank) * n_rows + row) * tiles + tile;
     if (tid < x.world) {

@@ -18,9 +18,28 @@ import numpy as np
 SJK_REGION_SINK, SJK_REGION_BODY, SJK_REGION_RING = 1, 2, 4
 
 
-def group_range(rank, world, n_groups):
-    """Contiguous, balanced range [g0, g1) of the sealed groups owned by `rank`."""
-    return n_groups * rank // world, n_groups * (rank + 1) // world
+# attention time of one 128-position chunk of staged rows (sink or staging ring) in units of one sealed record of
+# the same KV head: the tensor-core body kernel decodes a tq6_0 chunk in about 4.5 record times
+CHUNK_WEIGHT = 4.5
+
+
+def group_range(rank, world, n_groups, sink_chunks=0, tail_chunks=0, chunk_weight=CHUNK_WEIGHT):
+    """Contiguous range [g0, g1) of the sealed groups owned by `rank`, balanced by attention cost: rank 0 also
+    attends over `sink_chunks` chunks of sink rows and the last rank over `tail_chunks` chunks of the staging ring,
+    each costing `chunk_weight` groups, so those ranks get correspondingly fewer groups (with no sink or tail:
+    n_groups / world each, to within one group)."""
+    total = n_groups + chunk_weight * (sink_chunks + tail_chunks)
+
+    def bound(r):                                   # first group of rank r
+        if r <= 0:
+            return 0
+        if r >= world:
+            return n_groups
+        b = int(np.floor(total * r / world - chunk_weight * sink_chunks + 0.5)) if (sink_chunks or tail_chunks) \
+            else n_groups * r // world
+        return min(max(b, 0), n_groups)
+
+    return bound(rank), bound(rank + 1)
 
 
 def regions(rank, world):

@@ -85,6 +85,14 @@ def test_group_ranges_and_regions(world):
     assert ranges[0][0] == 0 and ranges[-1][1] == n
     assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
     assert max(b - a for a, b in ranges) - min(b - a for a, b in ranges) <= 1
+    # weighted by cost (config 4: one sink chunk on rank 0, 32 ring chunks on the last rank)
+    w = slices.CHUNK_WEIGHT
+    wr = [slices.group_range(r, world, n, sink_chunks=1, tail_chunks=32) for r in range(world)]
+    assert wr[0][0] == 0 and wr[-1][1] == n and all(a[1] == b[0] for a, b in zip(wr, wr[1:]))
+    cost = [b - a + (w if r == 0 else 0) + (32 * w if r == world - 1 else 0) for r, (a, b) in enumerate(wr)]
+    assert max(cost) - min(cost) <= 1.0, cost
+    if world > 1:
+        assert wr[-1][1] - wr[-1][0] < n // world
     regs = [slices.regions(r, world) for r in range(world)]
     assert sum(1 for r in regs if r & slices.SJK_REGION_SINK) == 1 and regs[0] & slices.SJK_REGION_SINK
     assert sum(1 for r in regs if r & slices.SJK_REGION_RING) == 1 and regs[-1] & slices.SJK_REGION_RING
