@@ -148,17 +148,6 @@ __device__ __forceinline__ void warp_arrive(uint64_t * bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
-// The 6-bit codes of elements j0 .. j0 + 7 (j0 % 8 == 0) of a tq6_0 block (norm, qs[64] nibbles, qh[32] 2-bit
-// fields, sj_kvarn.h:1249-1284) as 8 bytes: nibble pairs spread with one PRMT, the high bits from a 256-entry
-// table qh_lut[y] = (2-bit fields of y) << 4 in bytes 0..3.
-__device__ __forceinline__ uint2 codes8(const uint8_t * blk, int j0, const uint32_t * qh_lut) {
-    const uint32_t qs = (uint32_t) *reinterpret_cast<const uint16_t *>(blk + 2 + j0 / 2) |
-                        ((uint32_t) *reinterpret_cast<const uint16_t *>(blk + 4 + j0 / 2) << 16);
-    const uint32_t qh = *reinterpret_cast<const uint16_t *>(blk + 66 + j0 / 4);
-    const uint32_t a = qs & 0x0F0F0F0Fu, b = (qs >> 4) & 0x0F0F0F0Fu;          // nibbles 0 2 4 6 / 1 3 5 7
-    return make_uint2(prmt(a, b, 0x5140u) | qh_lut[qh & 0xFFu], prmt(a, b, 0x7362u) | qh_lut[qh >> 8]);
-}
-
 SJK_DEV void body_tc_body(const TcParams & p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -378,7 +367,7 @@ SJK_DEV void body_tc_body(const TcParams & p) {
                     const uint8_t * blk = r0 + SJKVARN_TQ6_BLOCK_BYTES * b;
 #pragma unroll
                     for (int g = 0; g < 8; ++g) {
-                        const uint2 cw = codes8(blk, 64 * half + 8 * g, qh_lut);    // elements 64 half + 8 g ..
+                        const uint2 cw = tq6_codes8(blk, 64 * half + 8 * g, qh_lut);    // elements 64 half + 8 g ..
 #pragma unroll
                         for (int pp = 0; pp < 4; ++pp) {
                             const uint32_t w = pp < 2 ? cw.x : cw.y, sh = 16 * (pp & 1);
@@ -402,7 +391,7 @@ SJK_DEV void body_tc_body(const TcParams & p) {
                 for (int k = 0; k < 8; ++k) {
                     const int it = tid + 512 * k, t = it >> 5, gch = it & 31;          // channels 8 gch ..
                     const uint8_t * vblk = stg + t * D_STG_TQ6 + 2 * SJKVARN_TQ6_BLOCK_BYTES + SJKVARN_TQ6_BLOCK_BYTES * (gch >> 4);
-                    *reinterpret_cast<uint2 *>(vcodes + t * 256 + 8 * gch) = codes8(vblk, 8 * (gch & 15), qh_lut);
+                    *reinterpret_cast<uint2 *>(vcodes + t * 256 + 8 * gch) = tq6_codes8(vblk, 8 * (gch & 15), qh_lut);
                 }
             }
             ok = dense_wait();

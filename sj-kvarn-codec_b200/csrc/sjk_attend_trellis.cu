@@ -261,6 +261,9 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 // R: query rows per KV head the kernel computes (8 or 16, padded; the MMA N is 2 R)
 template <int BK, int BV, int R>
 SJK_DEV void trellis_ws_body(const TwParams & p) {
+    // a kernel launched as this one's programmatic dependent (the same call's dense kernel, or its merge) may start
+    // now on the SMs this grid leaves free
+    asm volatile("griddepcontrol.launch_dependents;");
     constexpr int RH = R / 2;                                   // B_K rows per thread (two row halves)
     constexpr int LPR = 32 / R, LPH = 32 / RH;                  // lanes per row after a warp_rows<R> / <RH>
     extern __shared__ __align__(128) uint8_t sm[];
@@ -706,12 +709,11 @@ size_t sjk_tc_trellis_params_bytes(void) { return sizeof(TwParams); }
 // One sequence: records [0, n_rec) of KV heads kv0 .. kv0 + n_kv - 1, each head split into `splits` contiguous
 // ranges; item (head, split) is CTA hl * splits + split and writes partial slot split0 + split.
 int sjk_tc_trellis_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head,
-                          int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
-                          sjk_stream st) {
-    const int splits = sjk_trellis_split_count(n_kv, n_rec);
+                          int kv0, int n_kv, const float * q, float scale, float * part, int split0, int splits,
+                          int * splits_out, sjk_stream st) {
     *splits_out = splits;
     if (splits <= 0) return 0;
-    if (split0 + splits > 0xFFFF) return SJK_ERR_UNSUPPORTED;
+    if (split0 + splits > 0xFFFF || splits * n_kv > MAX_CTAS) return SJK_ERR_UNSUPPORTED;
     static thread_local TwParams p;
     fill_single(p, *v, B < N ? B : N, n_rec, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, splits);
     return launch(p, st);

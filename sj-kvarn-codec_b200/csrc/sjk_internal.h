@@ -35,16 +35,19 @@ int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_re
 // tensor-core attention over the sealed body of a trellis layer (2- and 3-bit codes, sjk_attend_trellis.cu)
 int sjk_tc_trellis_supported(const sjk_view * v, int n_q, int grp);
 int sjk_tc_trellis_max_splits(int n_kv);
+// splits: per KV head, from the call's plan (sjk_plan_counts)
 int sjk_tc_trellis_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, uint32_t qpos0, int n_q, int n_head,
-                          int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
-                          sjk_stream st);
+                          int kv0, int n_kv, const float * q, float scale, float * part, int split0, int splits,
+                          int * splits_out, sjk_stream st);
 
 // tensor-core attention over the staged rows: the sink [0, S) and the staging ring [B, N) (sjk_attend_dense.cu)
 int sjk_tc_dense_supported(const sjk_view * v, int n_q, int grp);
 int sjk_tc_dense_splits(uint32_t n_chunks, int n_kv, int * chunks_per_split);
+// beside_tc: launched right after the same call's trellis kernel, as its programmatic dependent (side by side on the
+// SMs it leaves free; the kernel's completion still follows the trellis kernel's)
 int sjk_tc_dense_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv0, int n_kv,
                         const float * q, float scale, float * part, int split0, int splits, uint32_t n_sink_chunks,
-                        uint32_t n_chunks, int chunks_per_split, sjk_stream st);
+                        uint32_t n_chunks, int chunks_per_split, bool beside_tc, sjk_stream st);
 
 // device status words of the tensor-core translation units (read and cleared; -1 on a CUDA error)
 int sjk_tc_body_status_take(void);

@@ -14,24 +14,41 @@ SJK_HD int sjk_split_target(int n_kv) {
     return t < 1 ? 1 : t;
 }
 
-// the dense (staged-row) kernel: n_chunks chunks per KV head in items of *cps chunks; returns the item count
-SJK_HD int sjk_dense_split_count(uint32_t n_chunks, int n_kv, int * cps) {
+// the dense (staged-row) kernel: n_chunks chunks per KV head in items of *cps chunks, the items of all KV heads on at
+// most max_ctas SMs (one CTA per SM, one wave); returns the items per KV head
+SJK_HD int sjk_dense_split_count(uint32_t n_chunks, int n_kv, int * cps, int max_ctas = 148) {
     if (n_chunks == 0) { *cps = 1; return 0; }
-    const int target = (2 * 148 + n_kv - 1) / n_kv;
+    const int target = n_kv > 0 && n_kv <= max_ctas ? max_ctas / n_kv : 1;
     int c = (int) ((n_chunks + (uint32_t) target - 1) / (uint32_t) target);
     if (c < 1) c = 1;
     *cps = c;
     return (int) ((n_chunks + (uint32_t) c - 1) / (uint32_t) c);
 }
 
-// the trellis body kernel (persistent, one CTA per SM over the call's KV heads): splits per KV head
-SJK_HD int sjk_trellis_split_count(int n_kv, uint32_t n_rec) {
+// the trellis body kernel (persistent, one CTA per SM over the call's KV heads, on at most max_ctas SMs): splits per
+// KV head
+SJK_HD int sjk_trellis_split_count(int n_kv, uint32_t n_rec, int max_ctas = 148) {
     const int n = n_kv > 0 ? n_kv : 1;
-    int t = (148 + n - 1) / n;
-    if (t > 148) t = 148;
+    int t = max_ctas / n;
+    if (t < 1) t = 1;
     if ((uint32_t) t > n_rec) t = (int) n_rec;
-    while (t * n_kv > 148) --t;
     return t;
+}
+
+// When one call has both sealed trellis records and staged rows, the trellis kernel and the dense kernel run side by
+// side on disjoint SMs (the dense kernel is a programmatic dependent that starts at once on the SMs the trellis kernel
+// leaves free). A staged chunk costs about 3.2 trellis records of CTA time (a dense chunk about 17 K cycles, a trellis
+// record about 6.5 K in steady state, plus the trellis kernel's longer pipeline fill; tuned on config 2's shapes); the
+// SMs are shared in proportion, with at least one CTA per KV head on each side. Returns the dense kernel's SMs (0: the
+// call has only one of the two); the trellis kernel takes at most the others.
+constexpr uint32_t SJK_CHUNK_W10 = 32;   // chunk weight in tenths of a trellis record
+SJK_HD int sjk_dense_side_sms(int n_kv, uint32_t n_rec, uint32_t n_chunks) {
+    if (n_rec == 0 || n_chunks == 0 || n_kv <= 0 || 2 * n_kv > 148) return 0;
+    const uint64_t wt = (uint64_t) n_rec * 10u, wd = (uint64_t) n_chunks * SJK_CHUNK_W10;
+    int k = (int) ((148u * wd + (wt + wd) / 2u) / (wt + wd));
+    if (k < n_kv) k = n_kv;
+    if (k > 148 - n_kv) k = 148 - n_kv;
+    return k;
 }
 
 // the 4-bit tensor-core body kernel: splits per KV head over n_rec records and n_dense staged chunks
@@ -86,6 +103,7 @@ struct sjk_dyn_state {
     int splits_tc;              // its partial slots [0, splits_tc)
     uint32_t n_sink_d, n_dense; // the dense kernel's chunks (sink chunks first)
     int cps_d, splits_d;        // chunks per item; slots [splits_tc, splits_tc + splits_d)
+    int dense_sms;              // > 0: the dense kernel runs beside the trellis kernel on this many SMs
     sjk_plan_v1 v1;             // the CUDA-core kernel; slots after those
     int splits_v1;
     int splits;                 // all partial slots of the call
@@ -104,7 +122,10 @@ SJK_HD void sjk_plan_counts(const sjk_paths & pa, uint32_t S, uint32_t B, uint32
         d->n_dense = d->n_sink_d + ((regions & SJK_REGION_RING) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
     }
     d->cps_d = 1;
-    d->splits_d = (pa.dense && !pa.fused) ? sjk_dense_split_count(d->n_dense, n_kv, &d->cps_d) : 0;
+    // trellis records and staged rows in one call: the two kernels share the SMs and run side by side
+    const uint32_t n_tc_t = (pa.tc_trellis && !pa.tc_body) ? d->n_tc : 0u;
+    d->dense_sms = (pa.dense && !pa.fused) ? sjk_dense_side_sms(n_kv, n_tc_t, d->n_dense) : 0;
+    d->splits_d = (pa.dense && !pa.fused) ? sjk_dense_split_count(d->n_dense, n_kv, &d->cps_d, d->dense_sms ? d->dense_sms : 148) : 0;
     d->v1 = sjk_make_plan_v1(S, B, N, n_kv, d->n_tc, pa.dense, regions);
     d->splits_v1 = d->v1.n_chunks > 0 ? d->v1.splits : 0;
     d->dense_regions = pa.fused ? ((regions & SJK_REGION_SINK) ? 1u : 0u) | ((regions & SJK_REGION_RING) ? 2u : 0u) : 0u;
@@ -119,7 +140,7 @@ SJK_HD void sjk_plan_counts(const sjk_paths & pa, uint32_t S, uint32_t B, uint32
         }
         d->splits_tc = sjk_tcbody_split_count(n_kv, d->n_tc, n_dense_b);
     } else if (pa.tc_trellis && d->n_tc > 0) {
-        d->splits_tc = sjk_trellis_split_count(n_kv, d->n_tc);
+        d->splits_tc = sjk_trellis_split_count(n_kv, d->n_tc, 148 - d->dense_sms);
     }
     d->splits = d->splits_tc + d->splits_d + d->splits_v1;
 }

@@ -215,6 +215,11 @@ __device__ __forceinline__ void cp_async16(void * dst, const void * src, uint32_
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// close the thread's group of asynchronous copies issued since the last commit (an empty group is fine)
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// wait until at most N of the thread's committed groups are still in flight
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ---- numeric helpers shared by the tensor-core kernels ------------------------------------------------
 namespace num {
@@ -401,6 +406,17 @@ __device__ __forceinline__ uint2 digits3x2(float2 v, float2 sc) {
     const float2 f = fma2(v, sc, make_float2(MAGIC, MAGIC));
     return make_uint2((__float_as_uint(f.x) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u,
                       (__float_as_uint(f.y) + (0x00808080u - MAGIC_BITS)) ^ 0x00808080u);
+}
+
+// The 6-bit codes of elements j0 .. j0 + 7 (j0 % 8 == 0) of a tq6_0 block (norm, qs[64] nibbles, qh[32] 2-bit
+// fields, sj_kvarn.h:1249-1284) as 8 bytes: nibble pairs spread with one PRMT, the high bits from a 256-entry
+// table qh_lut[y] = (2-bit fields of y) << 4 in bytes 0..3.
+__device__ __forceinline__ uint2 tq6_codes8(const uint8_t * blk, int j0, const uint32_t * qh_lut) {
+    const uint32_t qs = (uint32_t) *reinterpret_cast<const uint16_t *>(blk + 2 + j0 / 2) |
+                        ((uint32_t) *reinterpret_cast<const uint16_t *>(blk + 4 + j0 / 2) << 16);
+    const uint32_t qh = *reinterpret_cast<const uint16_t *>(blk + 66 + j0 / 4);
+    const uint32_t a = qs & 0x0F0F0F0Fu, b = (qs >> 4) & 0x0F0F0F0Fu;          // nibbles 0 2 4 6 / 1 3 5 7
+    return make_uint2(prmt(a, b, 0x5140u) | qh_lut[qh & 0xFFu], prmt(a, b, 0x7362u) | qh_lut[qh >> 8]);
 }
 
 }  // namespace num
