@@ -476,6 +476,42 @@ int    sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t N, uint3
                                const float * q, float scale, void * scratch, size_t scratch_bytes, const sjk_xchg_peers * x,
                                uint32_t epoch, float * out, sjk_stream st);
 
+/* ---- the paged pool's bookkeeping on the device: batched reservation, release and truncation ----
+ * Replaces, for many sequences at once, the host loops over sj_kvarn_pool_alloc / sj_kvarn_pool_release that a
+ * sequence's commit and truncation run (sj_kvarn.h:1716-1739 reserve / release, 1581-1603 truncate). The device pool is
+ * the host pool's free-id stack in device memory (sjk_pool_dev_bytes(n_blocks) bytes): sjk_pool_dev_load copies a
+ * host pool's stack in, sjk_pool_dev_store copies it back (both synchronous). Requests are served in order with the
+ * host's semantics, so a batch leaves the same block tables and the same stack as the same calls on the host pool.
+ * Block tables are DEVICE arrays of uint32 block ids (SJKVARN_NO_BLOCK = none), e.g. sj_kvarn_seq.d_blocks. */
+#define SJK_POOL_MAX_REQ  128
+#define SJK_TRUNC_MAX_REQ 256
+typedef struct sjk_block_req {
+    uint32_t * blocks;         /* DEVICE block table of one sequence */
+    uint32_t   g0, g1;         /* groups [g0, g1) */
+} sjk_block_req;
+size_t sjk_pool_dev_bytes(uint32_t n_blocks);
+int    sjk_pool_dev_load(void * dev_pool, const sj_kvarn_pool * pool, sjk_stream st);
+int    sjk_pool_dev_store(const void * dev_pool, sj_kvarn_pool * pool, sjk_stream st);
+/* every NO_BLOCK entry of [g0, g1) takes the id on top of the stack, in group order; a request that needs more
+ * blocks than are free takes none: status[i] (DEVICE int per request) = 0 or SJKVARN_ERR_POOL_FULL. One launch. */
+int    sjk_pool_reserve_batch(void * dev_pool, const sjk_block_req * reqs, int n, int * status, sjk_stream st);
+/* every entry of [g0, g1) that holds a block pushes it (in group order) and becomes SJKVARN_NO_BLOCK. One launch. */
+int    sjk_pool_release_batch(void * dev_pool, const sjk_block_req * reqs, int n, sjk_stream st);
+/* sj_kvarn_layer_truncate for a batch of (sequence, layer) caches: each request zeroes the records of the dropped
+ * groups (through its block table when blocks != NULL, skipping NO_BLOCK), the sink rows of [resume, min(n_old, S))
+ * and the resident ring rows of [max(resume, S), n_old), all requests in one launch; requests with release != 0
+ * (one per sequence: the layers share its blocks) then return the dropped groups' blocks to the device pool in
+ * request order (one more launch). body / sink / ring / blocks are DEVICE pointers (sj_kvarn_layer fields). */
+typedef struct sjk_trunc_req {
+    uint8_t  * body, * sink, * ring;
+    uint32_t * blocks;
+    uint32_t   S, cap, n_head_kv, group;
+    uint32_t   rec_bytes, sink_entry_bytes, stage_bytes;
+    uint32_t   B_old, B_new, n_old, resume;
+    int        release;
+} sjk_trunc_req;
+int    sjk_truncate_batch(const sjk_trunc_req * reqs, int n, void * dev_pool, sjk_stream st);
+
 /* ---- seeded synthetic inputs of the benchmark configurations (DEVICE outputs) ----
  * Input generation for benchmarks and parity tests; no counterpart in the reference. K = X * s with X ~ N(0, 1)
  * (Student-t(4) when heavy) and s ~ LogNormal(0, 1) channel scales with 4 outlier channels x 8 per (layer, head);

@@ -12,7 +12,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsjk_b200.so")
 OBJDIR = os.path.join(HERE, "_build")
 SOURCES = ["sjk_stage.cu", "sjk_seal.cu", "sjk_decode.cu", "sjk_attend.cu", "sjk_attend_tc.cu", "sjk_attend_dense.cu",
-           "sjk_attend_trellis.cu", "sjk_attend_batch.cu", "sjk_synth.cu", "sjk_xchg.cu", "sjk_host.cpp"]
+           "sjk_attend_trellis.cu", "sjk_attend_batch.cu", "sjk_synth.cu", "sjk_xchg.cu", "sjk_pool.cu", "sjk_host.cpp"]
 HEADERS = ["sjk_common.cuh", "sjk_internal.h", "sjk_tables.h", "sjk_tc.cuh", "sjk_desc.cuh", "sjk_plan.cuh", "sjk_synth.h", "sjk_merge.cuh", "../../include/sjk.h"]
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -58,6 +58,21 @@ class XchgPeers(C.Structure):
     _fields_ = [("buf", vp * XCHG_MAX_WORLD), ("world", C.c_int), ("rank", C.c_int)]
 
 
+POOL_MAX_REQ, TRUNC_MAX_REQ = 128, 256
+
+
+class BlockReq(C.Structure):
+    """sjk_block_req: groups [g0, g1) of one sequence's DEVICE block table."""
+    _fields_ = [("blocks", vp), ("g0", u32), ("g1", u32)]
+
+
+class TruncReq(C.Structure):
+    """sjk_trunc_req: one (sequence, layer) cache to scrub after a truncation (DEVICE pointers)."""
+    _fields_ = [("body", vp), ("sink", vp), ("ring", vp), ("blocks", vp), ("S", u32), ("cap", u32), ("n_head_kv", u32),
+                ("group", u32), ("rec_bytes", u32), ("sink_entry_bytes", u32), ("stage_bytes", u32), ("B_old", u32),
+                ("B_new", u32), ("n_old", u32), ("resume", u32), ("release", C.c_int)]
+
+
 class StateInfo(C.Structure):
     _fields_ = [("state_version", u32), ("format_version", u32), ("cfg", Config), ("rotation", u32),
                 ("rotation_n", u32), ("codebook_id", C.c_uint64), ("n_layers", C.c_int), ("n", u32), ("B", u32),
@@ -163,6 +178,12 @@ SIGNATURES = {
     "sjk_layer_view": (None, [P(Layer), P(View)]),
     "sjk_layer_record_copy": (C.c_int, [P(Layer), u32, C.c_int, vp]),
     # exchange of partials over peer memory
+    "sjk_pool_dev_bytes": (C.c_size_t, [u32]),
+    "sjk_pool_dev_load": (C.c_int, [vp, P(Pool), vp]),
+    "sjk_pool_dev_store": (C.c_int, [vp, P(Pool), vp]),
+    "sjk_pool_reserve_batch": (C.c_int, [vp, P(BlockReq), C.c_int, vp, vp]),
+    "sjk_pool_release_batch": (C.c_int, [vp, P(BlockReq), C.c_int, vp]),
+    "sjk_truncate_batch": (C.c_int, [P(TruncReq), C.c_int, vp, vp]),
     "sjk_xchg_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "sjk_xchg_alloc": (C.c_int, [C.c_size_t, P(vp), vp]),
     "sjk_xchg_free": (C.c_int, [vp]),
