@@ -399,7 +399,7 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     int splits_tc = 0;
     if (splits_tc_max) {
         const int rc = pa.tc_body ? sjk_tc_body_launch(v, B, N, d.n_tc, (int) d.dense_regions, qpos0, n_q, n_head, kv_head0, n_kv, q,
-                                                       scale, (float *) scratch, 0, &splits_tc, st)
+                                                       scale, (float *) scratch, 0, 148 - d.dense_sms, &splits_tc, st)
                                   : sjk_tc_trellis_launch(v, B, N, d.n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
                                                           (float *) scratch, 0, d.splits_tc, &splits_tc, st);
         if (rc) return rc;
@@ -410,7 +410,7 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (d.splits_d) {
         const int rc = sjk_tc_dense_launch(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, (float *) scratch,
                                            splits_tc, d.splits_d, d.n_sink_d, d.n_dense, d.cps_d,
-                                           d.dense_sms > 0 && splits_tc > 0 && pa.tc_trellis, st);
+                                           d.dense_sms > 0 && splits_tc > 0, st);
         if (rc) return rc;
     }
     AttnParams p;

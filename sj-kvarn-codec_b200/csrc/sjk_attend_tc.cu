@@ -946,7 +946,7 @@ constexpr double DENSE_WEIGHT = 4.5;
 // splits per KV head. Runs on the host (sjk_tc_body_launch) and in the descriptor-driven call's planner kernel.
 SJK_HD int fill_plan(TcParams & p, const sjk_view & v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0,
                      int n_q, int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0,
-                     bool enabled) {
+                     bool enabled, int max_ctas) {
     p.lay = v.lay; p.body = v.body; p.blocks = v.blocks; p.H = v.n_head_kv; p.kv0 = kv0; p.S = v.S;
     p.n_rec = n_rec; p.qpos0 = qpos0; p.n_q = n_q; p.n_head = n_head; p.grp = n_head / n_kv; p.rows = n_q * p.grp;
     for (int r = 0; r < NR; ++r) {
@@ -963,7 +963,7 @@ SJK_HD int fill_plan(TcParams & p, const sjk_view & v, uint32_t B, uint32_t N, u
         p.n_sink_chunks = (dense_regions & 1) ? (s_end + 127u) / 128u : 0u;
         p.n_dense = p.n_sink_chunks + ((dense_regions & 2) && N > t0 ? (N - t0 + 127u) / 128u : 0u);
     }
-    const int splits = enabled ? sjk_tcbody_split_count(n_kv, n_rec, p.n_dense) : 0;
+    const int splits = enabled ? sjk_tcbody_split_count(n_kv, n_rec, p.n_dense, max_ctas) : 0;
     p.n_splits = splits;
     if (splits == 0) return 0;
     // record ranges: split s takes d(s) chunks (u = s, s + splits, ..) and about target - DENSE_WEIGHT d(s) records
@@ -993,7 +993,8 @@ __global__ void body_tc_dyn_plan_kernel(const sjk_dyn_state * __restrict__ ds, s
                                         const float * q, float scale, float * part, TcParams * out) {
     if (threadIdx.x != 0) return;
     const sjk_dyn_state d = *ds;
-    fill_plan(*out, v, d.B, d.N, d.n_tc, (int) d.dense_regions, d.qpos0, n_q, n_head, kv0, n_kv, q, scale, part, 0, d.ok != 0);
+    fill_plan(*out, v, d.B, d.N, d.n_tc, (int) d.dense_regions, d.qpos0, n_q, n_head, kv0, n_kv, q, scale, part, 0, d.ok != 0,
+              148 - d.dense_sms);
 }
 
 }  // namespace
@@ -1015,10 +1016,11 @@ int sjk_tc_body_max_splits(int n_kv) {
 }
 
 int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
-                       int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int * splits_out,
-                       sjk_stream st) {
+                       int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int max_ctas,
+                       int * splits_out, sjk_stream st) {
     TcParams p;
-    const int splits = fill_plan(p, *v, B, N, n_rec, dense_regions, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, true);
+    const int splits = fill_plan(p, *v, B, N, n_rec, dense_regions, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, true,
+                                 max_ctas);
     *splits_out = splits;
     if (splits == 0) return 0;
     cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);

@@ -41,10 +41,12 @@ SJK_HD int sjk_trellis_split_count(int n_kv, uint32_t n_rec, int max_ctas = 148)
 // record about 6.5 K in steady state, plus the trellis kernel's longer pipeline fill; tuned on config 2's shapes); the
 // SMs are shared in proportion, with at least one CTA per KV head on each side. Returns the dense kernel's SMs (0: the
 // call has only one of the two); the trellis kernel takes at most the others.
+// (4-bit scalar layers do not use this: their body kernel takes the staged chunks itself, spread over all SMs, which
+// measured faster than the dense kernel beside it: 65.5 against 80.5 us on config 1.)
 constexpr uint32_t SJK_CHUNK_W10 = 32;   // chunk weight in tenths of a trellis record
-SJK_HD int sjk_dense_side_sms(int n_kv, uint32_t n_rec, uint32_t n_chunks) {
+SJK_HD int sjk_dense_side_sms(int n_kv, uint32_t n_rec, uint32_t n_chunks, uint32_t w10 = SJK_CHUNK_W10) {
     if (n_rec == 0 || n_chunks == 0 || n_kv <= 0 || 2 * n_kv > 148) return 0;
-    const uint64_t wt = (uint64_t) n_rec * 10u, wd = (uint64_t) n_chunks * SJK_CHUNK_W10;
+    const uint64_t wt = (uint64_t) n_rec * 10u, wd = (uint64_t) n_chunks * w10;
     int k = (int) ((148u * wd + (wt + wd) / 2u) / (wt + wd));
     if (k < n_kv) k = n_kv;
     if (k > 148 - n_kv) k = 148 - n_kv;
@@ -52,10 +54,11 @@ SJK_HD int sjk_dense_side_sms(int n_kv, uint32_t n_rec, uint32_t n_chunks) {
 }
 
 // the 4-bit tensor-core body kernel: splits per KV head over n_rec records and n_dense staged chunks
-SJK_HD int sjk_tcbody_split_count(int n_kv, uint32_t n_rec, uint32_t n_dense) {
+SJK_HD int sjk_tcbody_split_count(int n_kv, uint32_t n_rec, uint32_t n_dense, int max_ctas = 148) {
     const int n = n_kv > 0 ? n_kv : 1;
-    int t = (148 + n - 1) / n;
+    int t = max_ctas >= 148 ? (148 + n - 1) / n : max_ctas / n;
     if (t > 148) t = 148;
+    if (t < 1) t = 1;
     if ((uint32_t) t > n_rec + n_dense) t = (int) (n_rec + n_dense);
     return t;
 }
@@ -138,7 +141,7 @@ SJK_HD void sjk_plan_counts(const sjk_paths & pa, uint32_t S, uint32_t B, uint32
             n_dense_b = (d->dense_regions & 1) ? (s_end + 127u) / 128u : 0u;
             n_dense_b += (d->dense_regions & 2) && N > t0 ? (N - t0 + 127u) / 128u : 0u;
         }
-        d->splits_tc = sjk_tcbody_split_count(n_kv, d->n_tc, n_dense_b);
+        d->splits_tc = sjk_tcbody_split_count(n_kv, d->n_tc, n_dense_b, 148 - d->dense_sms);
     } else if (pa.tc_trellis && d->n_tc > 0) {
         d->splits_tc = sjk_trellis_split_count(n_kv, d->n_tc, 148 - d->dense_sms);
     }
