@@ -264,7 +264,7 @@ def run_config1(args, torch, dist, local_rank):
     s = torch.cuda.Stream()
     st = C.c_void_p(s.cuda_stream)
     t0 = time.time()
-    m = configs.build_config1(stream=st)
+    m = configs.build_config1(stream=st, layers=args.config1_layers)
     torch.cuda.synchronize()
     build_s = time.time() - t0
     a = AttnStep(torch, m, configs.CFG1["n_q"], s, st)
@@ -887,7 +887,8 @@ def main():
     ap.add_argument("--config3-steps", type=int, default=128, help="timed decode steps of config 3 (at least --steps)")
     ap.add_argument("--config4-layers", type=int, default=16, help="layers of the config-4 sequence")
     ap.add_argument("--config2-layers", type=int, default=16, help="layers of the config-2 model (fewer only for profiling)")
-    ap.add_argument("--only", choices=["seal", "seal2", "config2", "config3"], default=None,
+    ap.add_argument("--config1-layers", type=int, default=16, help="layers of the config-1 model (fewer only for profiling)")
+    ap.add_argument("--only", choices=["seal", "seal2", "config1", "config2", "config3"], default=None,
                     help="run one section alone on one GPU and print its numbers (for profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -919,6 +920,9 @@ def main():
             r = run_seal0(args, torch)
         elif args.only == "seal2":
             r = run_seal0(args, torch, bits=(3, 2), heavy=True, seed=2)
+        elif args.only == "config1":
+            r = run_config1(args, torch, None, local_rank)
+            r.pop("out0", None)
         elif args.only == "config2":
             r = run_config2(args, torch)
             r.pop("out0", None)
@@ -1027,9 +1031,10 @@ def main():
                                    "nccl_all_gather": cfg4["ms_exchange"] * 1e3, "nccl_merge": cfg4["ms_merge"] * 1e3},
             "nccl_path_us_per_call": cfg4["ms_nccl"] * 1e3, "split_exchange_path_us_per_call": cfg4["ms_split"] * 1e3,
             "peer_exchange_equals_nccl_path": cfg4["p2p_equals_nccl"],
-            "exchange": "per layer call, one sjk_attend_partial_xchg: the call's merge kernel stores the rank's (m, l, o) "
-                        "triples into every rank's exchange buffer over NVLink (CUDA IPC mappings, plain stores), waits "
-                        "for the other ranks' and merges all of them in rank order",
+            "exchange": "per layer call, one sjk_attend_partial_xchg: the partial attention, then one exchange launch "
+                        "that stores the rank's (m, l, o) triples into every rank's exchange buffer over NVLink (CUDA "
+                        "IPC mappings, 8-byte words tagged with the call's epoch), gathers the other ranks' and merges "
+                        "all of them in rank order",
             "bulk_seal": {"mtoks_per_gpu": cfg4["tokens_sealed"] / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "mtoks_all_gpus": cfg4["tokens_sealed"] * world / (cfg4["seal_ms"] * 1e-3) / 1e6,
                           "ms": cfg4["seal_ms"], "tokens_per_gpu": cfg4["tokens_sealed"],

@@ -382,7 +382,7 @@ int sjk_attend_batch(const sjk_view * views, const uint32_t * B, const uint32_t 
  * limits, such as inside a stream capture, a custom allocator's own callbacks or an engine whose memory
  * is planned ahead. No counterpart in the reference. The scratch for the split partials is a fixed 16 MiB
  * device array inside the library (held by every GPU that loads it, until exit) instead of a caller
- * buffer; shapes whose sjk_attend_scratch_bytes() bound exceeds 16 MiB return SJK_ERR_SCRATCH_LIMIT.
+ * buffer; shapes whose split partials need more than 16 MiB return SJK_ERR_SCRATCH_LIMIT.
  * The array's address is looked up on the first call on each device, so make that first call outside any
  * stream capture. All calls share the array: calls that overlap on the GPU race. Allocates nothing. */
 int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
@@ -450,7 +450,8 @@ int sjk_layer_record_copy(const sj_kvarn_layer * L, uint32_t g, int h, void * ho
  * sends its CUDA IPC handle (SJK_XCHG_HANDLE_BYTES) to the other ranks and maps theirs (sjk_xchg_open); the
  * sjk_xchg_peers it passes holds every rank's buffer as this process sees it (buf[rank] = its own). Every call carries
  * an epoch that all ranks count up alike from 1, one per exchange; consecutive epochs use alternate slot sets, so a
- * rank may publish epoch e + 1 while others still merge epoch e. A rank's wait for the others is bounded (about 1 s):
+ * rank may publish epoch e + 1 while others still merge epoch e. Every 8-byte word of a slot carries the epoch that
+ * wrote it, so a reader knows a value is current without a flag or a fence. A rank's wait for the others is bounded (about 1 s):
  * a rank that never publishes makes the others write zeros and raise SJK_DEVICE_TIMEOUT in sjk_device_status().
  * Plain stores and loads only: no TMA, no multicast. Buffers are freed (sjk_xchg_close, sjk_xchg_free) only after
  * every rank's last exchange completed. */
@@ -469,9 +470,10 @@ int    sjk_xchg_close(void * peer_buf);
  * (DEVICE) gets the merge of all ranks' triples in rank order. One launch. */
 int    sjk_xchg_exchange(const sjk_xchg_peers * x, const float * part, int n_rows, int D, uint32_t epoch, float * out,
                          sjk_stream st);
-/* sjk_attend_partial with the exchange folded into the call's last kernel: the merge kernel that forms this rank's
- * triples stores them into every rank's buffer, waits for the others' and writes the merged output out[n_q * n_head][D]
- * (the exchange shape: n_rows = n_q * n_head, D = head_dim). */
+/* sjk_attend_partial followed by the exchange, in one call: this rank's triples are formed at the end of the scratch
+ * (sjk_attend_scratch_bytes() leaves room for them) and one exchange launch stores them into every rank's buffer,
+ * gathers the others' and writes the merged output out[n_q * n_head][D] (the exchange shape: n_rows = n_q * n_head,
+ * D = head_dim). */
 int    sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, unsigned regions,
                                const float * q, float scale, void * scratch, size_t scratch_bytes, const sjk_xchg_peers * x,
                                uint32_t epoch, float * out, sjk_stream st);

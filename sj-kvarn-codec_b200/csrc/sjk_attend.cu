@@ -243,17 +243,12 @@ __global__ void __launch_bounds__(NT) attend_split_dyn_kernel(const AttnParams *
 // out[row, head] = sum_i o_i e^(m_i - m) / sum_i l_i e^(m_i - m) (sjk_merge.cuh). Grid (query row x head, channel tiles
 // of 64); each CTA recomputes the split weights (cheap) into shared memory and sums its 64 channels.
 using sjkm::MERGE_SPLITS;
-__device__ int sjk_xchg_dev_status;                   // SJK_DEVICE_TIMEOUT when an exchange wait ran out
 
 // part_out (optional): instead of out, write the combined partial (m, l, o[D]) of each row (o not normalized), the
 // form sjk_attend_partial returns
 // splits_dev (optional): read the split count from device memory (the descriptor-driven call's plan)
-// xchg (world > 0): the row's partial goes to every rank over peer memory instead, and out gets the merge of all
-// ranks' partials (sjk_attend_partial_xchg)
-template <bool XCHG>
 __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, int splits, int n_rows, int D, float * out,
-                                                           float * part_out, const int * splits_dev,
-                                                           const __grid_constant__ sjkm::XchgArgs xchg) {
+                                                           float * part_out, const int * splits_dev) {
     extern __shared__ float wts[];                     // [max(splits, ranks)] weights, then [4][64] partial sums
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
@@ -264,18 +259,7 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     float m, t;
     sjkm::merge_tile(part, splits, n_rows, D, row, d0, wts, s_red, m, t);
     const float * acc = wts + splits;
-    if (XCHG) {
-        const float my_o = tid < 64 ? sjkm::acc_o(acc, tid) : 0.0f;
-        const bool ok = sjkm::xchg_publish_wait(xchg, n_rows, D, row, (int) blockIdx.y, m, t, my_o);
-        if (!ok) {
-            if (tid < 64 && d0 + tid < D) out[(size_t) row * D + d0 + tid] = 0.0f;
-            if (tid == 0) atomicOr(&sjk_xchg_dev_status, (int) SJK_DEVICE_TIMEOUT);
-            return;
-        }
-        float m2, t2;
-        sjkm::merge_tile<true>(sjkm::xchg_slots(xchg, n_rows, D), xchg.world, n_rows, D, row, d0, wts, s_red, m2, t2);
-        sjkm::store_out(wts + xchg.world, t2, D, row, d0, out);
-    } else if (part_out) {
+    if (part_out) {
         if (tid < 64 && d0 + tid < D) part_out[(size_t) row * (D + 2) + 2 + d0 + tid] = sjkm::acc_o(acc, tid);
         if (blockIdx.y == 0 && tid == 0) { part_out[(size_t) row * (D + 2)] = m; part_out[(size_t) row * (D + 2) + 1] = t; }
     } else {
@@ -296,10 +280,16 @@ size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, i
     return (size_t) 3 * sjk_split_target(n_kv) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
 }
 
+// bytes of the rank's own partial in sjk_attend_partial_xchg's scratch (after the split partials), 256-aligned
+static size_t xchg_part_bytes(const sjk_view * v, int n_q, int n_head) {
+    return ((size_t) n_q * n_head * (v->lay.D + 2) * sizeof(float) + 255) & ~(size_t) 255;
+}
+
 extern "C" size_t sjk_attend_scratch_bytes(const sjk_view * v, uint32_t N, int n_q, int n_head) {
     (void) N;
-    if (!v) return 0;
-    return sjk_attend_heads_scratch_bytes(v, n_q, n_head, v->n_head_kv);
+    if (!v || n_q <= 0 || n_head <= 0) return 0;
+    // the split partials, plus room for the call's own partial (sjk_attend_partial_xchg)
+    return sjk_attend_heads_scratch_bytes(v, n_q, n_head, v->n_head_kv) + xchg_part_bytes(v, n_q, n_head);
 }
 
 namespace {
@@ -349,24 +339,20 @@ int launch_split(const AttnParams & p, const AttnParams * dyn, int splits, int n
 // Programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them on the
 // device (griddepcontrol.wait), so the launch gap between the two kernels disappears. splits_dev: the split count
 // is read from device memory (shared memory sized for max_splits).
-// xchg (optional): exchange the rows' partials with the other ranks and write the merge of all of them to out.
 int launch_merge(const float * part, int splits, const int * splits_dev, int max_splits, int n_rows, int D, float * out,
-                 float * part_out, sjk_stream st, const sjkm::XchgArgs * xchg = nullptr) {
-    sjkm::XchgArgs xa = {};
-    if (xchg) xa = *xchg;
+                 float * part_out, sjk_stream st) {
     const int n_w = splits_dev ? max_splits : splits;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64));
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t) ((n_w > xa.world ? n_w : xa.world) + 256) * sizeof(float);
+    cfg.dynamicSmemBytes = (size_t) (n_w + 256) * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = xa.world > 0 ? cudaLaunchKernelEx(&cfg, attend_merge_kernel<true>, part, splits, n_rows, D, out, part_out, splits_dev, xa)
-                                       : cudaLaunchKernelEx(&cfg, attend_merge_kernel<false>, part, splits, n_rows, D, out, part_out, splits_dev, xa);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, attend_merge_kernel, part, splits, n_rows, D, out, part_out, splits_dev);
     if (sjk_check(e))
         return SJK_ERR_DEVICE;
     return sjk_check_launch();
@@ -376,7 +362,7 @@ int launch_merge(const float * part, int splits, const int * splits_dev, int max
 
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
                      const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
-                     unsigned regions, float * part_out, const sjk_xchg_peers * xchg, uint32_t epoch) {
+                     unsigned regions, float * part_out) {
     if (!v || !q || !(out || part_out) || n_q <= 0 || n_head <= 0 || n_kv <= 0 || kv_head0 < 0 || kv_head0 + n_kv > v->n_head_kv ||
         n_head % n_kv)
         return SJKVARN_ERR_ARG;
@@ -421,12 +407,6 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     if (d.splits_v1) {
         const int rc = launch_split(p, nullptr, d.splits_v1, n_kv, st);
         if (rc) return rc;
-    }
-    if (xchg) {
-        sjkm::XchgArgs xa = {};
-        xa.world = xchg->world; xa.rank = xchg->rank; xa.epoch = epoch;
-        for (int i = 0; i < xchg->world; ++i) xa.buf[i] = reinterpret_cast<uint8_t *>(xchg->buf[i]);
-        return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, nullptr, st, &xa);
     }
     return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, part_out, st);
 }
@@ -548,9 +528,11 @@ extern "C" int sjk_attend_partial(const sjk_view * v, uint32_t B, uint32_t N, ui
                             regions, part_out);
 }
 
-// sjk_attend_partial whose partials go straight to every rank over peer memory: the merge kernel of the call stores
-// its rows' triples into every rank's exchange buffer, waits for every rank's and writes the merge of all of them to
-// out[n_q * n_head][D] - the all-gather + sjk_attend_merge of the same triples, in the call's own last kernel.
+// sjk_attend_partial whose partials go straight to every rank over peer memory: the call's merge kernel writes the
+// rank's triples to the end of the scratch, and one exchange launch (sjk_xchg_exchange) stores them into every rank's
+// exchange buffer, gathers every rank's and writes the merge of all of them to out[n_q * n_head][D] - the all-gather +
+// sjk_attend_merge of the same triples. (The exchange inside the merge kernel itself measured slower on 2 GPUs: 251.7
+// against 241.3 us per config-4 call.)
 extern "C" int sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
                                        unsigned regions, const float * q, float scale, void * scratch, size_t scratch_bytes,
                                        const sjk_xchg_peers * x, uint32_t epoch, float * out, sjk_stream st) {
@@ -559,28 +541,25 @@ extern "C" int sjk_attend_partial_xchg(const sjk_view * v, uint32_t B, uint32_t 
         return SJKVARN_ERR_ARG;
     for (int i = 0; i < x->world; ++i)
         if (!x->buf[i] || ((uintptr_t) x->buf[i] & 255)) return SJKVARN_ERR_ARG;
-    return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st,
-                            regions, nullptr, x, epoch);
+    const size_t own = xchg_part_bytes(v, n_q, n_head);
+    if (!scratch || scratch_bytes < own + 256) return SJKVARN_ERR_ARG;
+    const size_t split_bytes = (scratch_bytes - own) & ~(size_t) 255;
+    float * part = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + split_bytes);
+    const int rc = sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, nullptr, scratch, split_bytes, st,
+                                    regions, part);
+    if (rc) return rc;
+    return sjk_xchg_exchange(x, part, n_q * n_head, v->lay.D, epoch, out, st);
 }
 
 // out[n_rows][D] from n_parts partial sets parts[n_parts][n_rows][D + 2], combined in index order
 extern "C" int sjk_attend_merge(const float * parts, int n_parts, int n_rows, int D, float * out, sjk_stream st) {
     if (!parts || !out || n_parts <= 0 || n_rows <= 0 || D <= 0 || n_parts > MERGE_SPLITS) return SJKVARN_ERR_ARG;
-    attend_merge_kernel<false><<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
-        parts, n_parts, n_rows, D, out, nullptr, nullptr, sjkm::XchgArgs{});
+    attend_merge_kernel<<<dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64)), 256, (size_t) (n_parts + 256) * sizeof(float), st>>>(
+        parts, n_parts, n_rows, D, out, nullptr, nullptr);
     return sjk_check_launch();
 }
 
 SJK_DESC_STATUS_READER(attend_desc_status_take)
-
-namespace {
-int attend_xchg_status_take(void) {
-    int v = 0, zero = 0;
-    if (cudaMemcpyFromSymbol(&v, sjk_xchg_dev_status, sizeof v) != cudaSuccess) return -1;
-    if (cudaMemcpyToSymbol(sjk_xchg_dev_status, &zero, sizeof zero) != cudaSuccess) return -1;
-    return v;
-}
-}  // namespace
 
 // status words of every kernel with bounded waits (SJK_DEVICE_TIMEOUT) and of the descriptor-driven calls
 // (SJK_DEVICE_DESC) since the last call
@@ -588,9 +567,9 @@ extern "C" int sjk_device_status(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = sjk_tc_body_status_take(), b = sjk_tc_dense_status_take(), c = sjk_tc_trellis_status_take();
     const int d = attend_desc_status_take(), e = sjk_seal_desc_status_take(), f = sjk_stage_desc_status_take();
-    const int x = sjk_xchg_status_take(), y = attend_xchg_status_take();
-    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0 || x < 0 || y < 0) return -1;
-    return a | b | c | d | e | f | x | y;
+    const int x = sjk_xchg_status_take();
+    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0 || f < 0 || x < 0) return -1;
+    return a | b | c | d | e | f | x;
 }
 
 extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
@@ -620,7 +599,7 @@ void * g_static_ptr[256];                    // device address of sjk_static_scr
 extern "C" int sjk_attend_static(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
                                  const float * q, float scale, float * out, sjk_stream st) {
     if (!v || n_q <= 0 || n_head <= 0) return SJKVARN_ERR_ARG;
-    const size_t need = sjk_attend_scratch_bytes(v, N, n_q, n_head);
+    const size_t need = sjk_attend_heads_scratch_bytes(v, n_q, n_head, v->n_head_kv);   // the split partials of one call
     if (need > SJK_STATIC_SCRATCH_BYTES) return SJK_ERR_SCRATCH_LIMIT;
     int dev = 0;
     if (sjk_check(cudaGetDevice(&dev))) return SJK_ERR_DEVICE;

@@ -12,8 +12,7 @@ void sjk_set_sticky(int status);
 // (m, l, o[D]) per (query row, query head) instead of the normalized output
 int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0,
                      int n_kv, const float * q, float scale, float * out, void * scratch, size_t scratch_bytes,
-                     sjk_stream st, unsigned regions, float * part_out, const sjk_xchg_peers * xchg = nullptr,
-                     uint32_t epoch = 0);
+                     sjk_stream st, unsigned regions, float * part_out);
 size_t sjk_attend_heads_scratch_bytes(const sjk_view * v, int n_q, int n_head, int n_kv);
 // decode the K and V rows of position pos, KV head h, to k[D], v[D] (device)
 int sjk_kv_row(const sjk_view * v, uint32_t B, uint32_t pos, int h, float * k, float * vo, sjk_stream st);

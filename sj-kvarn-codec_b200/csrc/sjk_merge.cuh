@@ -7,15 +7,15 @@
 // One CTA of 256 threads per (row, 64-channel tile).
 //
 // Exchange over peer memory: rank r's CTA (row, tile) stores its tile of the rank's triple (m, l, o[64]) into slot
-// [parity][r][row] of every rank's exchange buffer (plain stores through CUDA IPC mappings of the other GPUs'
-// buffers; no TMA, no multicast), raises flag [parity][r][row][tile] = epoch in each buffer with a release store at
-// system scope, then waits (bounded) until the flags [parity][src][row][tile] of its own buffer all hold the epoch
-// and merges the world slots of its (row, tile) in rank order - the all-gather + merge of the same triples, in one
-// kernel.
-// Exchange buffer: flags u32 [2][SJK_XCHG_MAX_WORLD][n_rows][tiles] (rounded up to 256 bytes), then slots
-// float [2][world][n_rows][D + 2]. Consecutive epochs alternate parities; a rank publishes epoch e + 2 only after its
-// merge of e + 1 saw every rank's flags of e + 1, raised after those ranks' merges of e completed (stream order), so
-// a slot is never overwritten while it is read.
+// [parity][r][row] of every rank's exchange buffer (plain 8-byte stores through CUDA IPC mappings of the other GPUs'
+// buffers; no TMA, no multicast), then waits (bounded) until the tile's words of every rank's slot in its own buffer
+// carry the epoch, copies them to shared memory and merges the world triples in rank order there - the all-gather +
+// merge of the same triples, in one kernel. Every word holds a value in its low half and the epoch that wrote it in
+// its high half; 8-byte stores and loads are single-copy atomic, so a word is either the old or the new one, and no
+// fence or separate flag is needed (each word validates itself).
+// Exchange buffer: u64 words [2][world][n_rows][D + 2] (m, l, o[D] per row). Consecutive epochs alternate parities;
+// a rank publishes epoch e + 2 only after its merge of e + 1 saw every rank's words of e + 1, written after those
+// ranks' merges of e completed (stream order), so a slot is never overwritten while it is read.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -29,22 +29,13 @@ constexpr int MERGE_PRE = 24;             // outputs per thread loaded ahead of 
 constexpr uint64_t XCHG_WAIT_NS = 1000000000ull;   // 1 s of wall clock per exchange wait
 
 __host__ __device__ inline int merge_tiles(int D) { return (D + 63) / 64; }
-__host__ __device__ inline size_t xchg_flag_bytes(int n_rows, int D) {
-    return ((size_t) 2 * SJK_XCHG_MAX_WORLD * n_rows * merge_tiles(D) * sizeof(uint32_t) + 255) & ~(size_t) 255;
+__host__ __device__ inline size_t xchg_words_bytes(int world, int n_rows, int D) {
+    return (size_t) 2 * world * n_rows * (size_t) (D + 2) * sizeof(uint64_t);
 }
 
 // Combines `splits` partial sets part[splits][n_rows][D + 2] for (row, channels d0 .. d0 + 63). On return every thread
 // holds m and t = sum l w; the tile's unnormalized outputs are acc_o(wts + splits, tid) for tid < 64. wts: shared
 // memory of at least splits + 256 floats; s_red: 16 floats.
-// CG: read the partials through L2 only (partials that other GPUs wrote during this kernel)
-template <bool CG = false>
-__device__ __forceinline__ float ldp(const float * p) { return CG ? __ldcg(p) : *p; }
-template <bool CG = false>
-__device__ __forceinline__ float2 ldp2(const float * p) {
-    return CG ? __ldcg(reinterpret_cast<const float2 *>(p)) : *reinterpret_cast<const float2 *>(p);
-}
-
-template <bool CG = false>
 __device__ __forceinline__ void merge_tile(const float * part, int splits, int n_rows, int D, int row, int d0, float * wts,
                                            float * s_red, float & m_out, float & t_out) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -57,7 +48,7 @@ __device__ __forceinline__ void merge_tile(const float * part, int splits, int n
 #pragma unroll
     for (int k = 0; k < MERGE_PRE; ++k) {
         const int i = grp4 + 4 * k;
-        xo[k] = i < splits ? ldp<CG>(src + (size_t) i * step) : 0.0f;
+        xo[k] = i < splits ? src[(size_t) i * step] : 0.0f;
     }
     // one pass over (m, l) of the splits this thread owns (at most MERGE_SPLITS / 256)
     float mi[MERGE_SPLITS / 256], li[MERGE_SPLITS / 256];
@@ -66,7 +57,7 @@ __device__ __forceinline__ void merge_tile(const float * part, int splits, int n
         const int i = tid + 256 * k;
         mi[k] = -INFINITY; li[k] = 0.0f;
         if (i < splits) {
-            const float2 ml = ldp2<CG>(part + ((size_t) i * n_rows + row) * (D + 2));
+            const float2 ml = *reinterpret_cast<const float2 *>(part + ((size_t) i * n_rows + row) * (D + 2));
             mi[k] = ml.x; li[k] = ml.y;
         }
     }
@@ -101,7 +92,7 @@ __device__ __forceinline__ void merge_tile(const float * part, int splits, int n
         const int i = grp4 + 4 * k;
         if (i < splits) o = fmaf(xo[k], wts[i], o);
     }
-    for (int i = grp4 + 4 * MERGE_PRE; i < splits; i += 4) o = fmaf(ldp<CG>(src + (size_t) i * step), wts[i], o);
+    for (int i = grp4 + 4 * MERGE_PRE; i < splits; i += 4) o = fmaf(src[(size_t) i * step], wts[i], o);
     float * acc = wts + splits;
     acc[grp4 * 64 + dl] = o;
     __syncthreads();
@@ -133,51 +124,52 @@ __device__ __forceinline__ uint64_t gtimer() {
     return t;
 }
 
-// Publish this rank's triple tile (m, t, and o = my_o for threads 0..63) of (row, tile) to every rank, then wait for
-// every rank's; returns false (in every thread) when a wait ran out. n_rows, D: the shape of the exchange.
-__device__ __forceinline__ bool xchg_publish_wait(const XchgArgs & x, int n_rows, int D, int row, int tile, float m, float t,
-                                                  float my_o) {
-    const int tid = threadIdx.x, d0 = 64 * tile, tiles = merge_tiles(D);
-    const uint32_t par = x.epoch & 1u;
-    const size_t fb = xchg_flag_bytes(n_rows, D);
-    const size_t slot_off = (((size_t) par * x.world + x.rank) * n_rows + row) * (D + 2);
-    for (int dst = 0; dst < x.world; ++dst) {
-        float * slot = reinterpret_cast<float *>(x.buf[dst] + fb) + slot_off;
-        if (tid < 64 && d0 + tid < D) slot[2 + d0 + tid] = my_o;
-        if (tid == 64) { slot[0] = m; slot[1] = t; }          // every tile's CTA writes the row's (m, l): same values
-    }
-    // the CTA barrier orders every thread's slot stores before the flag stores below, and a release at system scope
-    // is cumulative: it makes the stores it is ordered after visible to a peer that acquires the flag
-    __syncthreads();
-    const size_t fidx_src = (((size_t) par * SJK_XCHG_MAX_WORLD + x.rank) * n_rows + row) * tiles + tile;
-    if (tid < x.world) {
-        uint32_t * flag = reinterpret_cast<uint32_t *>(x.buf[tid]) + fidx_src;
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(x.epoch) : "memory");
-    }
-    bool ok = true;
-    if (tid < x.world) {
-        const uint32_t * flag = reinterpret_cast<const uint32_t *>(x.buf[x.rank]) +
-                                (((size_t) par * SJK_XCHG_MAX_WORLD + tid) * n_rows + row) * tiles + tile;
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-        if (v != x.epoch) {
-            const uint64_t t0 = gtimer();
-            do {
-                __nanosleep(100);
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-            } while (v != x.epoch && gtimer() - t0 < XCHG_WAIT_NS);
-        }
-        ok = v == x.epoch;
-    }
-    ok = __syncthreads_and(ok) != 0;
-    __threadfence();
-    return ok;
-}
+constexpr int XCHG_TILE_WORDS = 66;        // m, l and 64 outputs of one (row, tile)
 
-// the local slots of the epoch's parity: [world][n_rows][D + 2]
-__device__ __forceinline__ const float * xchg_slots(const XchgArgs & x, int n_rows, int D) {
-    return reinterpret_cast<const float *>(x.buf[x.rank] + xchg_flag_bytes(n_rows, D)) +
-           (size_t) (x.epoch & 1u) * x.world * n_rows * (D + 2);
+// Publish this rank's triple tile (m, t, and o = my_o of threads 0..63) of (row, tile) to every rank, and gather every
+// rank's tile of the same (row, tile) into stage[world][66] (shared memory: m, l, o[64]); returns false (in every
+// thread) when a wait ran out. n_rows, D: the shape of the exchange.
+__device__ __forceinline__ bool xchg_publish_gather(const XchgArgs & x, int n_rows, int D, int row, int tile, float m, float t,
+                                                    float my_o, float * stage) {
+    const int tid = threadIdx.x, d0 = 64 * tile;
+    const uint32_t par = x.epoch & 1u;
+    const uint64_t tag = (uint64_t) x.epoch << 32;
+    const size_t row_words = (size_t) (D + 2);
+    // thread j < 64: o[d0 + j]; thread 64: m; thread 65: l (every tile's CTA writes the row's m and l: same values)
+    if (tid < XCHG_TILE_WORDS) {
+        const int w = tid < 64 ? 2 + d0 + tid : tid - 64;
+        if (w < D + 2) {
+            const float val = tid < 64 ? my_o : (tid == 64 ? m : t);
+            const uint64_t word = tag | __float_as_uint(val);
+            const size_t off = ((((size_t) par * x.world + x.rank) * n_rows + row) * row_words + (size_t) w) * sizeof(uint64_t);
+            for (int dst = 0; dst < x.world; ++dst)
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x.buf[dst] + off), "l"(word) : "memory");
+        }
+    }
+    // gather: word j of source src's tile, polled in this rank's own buffer until it carries the epoch
+    bool ok = true;
+    const uint8_t * own = x.buf[x.rank];
+    for (int i = tid; i < x.world * XCHG_TILE_WORDS; i += blockDim.x) {
+        const int src = i / XCHG_TILE_WORDS, j = i - src * XCHG_TILE_WORDS;
+        const int w = j < 2 ? j : 2 + d0 + (j - 2);
+        float v = 0.0f;
+        if (w < D + 2 && ok) {                                // after a wait ran out, the rest read as zeros
+            const uint64_t * p = reinterpret_cast<const uint64_t *>(own) + (((size_t) par * x.world + src) * n_rows + row) * row_words + w;
+            uint64_t word;
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(p) : "memory");
+            if ((word >> 32) != x.epoch) {
+                const uint64_t t0 = gtimer();
+                do {
+                    __nanosleep(32);
+                    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(p) : "memory");
+                } while ((word >> 32) != x.epoch && gtimer() - t0 < XCHG_WAIT_NS);
+            }
+            ok = ok && (word >> 32) == x.epoch;
+            v = __uint_as_float((uint32_t) word);
+        }
+        stage[i] = v;
+    }
+    return __syncthreads_and(ok) != 0;
 }
 
 }  // namespace sjkm

@@ -17,16 +17,17 @@ __global__ void __launch_bounds__(256) xchg_exchange_kernel(const float * __rest
                                                             const __grid_constant__ sjkm::XchgArgs x) {
     extern __shared__ float wts[];
     __shared__ float s_red[16];
+    __shared__ __align__(16) float stage[SJK_XCHG_MAX_WORLD * sjkm::XCHG_TILE_WORDS];
     const int row = blockIdx.x, tile = blockIdx.y, d0 = 64 * tile, tid = threadIdx.x;
     const float * pr = part + (size_t) row * (D + 2);
     const float my_o = (tid < 64 && d0 + tid < D) ? pr[2 + d0 + tid] : 0.0f;
-    if (!sjkm::xchg_publish_wait(x, n_rows, D, row, tile, pr[0], pr[1], my_o)) {
+    if (!sjkm::xchg_publish_gather(x, n_rows, D, row, tile, pr[0], pr[1], my_o, stage)) {
         if (tid < 64 && d0 + tid < D) out[(size_t) row * D + d0 + tid] = 0.0f;
         if (tid == 0) atomicOr(&xchg_status, (int) SJK_DEVICE_TIMEOUT);
         return;
     }
     float m, t;
-    sjkm::merge_tile<true>(sjkm::xchg_slots(x, n_rows, D), x.world, n_rows, D, row, d0, wts, s_red, m, t);
+    sjkm::merge_tile(stage, x.world, 1, sjkm::XCHG_TILE_WORDS - 2, 0, 0, wts, s_red, m, t);
     sjkm::store_out(wts + x.world, t, D, row, d0, out);
 }
 
@@ -41,7 +42,7 @@ bool valid(const sjk_xchg_peers * x) {
 
 extern "C" size_t sjk_xchg_bytes(int world, int n_rows, int D) {
     if (world <= 0 || world > SJK_XCHG_MAX_WORLD || n_rows <= 0 || D <= 0 || (D & 1)) return 0;
-    return sjkm::xchg_flag_bytes(n_rows, D) + 2 * (size_t) world * n_rows * (size_t) (D + 2) * sizeof(float);
+    return sjkm::xchg_words_bytes(world, n_rows, D);
 }
 
 extern "C" int sjk_xchg_alloc(size_t bytes, void ** buf, void * ipc_handle) {
