@@ -214,8 +214,10 @@ class AttnStep:
         self.L = sjk.lib()
         nl = len(m.layers)
         self.q = torch.stack([m.syn.queries(il, n_q) for il in range(nl)]).contiguous()     # [nl][n_q][HQ][D]
+        self.q_model = self.q.clone()                   # the model basis (sjk_layer_attend_model rotates inside)
         sjk.check(self.L.sjk_hadamard(C.c_void_p(self.q.data_ptr()), nl * n_q * HQ, D, None), "hadamard")
         self.out = torch.empty_like(self.q)
+        self.out_model = torch.empty_like(self.q)
         torch.cuda.synchronize()
         self.per = n_q * HQ * D
         self.B, self.N = m.pol.B, m.n
@@ -235,6 +237,15 @@ class AttnStep:
     def step(self):
         for il in range(len(self.m.layers)):
             self.attend(il)
+
+    def step_model(self):
+        """The same calls with the rotation folded in: model-basis queries in, model-basis outputs out."""
+        for il in range(len(self.m.layers)):
+            rc = self.L.sjk_layer_attend_model(C.byref(self.m.layers[il]), self.B, self.N, self.N - self.n_q, self.n_q, HQ,
+                                               C.c_void_p(self.q_model.data_ptr() + il * self.per * 4), SCALE,
+                                               C.c_void_p(self.out_model.data_ptr() + il * self.per * 4), self.st)
+            if rc:
+                raise self.sjk.SjkError(rc, "attend_model")
 
     def step_e2e(self):
         T, s = self.T, self.s
@@ -272,14 +283,15 @@ def run_config1(args, torch, dist, local_rank):
     with Clocks(local_rank) as clk:
         ms = time_events(torch, s, a.step, args.steps, args.warmup, barrier)
     ms_e2e = time_events(torch, s, a.step_e2e, args.steps, args.warmup, barrier)
+    ms_model = time_events(torch, s, a.step_model, args.steps, args.warmup, barrier)
     a.step()
     torch.cuda.synchronize()
     out0 = a.out[0].cpu().numpy().copy()                            # layer 0's output, for the parity check
     if dist:
-        t = torch.tensor([ms, ms_e2e], device="cuda")
+        t = torch.tensor([ms, ms_e2e, ms_model], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_e2e = float(t[0]), float(t[1])
-    res = dict(ms=ms, ms_e2e=ms_e2e, B=m.pol.B, N=m.n, build_s=build_s, clocks=clk.summary(), h2d=a.bytes_h2d(),
+        ms, ms_e2e, ms_model = float(t[0]), float(t[1]), float(t[2])
+    res = dict(ms=ms, ms_e2e=ms_e2e, ms_model=ms_model, B=m.pol.B, N=m.n, build_s=build_s, clocks=clk.summary(), h2d=a.bytes_h2d(),
                d2h=a.bytes_d2h(), launches_per_step=2 * len(m.layers), out0=out0)
     m.free()
     return res
@@ -998,6 +1010,10 @@ def main():
                    "parallelism": f"sequence replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (16 layers x 113 MB per step)"},
         "e2e": {"value": us_call_e2e, "unit": "us/call", "h2d_bytes_per_step": c1["h2d"], "d2h_bytes_per_step": c1["d2h"]},
+        "model_basis": {"value": c1["ms_model"] / 16 * 1e3, "unit": "us/call",
+                        "what": "sjk_layer_attend_model: model-basis queries in and outputs out, the rotations inside the "
+                                "call (queries on chip in the body kernel, outputs in the merge kernel's clusters); the "
+                                "headline takes rotated queries as sj_kvarn_layer_attend_row does"},
         "gpu_launches": c1["launches_per_step"] * args.steps,
         "clocks": c1["clocks"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -378,6 +378,17 @@ int sjk_attend_batch(const sjk_view * views, const uint32_t * B, const uint32_t 
                      int n_q, int n_head, const float * q, float scale, float * out, void * scratch, size_t scratch_bytes,
                      sjk_stream st);
 
+/* sjk_attend / sjk_layer_attend with the rotation folded in: q ([n_q][n_head][D], DEVICE) in the model basis and out
+ * in the model basis, where sjk_attend takes and returns rotated rows (the reference's attend_row contract, whose
+ * caller rotates: README.md:44-54). The 4-bit body kernel rotates its queries on chip and the merge kernel rotates
+ * the outputs (the D / 64 tile CTAs of a row as one cluster); calls that read q in other kernels rotate it once into
+ * the scratch first. Outputs equal sjk_hadamard(q) -> sjk_attend -> sjk_hadamard(out) bit for bit. D = 128, 256 or
+ * 512; scratch: sjk_attend_scratch_bytes() bytes. */
+int sjk_attend_model(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, const float * q,
+                     float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st);
+int sjk_layer_attend_model(const sj_kvarn_layer * L, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                           const float * q, float scale, float * out, sjk_stream st);
+
 /* sjk_attend for callers that cannot allocate device memory - code that runs where cudaMalloc is off
  * limits, such as inside a stream capture, a custom allocator's own callbacks or an engine whose memory
  * is planned ahead. No counterpart in the reference. The scratch for the split partials is a fixed 16 MiB

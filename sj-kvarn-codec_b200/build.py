@@ -13,7 +13,7 @@ LIB = os.path.join(HERE, "libsjk_b200.so")
 OBJDIR = os.path.join(HERE, "_build")
 SOURCES = ["sjk_stage.cu", "sjk_seal.cu", "sjk_decode.cu", "sjk_attend.cu", "sjk_attend_tc.cu", "sjk_attend_dense.cu",
            "sjk_attend_trellis.cu", "sjk_attend_batch.cu", "sjk_synth.cu", "sjk_xchg.cu", "sjk_pool.cu", "sjk_host.cpp"]
-HEADERS = ["sjk_common.cuh", "sjk_internal.h", "sjk_tables.h", "sjk_tc.cuh", "sjk_desc.cuh", "sjk_plan.cuh", "sjk_synth.h", "sjk_merge.cuh", "../../include/sjk.h"]
+HEADERS = ["sjk_common.cuh", "sjk_internal.h", "sjk_tables.h", "sjk_tc.cuh", "sjk_desc.cuh", "sjk_plan.cuh", "sjk_synth.h", "sjk_merge.cuh", "sjk_fwht.cuh", "../../include/sjk.h"]
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]

@@ -12,7 +12,10 @@
 // softmax + merge instead of one position-ordered pass), which the 1e-3 relative contract covers.
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "sjk_common.cuh"
+#include "sjk_fwht.cuh"
 #include "sjk_internal.h"
 #include "sjk_merge.cuh"
 #include "sjk_plan.cuh"
@@ -253,8 +256,10 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     __shared__ float s_red[16];
     const int row = blockIdx.x, d0 = blockIdx.y * 64;
     const int tid = threadIdx.x;
-    // launched as a programmatic dependent of the kernels that write the partials: wait until they completed
+    // launched as a programmatic dependent of the kernels that write the partials: wait until they completed; a
+    // kernel launched as this one's dependent (the exchange of sjk_attend_partial_xchg) may be set up meanwhile
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     if (splits_dev) splits = *splits_dev;
     float m, t;
     sjkm::merge_tile(part, splits, n_rows, D, row, d0, wts, s_red, m, t);
@@ -265,6 +270,53 @@ __global__ void __launch_bounds__(256) attend_merge_kernel(const float * part, i
     } else {
         sjkm::store_out(acc, t, D, row, d0, out);
     }
+}
+
+// The merge for outputs in the model basis (sjk_attend_model): the D / 64 tile CTAs of a row form one cluster; each
+// normalises its 64 outputs as attend_merge_kernel does and stores them into the shared row of the cluster's first
+// CTA, which applies the rotation (the reference's FWHT, an involution at scale 1/sqrt(D)) and writes the row.
+template <int D>
+__global__ void __launch_bounds__(256) attend_merge_rot_kernel(const float * part, int splits, int n_rows, float * out,
+                                                               float fwht_scale) {
+    namespace cg = cooperative_groups;
+    extern __shared__ float wts[];
+    __shared__ float s_red[16];
+    __shared__ __align__(16) float rowbuf[D];
+    const int row = blockIdx.x, d0 = blockIdx.y * 64, tid = threadIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    float m, t;
+    sjkm::merge_tile(part, splits, n_rows, D, row, d0, wts, s_red, m, t);
+    cg::cluster_group cl = cg::this_cluster();
+    float * dst = cl.map_shared_rank(rowbuf, 0);
+    if (tid < 64) {
+        const float s_inv = t == 0.0f ? 0.0f : 1.0f / t;
+        dst[d0 + tid] = sjkm::acc_o(wts + splits, tid) * s_inv;
+    }
+    cl.sync();
+    if (cl.block_rank() == 0 && tid < 32) {
+        constexpr int VPL = D / 32;
+        float v[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) v[i] = rowbuf[tid * VPL + i];
+        fwht_warp<VPL>(v, tid, fwht_scale);
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) out[(size_t) row * D + tid * VPL + i] = v[i];
+    }
+}
+
+// model-basis queries of a call rotated into the call's scratch (the calls whose kernels other than the 4-bit body
+// kernel read q): one warp per row, the reference's FWHT
+template <int D>
+__global__ void __launch_bounds__(256) rotate_rows_kernel(const float * src, float * dst, int n_rows, float fwht_scale) {
+    constexpr int VPL = D / 32;
+    const int lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= n_rows) return;
+    float v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) v[i] = src[(size_t) row * D + lane * VPL + i];
+    fwht_warp<VPL>(v, lane, fwht_scale);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) dst[(size_t) row * D + lane * VPL + i] = v[i];
 }
 
 template <int D>
@@ -339,9 +391,34 @@ int launch_split(const AttnParams & p, const AttnParams * dyn, int splits, int n
 // Programmatic dependent launch: the merge grid is set up while the partial kernels run and waits for them on the
 // device (griddepcontrol.wait), so the launch gap between the two kernels disappears. splits_dev: the split count
 // is read from device memory (shared memory sized for max_splits).
+// rot_out: out in the model basis (attend_merge_rot_kernel, clusters of the D / 64 tiles of a row)
 int launch_merge(const float * part, int splits, const int * splits_dev, int max_splits, int n_rows, int D, float * out,
-                 float * part_out, sjk_stream st) {
+                 float * part_out, sjk_stream st, bool rot_out = false) {
     const int n_w = splits_dev ? max_splits : splits;
+    if (rot_out) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned) n_rows, (unsigned) (D / 64));
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = (size_t) (splits + 256) * sizeof(float);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1; attr[1].val.clusterDim.y = (unsigned) (D / 64); attr[1].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        const float sc = sjk_fwht_scale(D);
+        cudaError_t e;
+        switch (D) {
+            case 128: e = cudaLaunchKernelEx(&cfg, attend_merge_rot_kernel<128>, part, splits, n_rows, out, sc); break;
+            case 256: e = cudaLaunchKernelEx(&cfg, attend_merge_rot_kernel<256>, part, splits, n_rows, out, sc); break;
+            case 512: e = cudaLaunchKernelEx(&cfg, attend_merge_rot_kernel<512>, part, splits, n_rows, out, sc); break;
+            default: return SJK_ERR_UNSUPPORTED;
+        }
+        if (sjk_check(e)) return SJK_ERR_DEVICE;
+        return sjk_check_launch();
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) n_rows, (unsigned) ((D + 63) / 64));
     cfg.blockDim = dim3(256);
@@ -360,9 +437,11 @@ int launch_merge(const float * part, int splits, const int * splits_dev, int max
 
 }  // namespace
 
-int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
-                     const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
-                     unsigned regions, float * part_out) {
+namespace {
+// model: q in the model basis and out in the model basis (sjk_attend_model); otherwise both rotated
+int attend_heads_impl(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
+                      const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
+                      unsigned regions, float * part_out, bool model) {
     if (!v || !q || !(out || part_out) || n_q <= 0 || n_head <= 0 || n_kv <= 0 || kv_head0 < 0 || kv_head0 + n_kv > v->n_head_kv ||
         n_head % n_kv)
         return SJKVARN_ERR_ARG;
@@ -382,10 +461,31 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
     const size_t need = (size_t) (splits_tc_max + d.splits_d + d.splits_v1) * n_q * n_head * (v->lay.D + 2) * sizeof(float);
     if (!scratch || scratch_bytes < need) return SJKVARN_ERR_ARG;
     if (splits_tc_max + d.splits_d + d.splits_v1 > MERGE_SPLITS) return SJK_ERR_UNSUPPORTED;
+    // model-basis queries: the 4-bit body kernel rotates them on chip when it is the call's only reader of q; otherwise
+    // they are rotated once into the end of the scratch, which sjk_attend_scratch_bytes() sizes for it
+    bool q_on_chip = false;
+    if (model) {
+        const int D = v->lay.D;
+        if (D != 128 && D != 256 && D != 512) return SJK_ERR_UNSUPPORTED;
+        q_on_chip = pa.tc_body && splits_tc_max > 0 && d.splits_d == 0 && d.splits_v1 == 0 && D == 256;
+        if (!q_on_chip) {
+            const size_t qb = (size_t) n_q * n_head * D * sizeof(float);
+            const size_t off = scratch_bytes >= qb ? (scratch_bytes - qb) & ~(size_t) 255 : 0;
+            if (scratch_bytes < qb || off < need) return SJKVARN_ERR_ARG;
+            float * qr = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + off);
+            const dim3 grid((unsigned) ((n_q * n_head + 7) / 8)), block(256);
+            const float sc = sjk_fwht_scale(D);
+            if (D == 128) rotate_rows_kernel<128><<<grid, block, 0, st>>>(q, qr, n_q * n_head, sc);
+            else if (D == 256) rotate_rows_kernel<256><<<grid, block, 0, st>>>(q, qr, n_q * n_head, sc);
+            else rotate_rows_kernel<512><<<grid, block, 0, st>>>(q, qr, n_q * n_head, sc);
+            if (sjk_check_launch()) return SJK_ERR_DEVICE;
+            q = qr;
+        }
+    }
     int splits_tc = 0;
     if (splits_tc_max) {
         const int rc = pa.tc_body ? sjk_tc_body_launch(v, B, N, d.n_tc, (int) d.dense_regions, qpos0, n_q, n_head, kv_head0, n_kv, q,
-                                                       scale, (float *) scratch, 0, 148 - d.dense_sms, &splits_tc, st)
+                                                       scale, (float *) scratch, 0, 148 - d.dense_sms, q_on_chip, &splits_tc, st)
                                   : sjk_tc_trellis_launch(v, B, N, d.n_tc, qpos0, n_q, n_head, kv_head0, n_kv, q, scale,
                                                           (float *) scratch, 0, d.splits_tc, &splits_tc, st);
         if (rc) return rc;
@@ -408,7 +508,15 @@ int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0,
         const int rc = launch_split(p, nullptr, d.splits_v1, n_kv, st);
         if (rc) return rc;
     }
-    return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, part_out, st);
+    return launch_merge(p.part, splits, nullptr, 0, n_q * n_head, v->lay.D, out, part_out, st, model && !part_out);
+}
+}  // namespace
+
+int sjk_attend_heads(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head, int kv_head0, int n_kv,
+                     const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st,
+                     unsigned regions, float * part_out) {
+    return attend_heads_impl(v, B, N, qpos0, n_q, n_head, kv_head0, n_kv, q, scale, out, scratch, scratch_bytes, st, regions,
+                             part_out, false);
 }
 
 // ---- descriptor-driven attention (the reference's region-aware flash attention op, INTEGRATION_LLAMACPP.md:50) ----
@@ -577,6 +685,15 @@ extern "C" int sjk_attend(const sjk_view * v, uint32_t B, uint32_t N, uint32_t q
     if (!v) return SJKVARN_ERR_ARG;
     return sjk_attend_heads(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st,
                             SJK_REGION_ALL, nullptr);
+}
+
+// sjk_attend with queries and outputs in the model basis: the rotation happens inside the call (on chip in the 4-bit
+// body kernel and in the merge kernel's clusters, or one rotation launch for the other kernels' queries)
+extern "C" int sjk_attend_model(const sjk_view * v, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                                const float * q, float scale, float * out, void * scratch, size_t scratch_bytes, sjk_stream st) {
+    if (!v || !out) return SJKVARN_ERR_ARG;
+    return attend_heads_impl(v, B, N, qpos0, n_q, n_head, 0, v->n_head_kv, q, scale, out, scratch, scratch_bytes, st,
+                             SJK_REGION_ALL, nullptr, true);
 }
 
 // ---- attention for callers that cannot allocate ------------------------------------------------------------

@@ -26,6 +26,7 @@
 // Every wait is bounded (sjk_tc.cuh); a role whose wait runs out stops, the others run out in turn, and the
 // issuer drains its own copies and MMAs before the TMEM is released.
 #include "sjk_common.cuh"
+#include "sjk_fwht.cuh"
 #include "sjk_internal.h"
 #include "sjk_plan.cuh"
 #include "sjk_tc.cuh"
@@ -59,8 +60,9 @@ struct TcParams {
     // divisions are done once on the host
     uint32_t row_iq[NR];        // r / grp
     int row_q[NR];              // iq n_head + r % grp: q row (and partial row) of r, less hl grp
-    const float * q;
+    const float * q;            // rotated queries, or model-basis ones for the QROT kernel (rotated on chip)
     float scale;
+    float fwht_scale;           // 1/sqrt(D) of the query rotation (QROT kernel)
     float * part;               // [splits][n_q*n_head][D + 2]
     int split0;                 // partial slot of this kernel's first split
     int n_splits;               // splits per KV head (the descriptor-driven grid may be wider)
@@ -122,6 +124,10 @@ enum : uint32_t { DM_ROWP = 256, DM_NRM = 1280, DM_RED = 3328, DM_RED_L = 3584, 
 constexpr uint32_t OFF_DCODE = OFF_DM + DM_END;               // V codes of a chunk, [token][channel] bytes
 constexpr uint32_t OFF_DCENT = OFF_DCODE + 128 * 256;        // centroid (fp16 hi | lo) table, one copy per bank
 constexpr uint32_t SMEM_TOTAL = OFF_DCENT + 64 * 32 * 4;
+// the kernel that takes model-basis queries (QROT) keeps the head's rotated query rows [16][256] after the rest
+constexpr uint32_t OFF_QROT = SMEM_TOTAL;
+constexpr uint32_t SMEM_TOTAL_QROT = OFF_QROT + NR * D * 4;
+static_assert(SMEM_TOTAL_QROT <= 227 * 1024, "shared memory (QROT)");
 constexpr uint32_t OFF_XF = OFF_DCODE;                        // [16][256] outputs on their way out (after the staged rows)
 constexpr uint32_t DCOL_A = 0, DCOL_S = 256, DCOL_O = 320;   // dense TMEM: A (2 blocks x hi|lo), S (2 x 32), O (2 x 32)
 static_assert(128 * D_STG_F16 <= 2 * REC_MAX && 128 * D_STG_TQ6 <= 2 * REC_MAX, "staged rows fit in stages 1..2");
@@ -148,6 +154,9 @@ __device__ __forceinline__ void warp_arrive(uint64_t * bar, int lane) {
     if (lane == 0) tc::mbar_arrive(bar);
 }
 
+// QROT: p.q holds model-basis queries; each CTA rotates its KV head's rows on chip (the reference's FWHT, the same
+// stage order and scale as sjk_hadamard) into shared memory before anything reads them
+template <bool QROT>
 SJK_DEV void body_tc_body(const TcParams & p) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -201,19 +210,37 @@ SJK_DEV void body_tc_body(const TcParams & p) {
         }
     };
     float qx[8];                                        // staged rows: this thread's q values (channel tid % 256)
+    float * qrot = reinterpret_cast<float *>(sm + OFF_QROT);
     if ((uint32_t) split < p.n_dense) {
         set_rowp(chunk_of((uint32_t) split));
-        const int d = tid & 255, r0 = (tid >> 8) * 8;
-        const float * __restrict__ qg = p.q;
+        if (!QROT) {
+            const int d = tid & 255, r0 = (tid >> 8) * 8;
+            const float * __restrict__ qg = p.q;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int r = r0 + i, rr = r < p.rows ? r : 0;
-            qx[i] = tid < 512 ? __ldg(qg + (size_t) (p.row_q[rr] + hl * p.grp) * D + d) : 0.0f;
+            for (int i = 0; i < 8; ++i) {
+                const int r = r0 + i, rr = r < p.rows ? r : 0;
+                qx[i] = tid < 512 ? __ldg(qg + (size_t) (p.row_q[rr] + hl * p.grp) * D + d) : 0.0f;
+            }
         }
+    }
+    if (QROT && warp < NR) {                            // warp r rotates query row r of the head (zeros past rows)
+        const int r = warp;
+        float v[D / 32];
+        const float * qr = p.q + (size_t) (p.row_q[r < p.rows ? r : 0] + hl * p.grp) * D + lane * (D / 32);
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) v[i] = r < p.rows ? __ldg(qr + i) : 0.0f;
+        fwht_warp<D / 32>(v, lane, p.fwht_scale);
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) qrot[r * D + lane * (D / 32) + i] = v[i];
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    if (QROT && (uint32_t) split < p.n_dense) {
+        const int d = tid & 255, r0 = (tid >> 8) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qx[i] = tid < 512 ? qrot[(r0 + i) * D + d] : 0.0f;
+    }
     // the merge kernel that follows may be launched now; it waits for this grid on the device
     asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t tmem = *tmem_slot;
@@ -520,7 +547,7 @@ SJK_DEV void body_tc_body(const TcParams & p) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) qv[i][j] = 0.0f;
             if (r < p.rows) {
-                const float * qr = p.q + (size_t) (p.row_q[r] + hl * p.grp) * D;
+                const float * qr = QROT ? qrot + r * D : p.q + (size_t) (p.row_q[r] + hl * p.grp) * D;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) qv[i][j] = qr[kch[j]];
             }
@@ -906,13 +933,14 @@ SJK_DEV void body_tc_body(const TcParams & p) {
     if (warp == 2 * NW) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
-__global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(const __grid_constant__ TcParams p) { body_tc_body(p); }
+template <bool QROT>
+__global__ void __launch_bounds__(NT, 1) attend_body_tc_kernel(const __grid_constant__ TcParams p) { body_tc_body<QROT>(p); }
 
 // the descriptor-driven form: the plan was made on the device (body_tc_dyn_plan_kernel); the grid covers the most
 // splits a plan can use and the CTAs past the plan's return at once
 __global__ void __launch_bounds__(NT, 1) attend_body_tc_dyn_kernel(const TcParams * __restrict__ pp) {
     if ((int) blockIdx.x >= pp->n_splits) return;
-    body_tc_body(*pp);
+    body_tc_body<false>(*pp);
 }
 
 // fp64 steps of the record balancing, rounded as written (the device form must not contract them into fma)
@@ -954,7 +982,7 @@ SJK_HD int fill_plan(TcParams & p, const sjk_view & v, uint32_t B, uint32_t N, u
         p.row_iq[r] = (uint32_t) iq;
         p.row_q[r] = iq * n_head + g;
     }
-    p.q = q; p.scale = scale; p.part = part; p.split0 = split0;
+    p.q = q; p.scale = scale; p.fwht_scale = 0.0f; p.part = part; p.split0 = split0;
     p.sink = v.sink; p.ring = v.ring; p.staging = v.staging; p.sink_type = v.sink_type; p.cap = v.cap;
     p.stage_bytes = (uint32_t) v.stage_bytes; p.B = B; p.N = N;
     p.n_sink_chunks = 0; p.n_dense = 0;
@@ -1017,15 +1045,23 @@ int sjk_tc_body_max_splits(int n_kv) {
 
 int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int max_ctas,
-                       int * splits_out, sjk_stream st) {
+                       bool q_model, int * splits_out, sjk_stream st) {
     TcParams p;
     const int splits = fill_plan(p, *v, B, N, n_rec, dense_regions, qpos0, n_q, n_head, kv0, n_kv, q, scale, part, split0, true,
                                  max_ctas);
+    p.fwht_scale = sjk_fwht_scale(D);
     *splits_out = splits;
     if (splits == 0) return 0;
-    cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
+    const dim3 grid((unsigned) splits, (unsigned) n_kv);
+    if (q_model) {
+        cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL_QROT);
+        if (e != cudaSuccess) return sjk_check(e);
+        attend_body_tc_kernel<true><<<grid, NT, SMEM_TOTAL_QROT, st>>>(p);
+        return sjk_check_launch();
+    }
+    cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
-    attend_body_tc_kernel<<<dim3((unsigned) splits, (unsigned) n_kv), NT, SMEM_TOTAL, st>>>(p);
+    attend_body_tc_kernel<false><<<grid, NT, SMEM_TOTAL, st>>>(p);
     return sjk_check_launch();
 }
 

@@ -388,21 +388,35 @@ extern "C" int sjk_layer_seal(sj_kvarn_layer * L, uint32_t B_from, uint32_t B_to
     return sjk_seal_ring(&vw, L->body, B_from, B_to, L->cfg.iters, st);
 }
 
+// the layer's attention scratch, grown to `need` (outside any stream capture; the old buffer is released after the
+// stream drains)
+static int layer_work(const sj_kvarn_layer * L, size_t need, sjk_stream st) {
+    if (need <= L->work_bytes) return 0;
+    void * w = NULL;
+    if (ck(cudaStreamSynchronize(st))) return SJK_ERR_DEVICE;
+    if (ck(cudaMalloc(&w, need))) return SJK_ERR_DEVICE;
+    sj_kvarn_layer * Lm = (sj_kvarn_layer *) L;
+    cudaFree(Lm->work);
+    Lm->work = w; Lm->work_bytes = need;
+    return 0;
+}
+
 extern "C" int sjk_layer_attend(const sj_kvarn_layer * L, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
                                 const float * q, float scale, float * out, sjk_stream st) {
     sjk_view vw;
     sjk_layer_view(L, &vw);
-    const size_t need = sjk_attend_scratch_bytes(&vw, N, n_q, n_head);
-    if (need > L->work_bytes) {
-        // grow the layer's scratch (outside any stream capture; the old buffer is released after the stream drains)
-        void * w = NULL;
-        if (ck(cudaStreamSynchronize(st))) return SJK_ERR_DEVICE;
-        if (ck(cudaMalloc(&w, need))) return SJK_ERR_DEVICE;
-        sj_kvarn_layer * Lm = (sj_kvarn_layer *) L;
-        cudaFree(Lm->work);
-        Lm->work = w; Lm->work_bytes = need;
-    }
+    const int rc = layer_work(L, sjk_attend_scratch_bytes(&vw, N, n_q, n_head), st);
+    if (rc) return rc;
     return sjk_attend(&vw, B, N, qpos0, n_q, n_head, q, scale, out, L->work, L->work_bytes, st);
+}
+
+extern "C" int sjk_layer_attend_model(const sj_kvarn_layer * L, uint32_t B, uint32_t N, uint32_t qpos0, int n_q, int n_head,
+                                      const float * q, float scale, float * out, sjk_stream st) {
+    sjk_view vw;
+    sjk_layer_view(L, &vw);
+    const int rc = layer_work(L, sjk_attend_scratch_bytes(&vw, N, n_q, n_head), st);
+    if (rc) return rc;
+    return sjk_attend_model(&vw, B, N, qpos0, n_q, n_head, q, scale, out, L->work, L->work_bytes, st);
 }
 
 extern "C" void sj_kvarn_layer_store(sj_kvarn_layer * L, uint32_t pos, const float * k_rot, const float * v_rot) {

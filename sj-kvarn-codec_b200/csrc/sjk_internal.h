@@ -27,10 +27,11 @@ int sjk_record_accum_v(const sj_kvarn_layout * lay, const uint8_t * rec, const f
 // number of partial slots per query row the launch writes (from split0).
 int sjk_tc_body_supported(const sjk_view * v, int n_q, int grp);
 int sjk_tc_body_max_splits(int n_kv);
-// max_ctas: SMs the kernel may take (fewer than 148 when the dense kernel runs beside it)
+// max_ctas: SMs the kernel may take (fewer than 148 when the dense kernel runs beside it); q_model: q holds model-basis
+// queries, which the kernel rotates on chip
 int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_rec, int dense_regions, uint32_t qpos0, int n_q,
                        int n_head, int kv0, int n_kv, const float * q, float scale, float * part, int split0, int max_ctas,
-                       int * splits_out, sjk_stream st);
+                       bool q_model, int * splits_out, sjk_stream st);
 
 // tensor-core attention over the sealed body of a trellis layer (2- and 3-bit codes, sjk_attend_trellis.cu)
 int sjk_tc_trellis_supported(const sjk_view * v, int n_q, int grp);

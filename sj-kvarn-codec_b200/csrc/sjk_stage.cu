@@ -10,6 +10,7 @@
 // blocks of a whole position are assembled in shared memory and leave in 16-byte stores, because a
 // position's slot ([H][K row | V row], 1568 B at D=256, H=4) is contiguous and 16-byte aligned.
 #include "sjk_common.cuh"
+#include "sjk_fwht.cuh"
 #include "sjk_desc.cuh"
 
 namespace {
@@ -31,34 +32,6 @@ struct StoreParams {
     const int32_t * desc;   // sjk_store_dyn: pos0 is the descriptor's QPOS0, read when the kernel runs
     sjk_desc_ref dref;
 };
-
-template <int VPL>
-SJK_DEV void fwht_warp(float (&x)[VPL], int lane, float scale) {
-    // stages inside a lane: partners j, j+h with h < VPL
-#pragma unroll
-    for (int h = 1; h < VPL; h <<= 1) {
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            if ((j & h) == 0) {
-                const float a = x[j], b = x[j + h];
-                x[j] = __fadd_rn(a, b);
-                x[j + h] = __fsub_rn(a, b);
-            }
-        }
-    }
-    // stages across lanes: partner lane ^ m holds index +- h (h = m*VPL)
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-        const bool upper = (lane & m) != 0;
-#pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            const float o = __shfl_xor_sync(FULL, x[j], m);
-            x[j] = upper ? __fsub_rn(o, x[j]) : __fadd_rn(x[j], o);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) x[j] = __fmul_rn(x[j], scale);
-}
 
 // code = number of decision midpoints not above v, as the reference's binary search
 // (sj_kvarn.h:1211-1219); NaN compares false everywhere and ends on 63
@@ -293,12 +266,6 @@ __global__ void __launch_bounds__(256) hadamard_kernel(float * x, int n_rows, fl
     for (int i = 0; i < VPL; ++i) r[lane * VPL + i] = v[i];
 }
 
-float host_fwht_scale(int n) {
-    // 1/sqrt(n) rounded as the reference does: FDIV(1, sqrtf(n)) (sj_kvarn.h:747)
-    volatile float s = sqrtf((float) n);
-    volatile float r = 1.0f / s;
-    return r;
-}
 
 }  // namespace
 
@@ -308,7 +275,7 @@ extern "C" int sjk_hadamard(float * x, int n_rows, int n, sjk_stream st) {
     if (!x || n_rows < 0) return SJKVARN_ERR_ARG;
     if (n_rows == 0) return 0;
     const dim3 grid((unsigned) ((n_rows + 7) / 8)), block(256);
-    const float s = host_fwht_scale(n);
+    const float s = sjk_fwht_scale(n);
     switch (n) {
         case 128: hadamard_kernel<128><<<grid, block, 0, st>>>(x, n_rows, s); break;
         case 256: hadamard_kernel<256><<<grid, block, 0, st>>>(x, n_rows, s); break;
@@ -361,7 +328,7 @@ extern "C" int sjk_store_batch(const sjk_view * views, const uint32_t * pos, int
     StoreParams & p = b.c;
     p.S = v0.S; p.cap = v0.cap; p.H = v0.n_head_kv; p.pos0 = 0;
     p.staging = v0.staging; p.sink_f16 = v0.sink_type == SJKVARN_SINK_F16; p.rotate = rotate;
-    p.fwht_scale = host_fwht_scale(v0.lay.D); p.stage_bytes = (uint32_t) v0.stage_bytes;
+    p.fwht_scale = sjk_fwht_scale(v0.lay.D); p.stage_bytes = (uint32_t) v0.stage_bytes;
     p.sink = nullptr; p.ring = nullptr;
     const int warps = 2 * p.H < 8 ? 2 * p.H : 8;
     const size_t smem = 128 * sizeof(float) + (size_t) 2 * p.H * p.stage_bytes;
@@ -396,7 +363,7 @@ int store_launch(const sjk_view * v, uint8_t * sink, uint8_t * ring, uint32_t po
     p.desc = desc; p.dref = sjk_desc_ref_of(*v);
     p.k = k; p.v = vv; p.sink = sink; p.ring = ring; p.pos0 = pos0; p.S = v->S; p.cap = v->cap; p.H = v->n_head_kv;
     p.staging = v->staging; p.sink_f16 = v->sink_type == SJKVARN_SINK_F16; p.rotate = rotate;
-    p.fwht_scale = host_fwht_scale(v->lay.D); p.stage_bytes = (uint32_t) v->stage_bytes;
+    p.fwht_scale = sjk_fwht_scale(v->lay.D); p.stage_bytes = (uint32_t) v->stage_bytes;
     const int warps = 2 * p.H < 8 ? 2 * p.H : 8;
     const size_t smem = 128 * sizeof(float) + (size_t) 2 * p.H * p.stage_bytes;
     if (smem > 48 * 1024) return SJK_ERR_UNSUPPORTED;

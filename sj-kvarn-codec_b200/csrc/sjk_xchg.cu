@@ -19,6 +19,8 @@ __global__ void __launch_bounds__(256) xchg_exchange_kernel(const float * __rest
     __shared__ float s_red[16];
     __shared__ __align__(16) float stage[SJK_XCHG_MAX_WORLD * sjkm::XCHG_TILE_WORDS];
     const int row = blockIdx.x, tile = blockIdx.y, d0 = 64 * tile, tid = threadIdx.x;
+    // launched as a programmatic dependent of the kernel that writes part (sjk_attend_partial_xchg's merge): wait for it
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float * pr = part + (size_t) row * (D + 2);
     const float my_o = (tid < 64 && d0 + tid < D) ? pr[2 + d0 + tid] : 0.0f;
     if (!sjkm::xchg_publish_gather(x, n_rows, D, row, tile, pr[0], pr[1], my_o, stage)) {
@@ -86,8 +88,17 @@ extern "C" int sjk_xchg_exchange(const sjk_xchg_peers * x, const float * part, i
     sjkm::XchgArgs xa = {};
     xa.world = x->world; xa.rank = x->rank; xa.epoch = epoch;
     for (int i = 0; i < x->world; ++i) xa.buf[i] = reinterpret_cast<uint8_t *>(x->buf[i]);
-    xchg_exchange_kernel<<<dim3((unsigned) n_rows, (unsigned) sjkm::merge_tiles(D)), 256, (size_t) (x->world + 256) * sizeof(float),
-                           st>>>(part, n_rows, D, out, xa);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) n_rows, (unsigned) sjkm::merge_tiles(D));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t) (x->world + 256) * sizeof(float);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (sjk_check(cudaLaunchKernelEx(&cfg, xchg_exchange_kernel, part, n_rows, D, out, xa))) return SJK_ERR_DEVICE;
     return sjk_check_launch();
 }
 

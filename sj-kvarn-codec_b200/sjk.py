@@ -159,6 +159,8 @@ SIGNATURES = {
     "sjk_decode": (C.c_int, [P(Layout), vp, C.c_int, vp, vp, vp]),
     "sjk_attend_scratch_bytes": (C.c_size_t, [P(View), u32, C.c_int, C.c_int]),
     "sjk_attend": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp, C.c_size_t, vp]),
+    "sjk_attend_model": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp, C.c_size_t, vp]),
+    "sjk_layer_attend_model": (C.c_int, [P(Layer), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sjk_attend_static": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, vp, C.c_float, vp, vp]),
     "sjk_attend_partial": (C.c_int, [P(View), u32, u32, u32, C.c_int, C.c_int, C.c_uint, vp, C.c_float, vp, vp, C.c_size_t, vp]),
     "sjk_attend_merge": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, vp]),

@@ -360,3 +360,36 @@ def test_record_scores_and_accum_v_match_reference(L, oracle_lib, bk, bv, body):
         acc = acc0.copy()
         R.sj_kvarn_record_accum_v(C.byref(lay), rec.ctypes.data, w.ctypes.data, n, acc.ctypes.data)
         assert np.array_equal(gu.host(dacc, np.uint32), acc.view(np.uint32)), n
+
+
+@pytest.mark.parametrize("D,bk,bv,body,staging", [(256, 4, 4, 0, 0), (256, 4, 4, 0, 1), (256, 3, 2, 1, 0), (128, 4, 4, 0, 0),
+                                                   (256, 4, 2, 0, 0)])
+def test_attend_model_basis(L, oracle_lib, D, bk, bv, body, staging):
+    """The rotation folded into the call (sjk_layer_attend_model: model-basis queries in, model-basis outputs out)
+    equals sjk_hadamard(q) -> sjk_layer_attend -> sjk_hadamard(out) bit for bit: the 4-bit body kernel rotating its
+    queries on chip (D = 256), the trellis, dense and CUDA-core kernels reading a rotated copy, and the merge's
+    clusters rotating the outputs; and it stays within tolerance of the oracle's attention over the model-basis
+    rotation of the same rows."""
+    H = 2
+    layer, oc, B, cfg = _build_pair(L, oracle_lib, D, H, bk, bv, body, staging, True, 1500, 256, 512, 64, seed=17)
+    scale = np.float32(1.0 / np.sqrt(D))
+    for N, n_q, n_head in [(1500, 4, 8), (1500, 1, 2), (B + 40, 2, 4), (100, 2, 4)]:
+        qpos0 = N - n_q
+        q = synth.queries(N + 7, 1, n_q, n_head, D)[0]
+        dq = gu.dev(q)
+        dout = gu.dev_zeros(n_q * n_head * D * 4)
+        sjk.check(L.sjk_layer_attend_model(C.byref(layer), B, N, qpos0, n_q, n_head, gu.ptr(dq), scale, gu.ptr(dout), None))
+        # the same through the explicit rotations
+        dqr = gu.dev(q)
+        sjk.check(L.sjk_hadamard(gu.ptr(dqr), n_q * n_head, D, None))
+        dref = gu.dev_zeros(n_q * n_head * D * 4)
+        sjk.check(L.sjk_layer_attend(C.byref(layer), B, N, qpos0, n_q, n_head, gu.ptr(dqr), scale, gu.ptr(dref), None))
+        sjk.check(L.sjk_hadamard(gu.ptr(dref), n_q * n_head, D, None))
+        assert np.array_equal(gu.host(dout, np.uint32), gu.host(dref, np.uint32)), (N, n_q, n_head)
+        # and against the oracle: attention over the rotated query, its output rotated back on the host
+        qr = oracle_lib.fwht_rows(q.reshape(-1, D).copy()).reshape(n_q, n_head, D)
+        ref = oracle_lib.fwht_rows(oc.attend(B, N, qpos0, qr, scale).reshape(-1, D).copy()).reshape(n_q, n_head, D)
+        assert gu.rel_err_rows(gu.host(dout, np.float32, (n_q, n_head, D)), ref) <= ATTN_TOL_TIGHT, (N, n_q, n_head)
+    assert L.sjk_device_status() == 0
+    L.sj_kvarn_layer_free(C.byref(layer))
+    oc.close()
