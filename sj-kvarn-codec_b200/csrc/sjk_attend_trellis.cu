@@ -23,8 +23,9 @@
 // sequences of a paged pool. Roles, linked only by mbarriers, overlap consecutive records:
 //   warps 0-7    K side   B_K = [Q' hi | Q' lo] and the zero-point sums C, then A_K (shared, MN-major)
 //   warps 8-15   V side   A_V into TMEM (double-buffered), then the epilogue of the previous record
-//   warps 16-19  softmax  scores, online softmax per item, B_V = [P' hi | P' lo], the sums of p and p Vz
-//   warp 20      issuer   bulk copies of records into a 2-stage ring (no multicast), the MMAs, commits
+//   warps 16-23  softmax  scores, online softmax per item, B_V = [P' hi | P' lo], the sums of p and p Vz
+//                         (warps 16-19 at 8 query rows per KV head)
+//   warp 24 (20) issuer   bulk copies of records into a 2-stage ring (no multicast), the MMAs, commits
 // Every wait is bounded; a role whose wait runs out raises a CTA abort flag, the others stop at their next
 // wait, and the issuer drains its own copies and MMAs before the TMEM is released.
 #include <cuda_fp16.h>
@@ -41,8 +42,11 @@ using namespace tc::num;
 constexpr int NR = 16;                  // most query rows per KV head (the kernels pad to 8 or 16; B = [hi | lo] rows)
 constexpr int D = 256;
 constexpr int G = 128;
-constexpr int NT = 672;                 // 8 K-side warps, 8 V-side warps, 4 softmax warps, 1 issuer warp
-constexpr int W_V = 8, W_S = 16, W_I = 20;
+constexpr int W_V = 8, W_S = 16;       // 8 K-side warps, 8 V-side warps, then the softmax warps and 1 issuer warp
+// softmax warps: 8 at 16 query rows (two per TMEM lane quarter, one half of the rows each), 4 at 8 rows
+template <int R> constexpr int SW_N = R == 16 ? 8 : 4;
+template <int R> constexpr int W_I = W_S + SW_N<R>;
+template <int R> constexpr int NT = 32 * (W_I<R> + 1);
 constexpr uint32_t TM_COLS = 512;
 constexpr uint32_t COL_AV = 0, COL_S = 256, COL_O = 320;     // A_V [2 buffers][2 tiles][64] | S [2][32] | O [2 tiles][32]
 constexpr uint32_t REC_MAX = 26880;     // largest trellis record at D = 256 (3/3t)
@@ -97,7 +101,7 @@ constexpr uint32_t OFF_BV = OFF_BK + 2 * TILE_B;                // [P' hi | P' l
 constexpr uint32_t OFF_F = OFF_BV + TILE_B;                     // floats below
 enum : uint32_t {
     F_REDC = 0,         // [2][8 warps][8]   zero-point partials of the K side
-    F_REDM = 128,       // [4 warps][16]     score maxima
+    F_REDM = 128,       // [4 lane quarters][16] score maxima
     F_REDL = 192,       // [4][16]           sums of p
     F_REDZ = 256,       // [4][16]           sums of p Vz
     F_C = 320,          // [2][16]           C[r] per record parity
@@ -265,7 +269,8 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
     // now on the SMs this grid leaves free
     asm volatile("griddepcontrol.launch_dependents;");
     constexpr int RH = R / 2;                                   // B_K rows per thread (two row halves)
-    constexpr int LPR = 32 / R, LPH = 32 / RH;                  // lanes per row after a warp_rows<R> / <RH>
+    constexpr int LPH = 32 / RH;                                // lanes per row after a warp_rows<RH>
+    constexpr int NSW = SW_N<R>, WI = W_I<R>, NTH = NT<R>;
     extern __shared__ __align__(128) uint8_t sm[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const sj_kvarn_layout & l = p.lay;
@@ -277,12 +282,12 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
     uint32_t n = 0;
     for (int i = i0; i < i1; ++i) n += p.item[i].r1 - p.item[i].r0;
 
-    if (warp == W_I) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
-    if (tid == W_I * 32) {
+    if (warp == WI) { tc::tmem_alloc(tmem_slot, TM_COLS); tc::tmem_relinquish(); }
+    if (tid == WI * 32) {
         for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&bars[B_RFULL + i], 1); tc::mbar_init(&bars[B_REMPTY + i], 20);
-            tc::mbar_init(&bars[B_SFULL + i], 1); tc::mbar_init(&bars[B_SFREE + i], 4);
-            tc::mbar_init(&bars[B_CFULL + i], 1); tc::mbar_init(&bars[B_AZFULL + i], 4);
+            tc::mbar_init(&bars[B_RFULL + i], 1); tc::mbar_init(&bars[B_REMPTY + i], WI);
+            tc::mbar_init(&bars[B_SFULL + i], 1); tc::mbar_init(&bars[B_SFREE + i], NSW);
+            tc::mbar_init(&bars[B_CFULL + i], 1); tc::mbar_init(&bars[B_AZFULL + i], NSW);
             tc::mbar_init(&bars[B_AVFULL + i], 8); tc::mbar_init(&bars[B_VDONE + i], 1);
         }
         tc::mbar_init(&bars[B_AKFULL], 8); tc::mbar_init(&bars[B_OFREE], 8);
@@ -293,7 +298,7 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
     {
         const uint16_t * ck = sjk_codebook(BK, 0), * cv = sjk_codebook(BV, 1);
         constexpr int NK = 1 << (6 + BK), NV = 1 << (6 + BV), NI = NK > NV ? NK : NV;
-        for (int i = tid; i < NI * 8; i += NT) {
+        for (int i = tid; i < NI * 8; i += NTH) {
             const int idx = i >> 3;
             const uint32_t w = (uint32_t) (idx < NK ? ck[idx] : 0) | ((uint32_t) (idx < NV ? cv[idx] : 0) << 16);
             reinterpret_cast<uint4 *>(sm + OFF_TBL)[i] = make_uint4(w, w, w, w);
@@ -432,13 +437,22 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
             vc_prev = vc;
         }
         if (ok && n > 0) epilogue(n - 1, vc_prev);
-    } else if (warp < W_I) {
+    } else if (warp < WI) {
         // ================================ softmax ================================
-        const int quarter = warp & 3, t = 32 * quarter + lane;
+        // warp w reads the scores of TMEM lane quarter w % 4 (its 32 tokens) for RS of the R rows from r0 on
+        constexpr int RS = R * 4 / NSW, LPS = 32 / RS;
+        const int quarter = warp & 3, r0 = RS * ((warp - W_S) >> 2), t = 32 * quarter + lane;
         const uint32_t lane_base = (uint32_t) (32 * quarter) << 16;
         const float sl2 = p.scale * LOG2E;
         float M = -INFINITY, L = 0.0f;                          // warp W_S, lane r < 16: running max / sum of row r
         uint32_t g3 = 0;                                        // g % 3: slot of alpha / z (the epilogue of g - 3 is done)
+        auto ldrs = [](const float * src, float (&v)[RS]) {
+#pragma unroll
+            for (int i = 0; i < RS; i += 4) {
+                const float4 x = *reinterpret_cast<const float4 *>(src + i);
+                v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+            }
+        };
         for (uint32_t g = 0; g < n; ++g, cur.next(p), g3 = g3 == 2 ? 0 : g3 + 1) {
             const TwItem & itm = p.item[cur.it];
             const TwSeq & sq = p.seq[itm.seq_hl & 0xFFFFu];
@@ -447,25 +461,27 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
             // every softmax warp reaches the group barriers below on every record, also after a wait gave up
             bool ok = warp_wait(&bars[B_SFULL + s], (g >> 1) & 1u, abort) && warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
                       warp_wait(&bars[B_CFULL + s], (g >> 1) & 1u, abort);
-            float sc[R], vsc = 0.0f, vz = 0.0f;
+            float sc[RS], vsc = 0.0f, vz = 0.0f;
             if (ok) {
                 tc::fence_after_sync();
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
                 const float kt = h2f_at(rec + l.k_tok + 2 * t);
                 vsc = h2f_at(rec + l.v_scale + 2 * t);
                 vz = h2f_at(rec + l.v_zero + 2 * t);
-                float c[R];
-#pragma unroll
-                for (int i = 0; i < R / 8; ++i) ld8(F + F_C + s * NR + 8 * i, *reinterpret_cast<float (*)[8]>(c + 8 * i));
+                float c[RS];
+                ldrs(F + F_C + s * NR + r0, c);
                 // the record stage and C[s] are rewritten only after this arrival (record g + 2)
                 warp_arrive(&bars[B_REMPTY + s], lane);
-                uint32_t a[R], al[R];
-                if constexpr (R == 16) {
-                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s, a);
-                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + R, al);
+                uint32_t a[RS], al[RS];
+                if constexpr (RS == 16) {
+                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + r0, a);
+                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + R + r0, al);
+                } else if constexpr (RS == 8) {
+                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + r0, a);
+                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + R + r0, al);
                 } else {
-                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s, a);
-                    tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + R, al);
+                    tc::ld_x4_u(tmem + lane_base + COL_S + 32 * s + r0, a);
+                    tc::ld_x4_u(tmem + lane_base + COL_S + 32 * s + R + r0, al);
                 }
                 tc::wait_ld();
                 tc::fence_before_sync();
@@ -474,14 +490,15 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
                 const bool in = pos < sq.b_end;
                 const float kts = kt * sl2;
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
+                for (int i = 0; i < RS; ++i) {
+                    const int r = r0 + i;
                     const bool vis = in && r < p.rows && pos < sq.qpos0 + p.row_iq[r] + 1u;
-                    sc[r] = vis ? kts * ((__uint_as_float(a[r]) + __uint_as_float(al[r])) + c[r]) : -INFINITY;
+                    sc[i] = vis ? kts * ((__uint_as_float(a[i]) + __uint_as_float(al[i])) + c[i]) : -INFINITY;
                 }
-                const float mw = warp_rows<R, true>(sc, lane);
-                if (lane % LPR == 0) F[F_REDM + quarter * NR + lane / LPR] = mw;
+                const float mw = warp_rows<RS, true>(sc, lane);
+                if (lane % LPS == 0) F[F_REDM + quarter * NR + r0 + lane / LPS] = mw;
             }
-            if (!tc::nbar_and(2, 128, ok)) break;
+            if (!tc::nbar_and(2, 32 * NSW, ok)) break;
             if (warp == W_S && lane < R) {
                 const int r = lane;
                 const float mrec = fmaxf(fmaxf(F[F_REDM + r], F[F_REDM + NR + r]), fmaxf(F[F_REDM + 2 * NR + r], F[F_REDM + 3 * NR + r]));
@@ -490,30 +507,33 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
                 F[F_MN + r] = mnew;
                 M = mnew;
             }
-            tc::nbar_sync(2, 128);
-            float mn[R];
-#pragma unroll
-            for (int i = 0; i < R / 8; ++i) ld8(F + F_MN + 8 * i, *reinterpret_cast<float (*)[8]>(mn + 8 * i));
+            tc::nbar_sync(2, 32 * NSW);
+            float mn[RS];
+            ldrs(F + F_MN + r0, mn);
             // B_V is free once the V MMAs of the previous record completed
             ok = g == 0 || warp_wait(&bars[B_VDONE + (s ^ 1u)], ((g - 1) >> 1) & 1u, abort);
             if (ok) {
                 uint8_t * bv = sm + OFF_BV;
-                float ls[R], zs[R];
+                float ls[RS], zs[RS];
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const float pw = mn[r] == -INFINITY ? 0.0f : ex2(sc[r] - mn[r]);
-                    ls[r] = pw;
-                    zs[r] = pw * vz;
+                for (int i = 0; i < RS; ++i) {
+                    const int r = r0 + i;
+                    const float pw = mn[i] == -INFINITY ? 0.0f : ex2(sc[i] - mn[i]);
+                    ls[i] = pw;
+                    zs[i] = pw * vz;
                     const float x = pw * vsc;
                     const __half hi = __float2half_rn(x);
                     *reinterpret_cast<__half *>(bv + h_off(r, t)) = hi;
                     *reinterpret_cast<__half *>(bv + h_off(R + r, t)) = __float2half_rn(x - __half2float(hi));
                 }
-                const float lw = warp_rows<R, false>(ls, lane), zw = warp_rows<R, false>(zs, lane);
-                if (lane % LPR == 0) { F[F_REDL + quarter * NR + lane / LPR] = lw; F[F_REDZ + quarter * NR + lane / LPR] = zw; }
+                const float lw = warp_rows<RS, false>(ls, lane), zw = warp_rows<RS, false>(zs, lane);
+                if (lane % LPS == 0) {
+                    F[F_REDL + quarter * NR + r0 + lane / LPS] = lw;
+                    F[F_REDZ + quarter * NR + r0 + lane / LPS] = zw;
+                }
                 tc::fence_proxy_async();
             }
-            if (!tc::nbar_and(2, 128, ok)) break;
+            if (!tc::nbar_and(2, 32 * NSW, ok)) break;
             if (warp == W_S && lane < R) {
                 const int r = lane;
                 const float lsum = (F[F_REDL + r] + F[F_REDL + NR + r]) + (F[F_REDL + 2 * NR + r] + F[F_REDL + 3 * NR + r]);
@@ -567,8 +587,10 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
             }
             return true;
         };
-        prefetch_to(4);
+        // the first two records are copied before anything is prefetched: their requests go first
         bool ok = load_to(2);
+        for (; np < nl; ++np) pc.next(p);
+        prefetch_to(4);
         for (uint32_t g = 0; g < n && ok; ++g) {
             prefetch_to(g + 5);
             ok = wait_bar(&bars[B_AKFULL], g & 1u, abort) && (g < 2 || wait_bar(&bars[B_SFREE + (g & 1u)], ((g - 2) >> 1) & 1u, abort));
@@ -596,18 +618,18 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    if (warp == W_I) tc::tmem_dealloc(tmem, TM_COLS);
+    if (warp == WI) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
 template <int BK, int BV, int R>
-__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
+__global__ void __launch_bounds__(NT<R>, 1) attend_trellis_ws_kernel(const __grid_constant__ TwParams p) {
     trellis_ws_body<BK, BV, R>(p);
 }
 
 // the descriptor-driven form: the work list was planned on the device (trellis_dyn_plan_kernel); the grid covers
 // the most CTAs a plan can use and the CTAs past the plan's return at once
 template <int BK, int BV, int R>
-__global__ void __launch_bounds__(NT, 1) attend_trellis_ws_dyn_kernel(const TwParams * __restrict__ pp) {
+__global__ void __launch_bounds__(NT<R>, 1) attend_trellis_ws_dyn_kernel(const TwParams * __restrict__ pp) {
     if ((int) blockIdx.x >= pp->n_cta) return;
     trellis_ws_body<BK, BV, R>(*pp);
 }
@@ -618,13 +640,13 @@ int launch_kernel(const TwParams & p, const TwParams * dyn, sjk_stream st) {
         auto kfn = attend_trellis_ws_dyn_kernel<BK, BV, R>;
         const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
         if (e != cudaSuccess) return sjk_check(e);
-        kfn<<<(unsigned) p.n_cta, NT, SMEM_TOTAL, st>>>(dyn);
+        kfn<<<(unsigned) p.n_cta, NT<R>, SMEM_TOTAL, st>>>(dyn);
         return sjk_check_launch();
     }
     auto kfn = attend_trellis_ws_kernel<BK, BV, R>;
     const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
-    kfn<<<(unsigned) p.n_cta, NT, SMEM_TOTAL, st>>>(p);
+    kfn<<<(unsigned) p.n_cta, NT<R>, SMEM_TOTAL, st>>>(p);
     return sjk_check_launch();
 }
 
