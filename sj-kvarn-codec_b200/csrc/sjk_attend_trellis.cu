@@ -204,27 +204,21 @@ __device__ __forceinline__ uint32_t pair_at(const uint8_t * tbl, const uint32_t 
     return prmt(lds32(tbl, tbl_off<BITS>(win, j, lane4)), lds32(tbl, tbl_off<BITS>(win, j + 1, lane4)), sel);
 }
 
-// K side: the 128 tokens of one channel as fp16 into its 16 MN-major chunks of A_K (a rolled loop over 4 x 32)
+// K side, 32 tokens at a time: tokens 32 sc .. 32 sc + 31 of one channel as the fp16 pairs of its MN-major A_K
+// chunks 4 sc .. 4 sc + 3 (prev: the stream word before them; w: their BITS words)
 template <int BITS>
-__device__ __forceinline__ void decode_k(const uint8_t * tbl, uint32_t (&w)[4 * BITS], uint32_t lane4, uint8_t * ak_ch) {
-    uint32_t prev = 0;
-#pragma unroll 1
-    for (int sc = 0; sc < 4; ++sc) {
-        uint32_t win[BITS + 1];
-        win[0] = prev;
+__device__ __forceinline__ void decode_k_sub(const uint8_t * tbl, uint32_t prev, const uint32_t * w, uint32_t lane4, uint32_t (&o)[16]) {
+    uint32_t win[BITS + 1];
+    win[0] = prev;
 #pragma unroll
-        for (int i = 0; i < BITS; ++i) win[1 + i] = w[i];
+    for (int i = 0; i < BITS; ++i) win[1 + i] = w[i];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            uint32_t o[4];
+    for (int j = 0; j < 16; ++j) o[j] = pair_at<BITS>(tbl, win, 2 * j, lane4, 0x5410u);
+}
+__device__ __forceinline__ void store_k_sub(uint8_t * ak_ch, int sc, const uint32_t (&o)[16]) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = pair_at<BITS>(tbl, win, 8 * c + 2 * i, lane4, 0x5410u);
-            *reinterpret_cast<uint4 *>(ak_ch + (4 * sc + c) * AK_SBO) = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        prev = w[BITS - 1];
-#pragma unroll
-        for (int i = 0; i < 3 * BITS; ++i) w[i] = w[i + BITS];
-    }
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4 *>(ak_ch + (4 * sc + c) * AK_SBO) = make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 // V side: the 128 tokens of one channel as fp16 pairs (token 2i low) into the thread's TMEM lane
 template <int BITS>
@@ -333,16 +327,29 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
                 }
             }
             const uint32_t s = g & 1u;
-            // every K warp reaches the group barrier below on every record, also after a wait gave up
-            const bool ok = warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort) &&
-                            (g == 0 || warp_wait(&bars[B_SFULL + ((g - 1) & 1u)], ((g - 1) >> 1) & 1u, abort));
+            // every K warp reaches the group barrier below on every record, also after a wait gave up. What only
+            // reads the record (the zero-point partials, the stream words, the first 32 tokens into registers) runs
+            // before the wait for the previous record's K MMAs, which read B_K and A_K.
+            bool ok = warp_wait(&bars[B_RFULL + s], (g >> 1) & 1u, abort);
+            float2 ks = make_float2(0.0f, 0.0f);
+            uint32_t w[4 * BK], o[16];
             if (ok) {
                 tc::fence_after_sync();
                 const uint8_t * rec = sm + OFF_REC + s * REC_MAX;
-                // B_K and the zero-point partials
-                const float2 ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
+                ks = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_scale + 4 * jp));
                 const float2 kz = __half22float2(*reinterpret_cast<const __half2 *>(rec + l.k_zero + 4 * jp));
                 float cz[RH];
+#pragma unroll
+                for (int i = 0; i < RH; ++i) cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
+                const float cw = warp_rows<RH, false>(cz, lane);
+                if (lane % LPH == 0) F[F_REDC + s * 64 + warp * 8 + lane / LPH] = cw;
+                load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
+                warp_arrive(&bars[B_REMPTY + s], lane);
+                decode_k_sub<BK>(tbl, 0u, w, lane4, o);
+            }
+            ok = ok && (g == 0 || warp_wait(&bars[B_SFULL + ((g - 1) & 1u)], ((g - 1) >> 1) & 1u, abort));
+            if (ok) {
+                tc::fence_after_sync();
 #pragma unroll
                 for (int i = 0; i < RH; ++i) {
                     const int r = RH * rh + i;
@@ -352,14 +359,16 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
                     const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
                     *reinterpret_cast<__half2 *>(bk + r * 16) = hi;
                     *reinterpret_cast<__half2 *>(bk + (R + r) * 16) = lo;
-                    cz[i] = fmaf(q2[i].y, kz.y, q2[i].x * kz.x);
                 }
-                const float cw = warp_rows<RH, false>(cz, lane);
-                if (lane % LPH == 0) F[F_REDC + s * 64 + warp * 8 + lane / LPH] = cw;
-                uint32_t w[4 * BK];
-                load_words<BK>(rec + l.k_payload + d * (16 * BK), w);
-                warp_arrive(&bars[B_REMPTY + s], lane);
-                decode_k<BK>(tbl, w, lane4, ak_ch);
+                store_k_sub(ak_ch, 0, o);
+#pragma unroll 1
+                for (int sc = 1; sc < 4; ++sc) {
+                    const uint32_t prev = w[BK - 1];
+#pragma unroll
+                    for (int i = 0; i < 3 * BK; ++i) w[i] = w[i + BK];
+                    decode_k_sub<BK>(tbl, prev, w, lane4, o);
+                    store_k_sub(ak_ch, sc, o);
+                }
                 tc::fence_proxy_async();
             }
             if (!tc::nbar_and(1, 256, ok)) break;               // zero-point partials of all K warps in place
