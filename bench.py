@@ -900,7 +900,7 @@ def main():
     ap.add_argument("--config4-layers", type=int, default=16, help="layers of the config-4 sequence")
     ap.add_argument("--config2-layers", type=int, default=16, help="layers of the config-2 model (fewer only for profiling)")
     ap.add_argument("--config1-layers", type=int, default=16, help="layers of the config-1 model (fewer only for profiling)")
-    ap.add_argument("--only", choices=["seal", "seal2", "config1", "config2", "config3"], default=None,
+    ap.add_argument("--only", choices=["seal", "seal2", "config1", "config2", "config3", "config4"], default=None,
                     help="run one section alone on one GPU and print its numbers (for profiling captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -927,7 +927,8 @@ def main():
         td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
         dist = td
     if args.only:
-        # one section alone (profiling): config 0's or config 2's seal, config 2's attention, or a config-3 pool
+        # one section alone (profiling): config 0's or config 2's seal, config 1's or config 2's attention, a
+        # config-3 pool, or config 4 on one rank (the whole sequence)
         if args.only == "seal":
             r = run_seal0(args, torch)
         elif args.only == "seal2":
@@ -939,8 +940,10 @@ def main():
             r = run_config2(args, torch)
             r.pop("out0", None)
             r["seal"] = {k: r["seal"][k] for k in ("ms", "records")}
-        else:
+        elif args.only == "config3":
             r = run_config3(args, torch, None, 0, 1)
+        else:
+            r = run_config4(args, torch, None, 0, 1)
         print(json.dumps({"only": args.only, **{k: v for k, v in r.items() if not hasattr(v, "shape")}}), flush=True)
         return
     res = run_config1(args, torch, dist, local_rank)
