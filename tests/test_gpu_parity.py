@@ -197,14 +197,15 @@ def test_cache_build_bit_exact(L, oracle_lib, bk, bv, body, staging, sink_f16):
     (128, 0, True, 4, 4, 0), (256, 0, True, 3, 2, 1), (256, 1, False, 3, 3, 1), (256, 0, True, 2, 2, 1)])
 def test_attend_regions_and_shapes(L, oracle_lib, D, staging, sink_f16, bk, bv, body):
     """Attention over every staged-row format (tq6_0 / fp16 ring, fp16 / inherited sink), the 4-bit scalar and
-    the trellis bodies, and the query shapes the kernels take (up to 16 rows per KV head), with N inside the
-    sink, inside the body, at B and past B in a wrapped ring, the query rows causal inside the last chunk."""
+    the trellis bodies, and the query shapes the kernels take (up to 16 rows per KV head; 12 rows fill the 16-row
+    kernels partly), with N inside the sink, inside the body, at B and past B in a wrapped ring, the query rows
+    causal inside the last chunk."""
     H = 2
     layer, oc, B, cfg = _build_pair(L, oracle_lib, D, H, bk, bv, body, staging, sink_f16, 1500, 256, 512, 64, seed=11)
     assert B >= 128 + 5 * 128 and layer.cap < 1500 - 128
     scale = np.float32(1.0 / np.sqrt(D))
-    cases = [(1500, 1, 2), (1500, 1, 8), (1500, 4, 8), (1500, 16, 2), (B + 70, 4, 4), (B, 2, 4), (B - 50, 3, 2),
-             (100, 2, 4), (128 + 1, 1, 2)]
+    cases = [(1500, 1, 2), (1500, 1, 8), (1500, 4, 8), (1500, 16, 2), (1500, 3, 8), (B + 70, 4, 4), (B, 2, 4),
+             (B - 50, 3, 2), (100, 2, 4), (128 + 1, 1, 2)]
     for N, n_q, n_head in cases:
         qpos0 = N - n_q - (3 if N > 200 else 0)
         q = synth.queries(N, 1, n_q, n_head, D)[0]
