@@ -24,7 +24,7 @@
 //   warps 0-7    K side   B_K = [Q' hi | Q' lo] and the zero-point sums C, then A_K (shared, MN-major)
 //   warps 8-15   V side   A_V into TMEM (double-buffered), then the epilogue of the previous record
 //   warps 16-23  softmax  scores, online softmax per item, B_V = [P' hi | P' lo], the sums of p and p Vz
-//                         (warps 16-19 at 8 query rows per KV head)
+//                         (warps 16-19 at 4 or 8 query rows per KV head)
 //   warp 24 (20) issuer   bulk copies of records into a 2-stage ring (no multicast), the MMAs, commits
 // Every wait is bounded; a role whose wait runs out raises a CTA abort flag, the others stop at their next
 // wait, and the issuer drains its own copies and MMAs before the TMEM is released.
@@ -39,11 +39,11 @@ namespace {
 
 using namespace tc::num;
 
-constexpr int NR = 16;                  // most query rows per KV head (the kernels pad to 8 or 16; B = [hi | lo] rows)
+constexpr int NR = 16;                  // most query rows per KV head (the kernels pad to 4, 8 or 16; B = [hi | lo] rows)
 constexpr int D = 256;
 constexpr int G = 128;
 constexpr int W_V = 8, W_S = 16;       // 8 K-side warps, 8 V-side warps, then the softmax warps and 1 issuer warp
-// softmax warps: 8 at 16 query rows (two per TMEM lane quarter, one half of the rows each), 4 at 8 rows
+// softmax warps: 8 at 16 query rows (two per TMEM lane quarter, one half of the rows each), 4 at 4 or 8 rows
 template <int R> constexpr int SW_N = R == 16 ? 8 : 4;
 template <int R> constexpr int W_I = W_S + SW_N<R>;
 template <int R> constexpr int NT = 32 * (W_I<R> + 1);
@@ -245,7 +245,18 @@ template <int R, bool MAX>
 __device__ __forceinline__ float warp_rows(const float (&v)[R], int lane) {
     if constexpr (R == 16) return warp_rows16<MAX>(v, lane);
     else if constexpr (R == 8) return warp_rows8<MAX>(v, lane);
-    else return warp_rows4<MAX>(v, lane);
+    else if constexpr (R == 4) return warp_rows4<MAX>(v, lane);
+    else {                                                      // R = 2: lanes 16 r .. 16 r + 15 hold row r
+        const bool up = lane & 16;
+        const float x = __shfl_xor_sync(0xFFFFFFFFu, up ? v[0] : v[1], 16);
+        float c = MAX ? fmaxf(up ? v[1] : v[0], x) : (up ? v[1] : v[0]) + x;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) {
+            const float y = __shfl_xor_sync(0xFFFFFFFFu, c, o);
+            c = MAX ? fmaxf(c, y) : c + y;
+        }
+        return c;
+    }
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA
@@ -256,7 +267,7 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u));
 }
 
-// R: query rows per KV head the kernel computes (8 or 16, padded; the MMA N is 2 R)
+// R: query rows per KV head the kernel computes (4, 8 or 16, padded; the MMA N is 2 R, at least 16)
 template <int BK, int BV, int R>
 SJK_DEV void trellis_ws_body(const TwParams & p) {
     // a kernel launched as this one's programmatic dependent (the same call's dense kernel, or its merge) may start
@@ -398,18 +409,29 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
             if (!warp_wait(&bars[B_VDONE + es], (e >> 1) & 1u, abort)) return false;
             if (!warp_wait(&bars[B_AZFULL + es], (e >> 1) & 1u, abort)) return false;
             tc::fence_after_sync();
+            constexpr int EW = R < 8 ? R : 8;                   // rows per TMEM load
 #pragma unroll
-            for (int hh = 0; hh < R / 8; ++hh) {
-                uint32_t o[8], ol[8];
-                float al[8], z[8];
-                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + 8 * hh, o);
-                tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + R + 8 * hh, ol);
-                ld8(F + F_AL + e3 * NR + 8 * hh, al);
-                ld8(F + F_Z + e3 * NR + 8 * hh, z);
+            for (int hh = 0; hh < R / EW; ++hh) {
+                uint32_t o[EW], ol[EW];
+                float al[EW], z[EW];
+                if constexpr (EW == 8) {
+                    tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + 8 * hh, o);
+                    tc::ld_x8_u(tmem + lane_base + COL_O + 32 * tile + R + 8 * hh, ol);
+                } else {
+                    tc::ld_x4_u(tmem + lane_base + COL_O + 32 * tile, o);
+                    tc::ld_x4_u(tmem + lane_base + COL_O + 32 * tile + R, ol);
+                }
+#pragma unroll
+                for (int i = 0; i < EW; i += 4) {
+                    const float4 a4 = *reinterpret_cast<const float4 *>(F + F_AL + e3 * NR + EW * hh + i);
+                    const float4 z4 = *reinterpret_cast<const float4 *>(F + F_Z + e3 * NR + EW * hh + i);
+                    al[i] = a4.x; al[i + 1] = a4.y; al[i + 2] = a4.z; al[i + 3] = a4.w;
+                    z[i] = z4.x; z[i + 1] = z4.y; z[i + 2] = z4.z; z[i + 3] = z4.w;
+                }
                 tc::wait_ld();
 #pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    acc[8 * hh + r] = fmaf(acc[8 * hh + r], al[r], vc * ((__uint_as_float(o[r]) + __uint_as_float(ol[r])) + z[r]));
+                for (int r = 0; r < EW; ++r)
+                    acc[EW * hh + r] = fmaf(acc[EW * hh + r], al[r], vc * ((__uint_as_float(o[r]) + __uint_as_float(ol[r])) + z[r]));
             }
             tc::fence_before_sync();
             warp_arrive(&bars[B_OFREE], lane);
@@ -561,8 +583,11 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
         // ================================ issuer ================================
         // In program order: the K MMAs of record g, the V MMAs of record g - 1, the bulk copy of record g + 2; each
         // after blocking waits. Records up to four ahead are prefetched into L2, so the bulk copies read from it.
-        const uint32_t idesc_k = tc::idesc_f16(128, 2 * R) | (1u << 15);  // A MN-major (tokens contiguous per channel)
-        const uint32_t idesc_v = tc::idesc_f16(128, 2 * R);
+        // MMA N = 2 R columns ([hi | lo]), at least 16: at R = 4 columns 8-15 read B rows nobody writes, and nobody
+        // reads those columns back
+        constexpr int NB = 2 * R < 16 ? 16 : 2 * R;
+        const uint32_t idesc_k = tc::idesc_f16(128, NB) | (1u << 15);  // A MN-major (tokens contiguous per channel)
+        const uint32_t idesc_v = tc::idesc_f16(128, NB);
         const uint32_t rb = l.bytes;
         Cursor pc = cur, lc = cur;                              // L2 prefetch and load cursors
         uint32_t np = 0, nl = 0;                                // records prefetched / loaded
@@ -667,9 +692,10 @@ int launch_rows(const TwParams & p, const TwParams * dyn, sjk_stream st) {
     return bv == 3 ? launch_kernel<2, 3, R>(p, dyn, st) : launch_kernel<2, 2, R>(p, dyn, st);
 }
 
-// the 8-row kernel for up to 8 query rows per KV head (decode width 1 or 2 at GQA 4), else the 16-row one
+// the 4-row kernel for up to 4 query rows per KV head (decode width 1 at GQA 4), the 8-row one for up to 8, else
+// the 16-row one
 int launch(const TwParams & p, sjk_stream st, const TwParams * dyn = nullptr) {
-    return p.rows <= 8 ? launch_rows<8>(p, dyn, st) : launch_rows<16>(p, dyn, st);
+    return p.rows <= 4 ? launch_rows<4>(p, dyn, st) : p.rows <= 8 ? launch_rows<8>(p, dyn, st) : launch_rows<16>(p, dyn, st);
 }
 
 SJK_HD void fill_rows(TwParams & p, int n_q, int n_head, int n_kv) {
