@@ -209,6 +209,13 @@ SJK_DEV void body_tc_body(const TcParams & p) {
             rowp[tid] = r;
         }
     };
+    // The grid may be launched as a programmatic dependent of the previous kernel in the stream (the merge of the
+    // previous call, say), so that its set-up above overlaps that kernel's tail. Nothing above reads data another
+    // kernel writes; the queries, the block table, the cache and the partials come after this wait, which returns
+    // once the previous kernel has completed and its writes are visible (at once when there is none).
+    if (tid == 2 * NW * 32 && !p.blocks)                   // the first records into L2 meanwhile (a prefetch only)
+        for (uint32_t g = 0; g < 2 && g < n; ++g) tc::prefetch_l2(p.body + ((size_t) (r_begin + g) * p.H + h) * l.bytes, l.bytes);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float qx[8];                                        // staged rows: this thread's q values (channel tid % 256)
     float * qrot = reinterpret_cast<float *>(sm + OFF_QROT);
     if ((uint32_t) split < p.n_dense) {
@@ -1053,15 +1060,27 @@ int sjk_tc_body_launch(const sjk_view * v, uint32_t B, uint32_t N, uint32_t n_re
     *splits_out = splits;
     if (splits == 0) return 0;
     const dim3 grid((unsigned) splits, (unsigned) n_kv);
+    // programmatic dependent launch: the CTAs may start while the previous kernel of the stream finishes and wait
+    // for it on the device before they read anything (body_tc_body)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = q_model ? SMEM_TOTAL_QROT : SMEM_TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (q_model) {
         cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL_QROT);
         if (e != cudaSuccess) return sjk_check(e);
-        attend_body_tc_kernel<true><<<grid, NT, SMEM_TOTAL_QROT, st>>>(p);
+        if (sjk_check(cudaLaunchKernelEx(&cfg, attend_body_tc_kernel<true>, p))) return SJK_ERR_DEVICE;
         return sjk_check_launch();
     }
     cudaError_t e = cudaFuncSetAttribute(attend_body_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
-    attend_body_tc_kernel<false><<<grid, NT, SMEM_TOTAL, st>>>(p);
+    if (sjk_check(cudaLaunchKernelEx(&cfg, attend_body_tc_kernel<false>, p))) return SJK_ERR_DEVICE;
     return sjk_check_launch();
 }
 
