@@ -270,9 +270,6 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 // R: query rows per KV head the kernel computes (4, 8 or 16, padded; the MMA N is 2 R, at least 16)
 template <int BK, int BV, int R>
 SJK_DEV void trellis_ws_body(const TwParams & p) {
-    // a kernel launched as this one's programmatic dependent (the same call's dense kernel, or its merge) may start
-    // now on the SMs this grid leaves free
-    asm volatile("griddepcontrol.launch_dependents;");
     constexpr int RH = R / 2;                                   // B_K rows per thread (two row halves)
     constexpr int LPH = 32 / RH;                                // lanes per row after a warp_rows<RH>
     constexpr int NSW = SW_N<R>, WI = W_I<R>, NTH = NT<R>;
@@ -309,9 +306,23 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
             reinterpret_cast<uint4 *>(sm + OFF_TBL)[i] = make_uint4(w, w, w, w);
         }
     }
+    // the first two records of a sequence without a block table into L2 (a prefetch only: no load into the SM)
+    if (tid == WI * 32 && i0 < i1) {
+        const TwItem & it = p.item[i0];
+        const TwSeq & sq = p.seq[it.seq_hl & 0xFFFFu];
+        if (!sq.blocks)
+            for (uint32_t g = it.r0; g < it.r1 && g < it.r0 + 2; ++g)
+                tc::prefetch_l2(sq.body + ((size_t) g * p.n_head_kv + (it.h_slot & 0xFFFFu)) * p.lay.bytes, p.lay.bytes);
+    }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
+    // The grid may be launched as a programmatic dependent of the previous kernel in the stream (the previous call's
+    // merge, say): the set-up above reads nothing another kernel writes, and this wait returns once that kernel has
+    // completed. Only then may this grid's own dependents (the same call's staged-row kernel beside it, or its
+    // merge) start, on the SMs it leaves free.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t tmem = *tmem_slot;
     const uint8_t * tbl = sm + OFF_TBL;
     const uint32_t lane4 = (uint32_t) lane * 4u;
@@ -680,7 +691,18 @@ int launch_kernel(const TwParams & p, const TwParams * dyn, sjk_stream st) {
     auto kfn = attend_trellis_ws_kernel<BK, BV, R>;
     const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_TOTAL);
     if (e != cudaSuccess) return sjk_check(e);
-    kfn<<<(unsigned) p.n_cta, NT<R>, SMEM_TOTAL, st>>>(p);
+    // programmatic dependent launch: the set-up overlaps the previous kernel of the stream (trellis_ws_body waits)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) p.n_cta);
+    cfg.blockDim = dim3(NT<R>);
+    cfg.dynamicSmemBytes = SMEM_TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (sjk_check(cudaLaunchKernelEx(&cfg, kfn, p))) return SJK_ERR_DEVICE;
     return sjk_check_launch();
 }
 
