@@ -283,7 +283,10 @@ __global__ void __launch_bounds__(256) attend_merge_rot_kernel(const float * par
     __shared__ float s_red[16];
     __shared__ __align__(16) float rowbuf[D];
     const int row = blockIdx.x, d0 = blockIdx.y * 64, tid = threadIdx.x;
+    // launched as a programmatic dependent of the kernels that write the partials: wait until they completed; the
+    // next call's body kernel, launched as this one's dependent, may be set up meanwhile
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     float m, t;
     sjkm::merge_tile(part, splits, n_rows, D, row, d0, wts, s_red, m, t);
     cg::cluster_group cl = cg::this_cluster();

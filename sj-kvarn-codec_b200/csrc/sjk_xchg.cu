@@ -19,8 +19,10 @@ __global__ void __launch_bounds__(256) xchg_exchange_kernel(const float * __rest
     __shared__ float s_red[16];
     __shared__ __align__(16) float stage[SJK_XCHG_MAX_WORLD * sjkm::XCHG_TILE_WORDS];
     const int row = blockIdx.x, tile = blockIdx.y, d0 = 64 * tile, tid = threadIdx.x;
-    // launched as a programmatic dependent of the kernel that writes part (sjk_attend_partial_xchg's merge): wait for it
+    // launched as a programmatic dependent of the kernel that writes part (sjk_attend_partial_xchg's merge): wait for
+    // it; the next call's body kernel, launched as this one's dependent, may be set up meanwhile
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const float * pr = part + (size_t) row * (D + 2);
     const float my_o = (tid < 64 && d0 + tid < D) ? pr[2 + d0 + tid] : 0.0f;
     if (!sjkm::xchg_publish_gather(x, n_rows, D, row, tile, pr[0], pr[1], my_o, stage)) {
