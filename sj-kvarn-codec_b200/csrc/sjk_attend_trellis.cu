@@ -515,10 +515,8 @@ SJK_DEV void trellis_ws_body(const TwParams & p) {
                 // the record stage and C[s] are rewritten only after this arrival (record g + 2)
                 warp_arrive(&bars[B_REMPTY + s], lane);
                 uint32_t a[RS], al[RS];
-                if constexpr (RS == 16) {
-                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + r0, a);
-                    tc::ld_x16_u(tmem + lane_base + COL_S + 32 * s + R + r0, al);
-                } else if constexpr (RS == 8) {
+                static_assert(RS == 8 || RS == 4, "rows per softmax warp");
+                if constexpr (RS == 8) {
                     tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + r0, a);
                     tc::ld_x8_u(tmem + lane_base + COL_S + 32 * s + R + r0, al);
                 } else {
